@@ -1,0 +1,364 @@
+#!/usr/bin/env python
+"""Throughput of the SoVITS v2 Generator (vocoder) on B200, one JSON line.
+
+Workload (one "step"): one decoder forward over a batch of 16 utterances of
+10 s each -- z [16, 192, 500] ~ N(0,1), speaker g [16, 512, 1] ~ N(0,1),
+random-init weights N(0, 0.01) with zero bias (seeded; no checkpoints
+offline) -- giving 16 x 320 000 samples at 32 kHz.  Every rank decodes its own
+batch (utterances are independent units: weak scaling, no collective on the
+data path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode bf16|fp32]
+    python bench.py --impl reference ...   # the CPU reference arm
+
+value     audio-seconds per second, whole job, inputs resident in HBM.
+e2e       the same metric through the public C-ABI call with host buffers
+          (H2D of z/g and D2H of the waveform inside every timed step).
+roofline  the tap-GEMM conv kernel: achieved = algorithmic FLOPs / average
+          launch time (CUDA events around every launch on the forward's
+          stream, over the timed region); layer_roofline adds the survey's
+          layer-weighted fraction sum(t_roof) / sum(t_measured).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decoder audio-sec/sec at B=16×10 s bf16, 1/2/4/8 B200; % layer roofline"
+UNIT = "audio-s/s"
+SAMPLE_RATE = 32000
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# FP32 CUDA-core peak, nominal: 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz.
+FP32_CORE_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def audio_seconds(B: int, T0: int, hop: int) -> float:
+    return B * T0 * hop / SAMPLE_RATE
+
+
+def cpu_port_sample(sd, z, g, min_seconds=10.0, max_reps=4):
+    """The oracle port (float accumulation, all host threads) on one utterance."""
+    import oracle
+    oracle.build()
+    threads = os.cpu_count() or 1
+    oracle.decoder_forward(sd, z[:, :, :8], g, acc64=False, nthreads=threads)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.decoder_forward(sd, z, g, acc64=False, nthreads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            break
+    return reps, el, threads
+
+
+def run_reference(args, ws, rank):
+    """CPU reference arm: the C restatement of the reference decoder (the
+    Candle crate cannot be built here: no Rust toolchain), all host threads,
+    each step one 10 s utterance of the same workload."""
+    if rank != 0:
+        return
+    import oracle
+    gsv = load_pkg()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    z, g = gsv.synth.make_inputs(args.batch, args.frames)
+    z1, g1 = z[:1], g[:1]
+    oracle.build()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.decoder_forward(sd, z1, g1, acc64=False, nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.decoder_forward(sd, z1, g1, acc64=False, nthreads=threads)
+    el = time.perf_counter() - t0
+    secs = audio_seconds(1, args.frames, 640) * args.steps
+    value = secs / el
+    sample = f"1 utterance x {args.frames / 50:g} s (z [1,192,{args.frames}]) per step"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) z/g, N(0,0.01) random-init weights, zero bias",
+        "config": {"workload": f"B={args.batch} x {args.frames / 50:g} s Generator decode, "
+                               "sampled one utterance per step on the host CPU",
+                   "batch": args.batch, "frames": args.frames},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def load_pkg():
+    from __graft_entry__ import load_package
+    return load_package()
+
+
+def layer_roofline(stats, mode, pk):
+    """sum(t_roof) / sum(t_meas) over every launch; t_roof per launch is the
+    sum over its reference convs of max(F / P, bytes / BW) -- grouped launches
+    carry the summed work of same-shape convs, so the max is taken per launch
+    of uniform-shape convs."""
+    p_tensor = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) * 1e12
+    p_comp = p_tensor if mode == "bf16" else FP32_CORE_TFLOPS * 1e12
+    bw = pk["hbm_gbs"] * 1e9
+    rows, roof, meas = [], 0.0, 0.0
+    for s in stats:
+        t_meas = s["ms"] / 1e3
+        comp = s["flops"] / p_comp if s["kind"] in (0, 2) else 0.0
+        t_roof = max(comp, s["bytes"] / bw)
+        roof += t_roof
+        meas += t_meas
+        rows.append({"name": s["name"], "ms": round(s["ms"], 4),
+                     "roof_ms": round(1e3 * t_roof, 4),
+                     "frac": round(t_roof / t_meas, 3) if t_meas > 0 else None,
+                     "bound": "hbm" if s["bytes"] / bw >= comp else "compute"})
+    return roof, meas, rows
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--mode", choices=("bf16", "fp32"), default="bf16")
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--frames", type=int, default=500)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    ws, rank, local = dist_setup()
+
+    if args.impl == "reference":
+        run_reference(args, ws, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    gsv = load_pkg()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    B, T0 = args.batch, args.frames
+    z, g = gsv.synth.make_inputs(B, T0, seed_z=1 + 1000 * rank, seed_g=2 + 1000 * rank)
+    dec = gsv.Decoder.load(sd, device=local, mode=args.mode)
+    hop = dec.hop
+    secs_per_step = audio_seconds(B, T0, hop)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if ws == 1:
+            return x
+        t = torch.tensor([x], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput (value) --------------------------------
+    zt = torch.from_numpy(z).cuda()
+    gt = torch.from_numpy(g).cuda()
+    out = torch.empty(B * T0 * hop, device="cuda", dtype=torch.float32)
+    for _ in range(args.warmup):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    launches_per_step = dec.launch_count()
+    dec.set_stage_timing(2)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.forward_device(zt, gt, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    stats = dec.launch_stats()
+    dec.set_stage_timing(0)
+    value = ws * secs_per_step * args.steps / (ms / 1e3)
+    assert torch.isfinite(out).all().item()
+
+    # ---- end to end through the public call with host buffers (e2e) --------
+    zh = torch.from_numpy(z).pin_memory()
+    gh = torch.from_numpy(g).pin_memory()
+    wh = torch.empty(B * T0 * hop, dtype=torch.float32).pin_memory()
+    zn, gn, wn = zh.numpy(), gh.numpy(), wh.numpy()
+    for _ in range(args.warmup):
+        dec.forward(zn, gn, out=wn, stream=stream.cuda_stream)
+    barrier()
+    torch.cuda.synchronize()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(stream)
+    for _ in range(args.steps):
+        dec.forward(zn, gn, out=wn, stream=stream.cuda_stream)
+    h1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(h0.elapsed_time(h1))
+    e2e = {"value": ws * secs_per_step * args.steps / (ms_e2e / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": int(zn.nbytes + gn.nbytes), "d2h_bytes_per_step": int(wn.nbytes),
+           "ms_per_step": ms_e2e / args.steps}
+
+    # ---- roofline of the dominant kernel + layer-weighted fraction ----------
+    pk, pk_kind = peaks()
+    conv = [s for s in stats if s["kind"] == 0]
+    f_conv = sum(s["flops"] for s in conv)
+    t_conv = sum(s["ms"] for s in conv) / 1e3
+    if args.mode == "bf16":
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        bound = "tensor"
+    else:
+        peak = FP32_CORE_TFLOPS
+        bound = "fp32-core"
+    achieved = f_conv / t_conv / 1e12 if t_conv > 0 else None
+    traffic = None
+    prof = ROOT / "profiles" / f"tapconv_{args.mode}_traffic.json"
+    if prof.exists():
+        try:
+            traffic = json.loads(prof.read_text()).get("dram_bytes_per_step")
+        except (ValueError, OSError):
+            traffic = None
+    roof_s, meas_s, rows = layer_roofline(stats, args.mode, pk)
+    roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak if achieved else None, "traffic": traffic,
+                "kernel": "tapconv (all 97 tap-GEMM convs of one forward)",
+                "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
+                                                 else "nominal fp32 CUDA-core")}
+    layer = {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
+             "sum_meas_ms": 1e3 * meas_s, "hbm_gbs": pk["hbm_gbs"],
+             "compute_tflops": peak, "peaks": pk_kind}
+    if args.layers and rank == 0:
+        for r in rows:
+            log(f"{r['name']:<22s} {r['ms']:9.4f} ms  roof {r['roof_ms']:9.4f} ms  "
+                f"frac {r['frac']}  {r['bound']}")
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----------------------------------
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        reps, el, threads = cpu_port_sample(sd, z[:1], g[:1])
+        cpu = {"value": reps * audio_seconds(1, T0, hop) / el, "unit": UNIT, "cores": threads,
+               "kind": "port",
+               "sample": f"{reps} x 1 utterance of {T0 / 50:g} s (z [1,192,{T0}]) of the same "
+                         "workload, C restatement of the reference decoder, float accumulation"}
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.mode == "bf16" else "f32",
+            "data": "synthetic: seeded N(0,1) z/g, N(0,0.01) random-init weights, zero bias",
+            "config": {"workload": f"B={B} x {T0 / 50:g} s Generator decode per GPU "
+                                   f"(z [{B},192,{T0}] -> [{B},1,{T0 * hop}])",
+                       "batch": B, "frames": T0, "mode": args.mode,
+                       "l2": "no flush: one step moves several GB of activations through "
+                             "buffers of 164 MB each (> 126 MB L2)",
+                       "parallelism": f"utterance-sharded x{ws} (independent per-GPU batches)"},
+            "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
+            "layer_roofline": layer, "cpu_baseline": cpu, "clocks": clk,
+        }), flush=True)
+    dec.close()
+    if ws > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,299 @@
+"""gsvdec -- B200 (sm_100a) SoVITS v2 Generator of gpt-sovits-rs, Python side.
+
+This module is the host-side mirror of the reference's decoder interface,
+``impl Decoder { fn load(&StateDict, &Device, DType); fn forward(&self, x,
+Option<&Tensor>) -> Result<Vec<f32>> }`` (src/models/sovits_decoder.rs:231,
+386 of the reference crate), over the C ABI of ``libgsvdec.so``
+(include/gsvdec.h).  The CUDA library is the only compute path: if it is
+missing, importing ``Decoder`` raises instead of falling back to anything.
+
+Reference errors (``crate::Error`` values, src/lib.rs:76-97) surface as
+:class:`GsvDecError` carrying the library's status code and message.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+from typing import Mapping, Optional, Sequence
+
+import numpy as np
+
+from . import synth  # noqa: F401  (seeded weights / inputs)
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "_build" / "libgsvdec.so"
+
+GSV_OK = 0
+STATUS = {
+    -1: "GSV_E_INVALID_ARG", -2: "GSV_E_MISSING_KEY", -3: "GSV_E_SHAPE", -4: "GSV_E_DTYPE",
+    -5: "GSV_E_CUDA", -6: "GSV_E_OOM", -7: "GSV_E_UNSUPPORTED", -8: "GSV_E_TIMEOUT",
+}
+MODES = {"fp32": 0, "bf16": 1}
+MEM_HOST, MEM_DEVICE = 0, 1
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+
+# Every symbol include/gsvdec.h declares (checked by the CPU test suite).
+EXPORTS = (
+    "gsvdec_create", "gsvdec_create_from_file", "gsvdec_destroy", "gsvdec_get_info",
+    "gsvdec_forward", "gsvdec_forward_chunk", "gsvdec_forward_taps", "gsvdec_set_stage_timing",
+    "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
+    "gsvdec_last_error",
+)
+
+
+class GsvDecError(RuntimeError):
+    """A non-zero status from libgsvdec."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"{STATUS.get(code, code)}: {message}")
+        self.code = code
+        self.status = STATUS.get(code, str(code))
+
+
+class _Tensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int), ("ndim", ctypes.c_int),
+                ("shape", ctypes.c_int64 * 4), ("data", ctypes.c_void_p)]
+
+
+class _Info(ctypes.Structure):
+    _fields_ = [("mode", ctypes.c_int), ("device", ctypes.c_int), ("in_channels", ctypes.c_int),
+                ("gin_channels", ctypes.c_int), ("n_upsamples", ctypes.c_int),
+                ("n_resblocks", ctypes.c_int), ("hop", ctypes.c_int),
+                ("receptive_halo", ctypes.c_int), ("weight_bytes", ctypes.c_int64)]
+
+
+class _LaunchStat(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 48), ("kind", ctypes.c_int), ("n_convs", ctypes.c_int),
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double), ("ms", ctypes.c_float)]
+
+
+_lib = None
+
+
+def library(path: Optional[Path] = None) -> ctypes.CDLL:
+    """Load libgsvdec.so (built in-tree by build.py).  Raises if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise ImportError(f"libgsvdec.so not built at {p}; run gpt-sovits-rs_b200/build.py "
+                          "(there is no CPU fallback)")
+    lib = ctypes.CDLL(str(p))
+    vp, i, fp = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)
+    lib.gsvdec_last_error.restype = ctypes.c_char_p
+    lib.gsvdec_create.argtypes = [ctypes.POINTER(_Tensor), i, i, i, ctypes.POINTER(vp)]
+    lib.gsvdec_create_from_file.argtypes = [ctypes.c_char_p, i, i, ctypes.POINTER(vp)]
+    lib.gsvdec_destroy.argtypes = [vp]
+    lib.gsvdec_get_info.argtypes = [vp, ctypes.POINTER(_Info)]
+    lib.gsvdec_forward.argtypes = [vp, vp, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_forward_chunk.argtypes = [vp, vp, vp, i, i, i, i, vp, i, vp]
+    lib.gsvdec_forward_taps.argtypes = [vp, vp, vp, i, i, vp, ctypes.POINTER(fp), i]
+    lib.gsvdec_set_stage_timing.argtypes = [vp, i]
+    lib.gsvdec_get_stage_times.argtypes = [vp, fp]
+    lib.gsvdec_launch_count.argtypes = [vp, i, i, ctypes.POINTER(i)]
+    lib.gsvdec_get_launch_stats.argtypes = [vp, ctypes.POINTER(_LaunchStat), i, ctypes.POINTER(i)]
+    _lib = lib
+    return lib
+
+
+def _check(rc: int) -> None:
+    if rc != GSV_OK:
+        raise GsvDecError(rc, library().gsvdec_last_error().decode())
+
+
+def _as_weight(v):
+    """(array kept alive, dtype code) for a state-dict value (numpy or torch)."""
+    try:
+        import torch
+        if isinstance(v, torch.Tensor):
+            t = v.detach().cpu().contiguous()
+            if t.dtype == torch.bfloat16:
+                return t.view(torch.int16).numpy(), DT_BF16
+            if t.dtype == torch.float16:
+                return t.numpy(), DT_F16
+            return t.float().numpy(), DT_F32
+    except ImportError:  # pragma: no cover
+        pass
+    a = np.ascontiguousarray(np.asarray(v))
+    if a.dtype == np.float16:
+        return a, DT_F16
+    return np.ascontiguousarray(a, dtype=np.float32), DT_F32
+
+
+def _host_f32(a):
+    if a is None:
+        return None
+    try:
+        import torch
+        if isinstance(a, torch.Tensor):
+            a = a.detach().cpu().float().numpy()
+    except ImportError:  # pragma: no cover
+        pass
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+class Decoder:
+    """The Generator on one B200: ``Decoder.load(...)`` then ``forward(z, g)``."""
+
+    def __init__(self, handle: ctypes.c_void_p):
+        self._h = handle
+        info = _Info()
+        _check(library().gsvdec_get_info(self._h, ctypes.byref(info)))
+        self.info = {f: getattr(info, f) for f, _ in _Info._fields_}
+        self.mode = "fp32" if info.mode == 0 else "bf16"
+        self.hop = info.hop
+
+    # -- Decoder::load ------------------------------------------------------
+    @classmethod
+    def load(cls, state_dict: Mapping[str, object], device: int = 0, mode: str = "bf16") -> "Decoder":
+        """Decoder::load (src/models/sovits_decoder.rs:231-293) from ``dec.*`` tensors."""
+        if mode not in MODES:
+            raise ValueError(f"mode must be one of {sorted(MODES)}")
+        keep = []
+        items = list(state_dict.items())
+        arr = (_Tensor * max(1, len(items)))()
+        for idx, (k, v) in enumerate(items):
+            a, dt = _as_weight(v)
+            if a.ndim < 1 or a.ndim > 4:
+                raise ValueError(f"{k}: unsupported rank {a.ndim}")
+            name = k.encode()
+            keep += [a, name]
+            arr[idx].name = name
+            arr[idx].dtype = dt
+            arr[idx].ndim = a.ndim
+            for d in range(a.ndim):
+                arr[idx].shape[d] = a.shape[d]
+            arr[idx].data = a.ctypes.data
+        h = ctypes.c_void_p()
+        _check(library().gsvdec_create(arr, len(items), MODES[mode], device, ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def load_file(cls, path: str, device: int = 0, mode: str = "bf16") -> "Decoder":
+        """Decoder::load straight from a safetensors checkpoint (dec.* keys)."""
+        h = ctypes.c_void_p()
+        _check(library().gsvdec_create_from_file(str(path).encode(), MODES[mode], device,
+                                                 ctypes.byref(h)))
+        return cls(h)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            library().gsvdec_destroy(self._h)
+            self._h = None
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def out_len(self, T0: int) -> int:
+        return T0 * self.hop
+
+    # -- Decoder::forward ---------------------------------------------------
+    def forward(self, x, g=None, lengths: Optional[Sequence[int]] = None, out=None,
+                stream: Optional[int] = None) -> np.ndarray:
+        """Decoder::forward (src/models/sovits_decoder.rs:386-458) on host arrays.
+
+        x [B, C_in, T0], g [B, gin, 1] or None; returns the flattened fp32
+        waveform (utterances concatenated), like the reference's Vec<f32>.
+        ``out`` may be a preallocated (e.g. pinned) float32 array of B*hop*T0;
+        ``stream`` a cudaStream_t handle as an int (default: legacy stream).
+        """
+        z = _host_f32(x)
+        if z.ndim != 3:
+            raise ValueError("x must be [B, C, T]")
+        B, _, T0 = z.shape
+        gg = _host_f32(g)
+        ln = None if lengths is None else np.ascontiguousarray(np.asarray(lengths, np.int32))
+        if ln is not None and ln.shape != (B,):
+            raise ValueError("lengths must hold one value per utterance")
+        if out is None:
+            out = np.empty(B * self.out_len(T0), np.float32)
+        elif out.dtype != np.float32 or out.size != B * self.out_len(T0) or not out.flags.c_contiguous:
+            raise ValueError("out must be a contiguous float32 array of B*hop*T0 samples")
+        _check(library().gsvdec_forward(self._h, _ptr(z), _ptr(gg), _ptr(ln), B, T0, _ptr(out),
+                                        MEM_HOST, None if stream is None else ctypes.c_void_p(stream)))
+        return out
+
+    def forward_device(self, z, g=None, lengths=None, out=None, stream=None):
+        """Stream-async forward on CUDA tensors (torch) already on the device."""
+        import torch
+        B, _, T0 = z.shape
+        assert z.is_cuda and z.dtype == torch.float32 and z.is_contiguous()
+        if out is None:
+            out = torch.empty(B * self.out_len(T0), device=z.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream(z.device).cuda_stream
+        _check(library().gsvdec_forward(
+            self._h, ctypes.c_void_p(z.data_ptr()),
+            None if g is None else ctypes.c_void_p(g.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
+            B, T0, ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    def forward_chunk(self, x, g, frame_begin: int, frame_end: int, halo: int = 16) -> np.ndarray:
+        """Frames [frame_begin, frame_end) of one utterance with a recomputed halo."""
+        z = _host_f32(x)
+        if z.ndim != 3 or z.shape[0] != 1:
+            raise ValueError("x must be [1, C, T]")
+        gg = _host_f32(g)
+        wav = np.empty((frame_end - frame_begin) * self.hop, np.float32)
+        _check(library().gsvdec_forward_chunk(self._h, _ptr(z), _ptr(gg), z.shape[2], frame_begin,
+                                              frame_end, halo, _ptr(wav), MEM_HOST, None))
+        return wav
+
+    def forward_debug(self, x, g=None):
+        """Decoder::forward_debug (src/models/sovits_decoder.rs:473-526): the
+        waveform plus the per-layer taps [conv_pre(+cond), ups0, rb0, ...,
+        conv_post before tanh] in the reference's [B, C, T] layout."""
+        z = _host_f32(x)
+        B, _, T0 = z.shape
+        gg = _host_f32(g)
+        shapes = self.tap_shapes(B, T0)
+        taps = [np.empty(s, np.float32) for s in shapes]
+        fp = ctypes.POINTER(ctypes.c_float)
+        ptrs = (fp * len(taps))(*[t.ctypes.data_as(fp) for t in taps])
+        wav = np.empty(B * self.out_len(T0), np.float32)
+        _check(library().gsvdec_forward_taps(self._h, _ptr(z), _ptr(gg), B, T0, _ptr(wav), ptrs,
+                                             len(taps)))
+        return wav, taps
+
+    def tap_shapes(self, B: int, T0: int):
+        chans = [512, 256, 128, 64, 32, 16]
+        rates = [10, 8, 2, 2, 2]
+        shapes = [(B, chans[0], T0)]
+        L = T0
+        for i in range(self.info["n_upsamples"]):
+            L *= rates[i] if i < 5 else 2
+            shapes += [(B, chans[i + 1] if i + 1 < len(chans) else -1, L)] * 2
+        shapes.append((B, 1, L))
+        return shapes
+
+    # -- profiling ----------------------------------------------------------
+    def set_stage_timing(self, level) -> None:
+        """0 off, 1 stage events, 2 stage + per-launch events."""
+        _check(library().gsvdec_set_stage_timing(self._h, int(level)))
+
+    def launch_stats(self) -> list:
+        """Per-launch profile of the last forward (needs set_stage_timing(2))."""
+        n = ctypes.c_int()
+        _check(library().gsvdec_get_launch_stats(self._h, None, 0, ctypes.byref(n)))
+        arr = (_LaunchStat * max(1, n.value))()
+        _check(library().gsvdec_get_launch_stats(self._h, arr, n.value, ctypes.byref(n)))
+        return [{"name": a.name.decode(), "kind": a.kind, "n_convs": a.n_convs, "flops": a.flops,
+                 "bytes": a.bytes, "ms": a.ms} for a in arr[:n.value]]
+
+    def stage_times(self) -> dict:
+        ms = (ctypes.c_float * 5)()
+        _check(library().gsvdec_get_stage_times(self._h, ms))
+        return dict(zip(("pre", "upsample", "resblocks", "post", "total"), list(ms)))
+
+    def launch_count(self) -> int:
+        n = ctypes.c_int()
+        _check(library().gsvdec_launch_count(self._h, 0, 0, ctypes.byref(n)))
+        return n.value

@@ -1,0 +1,71 @@
+// gsv_internal.h -- descriptors shared by the host planner and the kernels.
+//
+// Every convolution of the Generator is expressed as one "tap GEMM":
+//
+//   acc[b, q, n] = sum_seg sum_j sum_c  X_seg[b, q + off_seg(j), c] * W_seg[j, n, c]
+//
+// over activations stored time-major ([B][L][C], channels innermost, so a
+// tap shift is a whole-row shift).  Rows outside [0, Lin) read as zero, which
+// is the zero padding of Conv1d (src/utils/weights.rs:78-113).
+//
+// * Conv1d(k, dil, pad):  off(j) = j*dil - pad, N = Cout, output row = q.
+// * ConvTranspose1d(k, s, pad) (src/models/sovits_decoder.rs:551-576) is
+//   written polyphase: output t = q*s + phi - pad takes the taps
+//   kk = phi + m*s, reading x[q - m].  With columns n = phi*Cout + cout the
+//   GEMM output [Q][s*Cout] is the [Lout][Cout] output shifted by pad rows,
+//   so no zero-stuffed input is ever formed: off(m) = -m, N = s*Cout,
+//   crop = pad*Cout elements.
+//
+// The epilogue maps element (q, n) to the flat output index
+// e = q*N + n - crop (dropped unless 0 <= e < Lout*Cout), t = e / Cout,
+// c = e % Cout, and computes
+//   v = (acc + bias[c] + bias_bc[b, c] + sum_r res_r[b, t, c]) / div
+// zeroing rows t >= len[b]; it stores v (out_raw) and/or leaky_relu(v, slope)
+// (out_act).  That folds the bias add, the broadcast cond add
+// (src/models/sovits_decoder.rs:393-399), the ResBlock residual add (:204),
+// the three-branch average (:418-442) and the LeakyReLU that starts the next
+// layer (:200, :202, :408, :449) into the producing kernel.
+#pragma once
+#include <cstdint>
+
+namespace gsv {
+
+constexpr int kMaxSeg = 3;
+constexpr int kMaxRes = 3;
+constexpr int kMaxGroup = 3;
+
+struct TapSeg {
+  const void* x;  // [B][Lin][Cin], mode dtype
+  const void* w;  // packed weights of this segment (layout depends on the kernel family)
+  int Lin;        // input rows per utterance
+  int Cin;
+  int ntaps;
+  int off0;       // row offset of tap 0
+  int offstep;    // row offset step between taps
+};
+
+struct TapConv {
+  TapSeg seg[kMaxSeg];
+  int nseg;
+  int B, Q, N, Cout, Lout, crop;
+  const float* bias;     // [Cout] (sum over segments), never null
+  const float* bias_bc;  // [B][Cout] per-utterance bias (cond), or null
+  const void* res[kMaxRes];
+  int nres;
+  float div;             // divisor applied after the sums (1 = none)
+  void* out_raw;         // [B][Lout][Cout] or null
+  void* out_act;         // [B][Lout][Cout] or null
+  float slope;           // LeakyReLU slope of out_act
+  const int* len;        // [B] valid output rows, or null
+  int row_tiles;         // tiles per utterance along q (set by the launcher)
+};
+
+struct TapConvGroup {
+  TapConv op[kMaxGroup];
+  int n;
+};
+
+// Ceil-div helper usable on host and device.
+__host__ __device__ inline int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace gsv

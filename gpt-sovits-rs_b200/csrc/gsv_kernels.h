@@ -1,0 +1,37 @@
+// gsv_kernels.h -- launchers of the device kernels (host-callable).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "gsv_internal.h"
+
+namespace gsv {
+
+// Element type of activations / packed weights in one arithmetic mode.
+enum class Dt { F32 = 0, BF16 = 1 };
+
+// fp32 CUDA-core tap GEMM (weights packed [tap][Cin][N] fp32).
+cudaError_t launch_tapconv_f32(const TapConvGroup& g, cudaStream_t st);
+// bf16 tcgen05 tap GEMM (weights packed [tap][N][Cin] bf16).
+cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st);
+// True when the tcgen05 kernel supports this op's geometry.
+bool tapconv_tc_supported(const TapConv& op);
+
+// z [B][Cin][Tsrc] fp32 (NCL, the reference layout) -> zt [B][T][Cin] (time-major)
+// reading frames [t_off, t_off + T); frames t >= len[b] are written as 0.
+cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_off, int T,
+                                const int* len, void* zt, Dt dt, cudaStream_t st);
+// bias_bc[b][c] = sum_i wc[c][i] g[b][i] + bc[c]   (the cond 1x1 conv)
+cudaError_t launch_cond(const float* g, const float* wc, const float* bc, int B, int gin, int C,
+                        float* bias_bc, cudaStream_t st);
+// Per-stage valid lengths: lens[s*B + b] for s in [0, nstage], stage 0 = frames.
+cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, const int* add,
+                           int nstage, int* lens, cudaStream_t st);
+// conv_post (Cout 1, K taps, pad) + optional bias + tanh over x [B][L][C]:
+// wav[b][t] = tanh(sum_{j,c} w[j][c] x[b][t + j - pad][c] + bias); rows t >= len[b]
+// give 0.  With pre_tanh != null the pre-tanh value is stored there too.
+cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, int K, int pad,
+                        float bias, const int* len, float* wav, float* pre_tanh, cudaStream_t st);
+// Time-major [B][L][C] (mode dtype) -> [B][C][L] fp32, the reference's layout (taps).
+cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st);
+
+}  // namespace gsv

@@ -1,0 +1,1061 @@
+// gsvdec_api.cu -- the C ABI (include/gsvdec.h): weight loading and packing
+// (Decoder::load), the per-call layer schedule (Decoder::forward) and the
+// workspace.  Host code only; kernels live in tapconv_*.cu / misc_kernels.cu.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/gsvdec.h"
+#include "gsv_kernels.h"
+#include "safetensors.h"
+
+namespace gsv {
+namespace {
+
+thread_local std::string g_last_error;
+
+int set_err(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                 \
+  do {                                                                                 \
+    cudaError_t e_ = (expr);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return set_err(e_ == cudaErrorMemoryAllocation ? GSV_E_OOM : GSV_E_CUDA,         \
+                     "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                     __LINE__);                                                        \
+  } while (0)
+
+#define GSV_TRY(expr)          \
+  do {                         \
+    int rc_ = (expr);          \
+    if (rc_ != GSV_OK) return rc_; \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// Host-side model, following Decoder::load (src/models/sovits_decoder.rs:231-293).
+
+struct HostConv {
+  std::vector<float> w;  // folded weight, the tensor's own layout [d0, d1, K]
+  std::vector<float> b;  // bias or empty
+  int d0 = 0, d1 = 0, K = 0;
+  int pad = 0, dil = 1, stride = 1;
+};
+
+struct HostModel {
+  HostConv pre, post, cond;
+  bool has_cond = false;
+  std::vector<HostConv> ups;  // weight [Cin, Cout, K]
+  struct RB {
+    std::vector<HostConv> c1, c2;
+  };
+  std::vector<RB> rbs;
+};
+
+float half_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+float bf16_to_float(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+struct TensorMap {
+  std::map<std::string, const gsvdec_tensor*> m;
+  const gsvdec_tensor* get(const std::string& k) const {
+    auto it = m.find(k);
+    return it == m.end() ? nullptr : it->second;
+  }
+};
+
+int64_t numel(const gsvdec_tensor* t) {
+  int64_t n = 1;
+  for (int i = 0; i < t->ndim; ++i) n *= t->shape[i];
+  return n;
+}
+
+int to_f32(const gsvdec_tensor* t, std::vector<float>& out) {
+  const int64_t n = numel(t);
+  out.resize((size_t)n);
+  if (!t->data && n) return set_err(GSV_E_INVALID_ARG, "tensor %s has no data", t->name);
+  switch (t->dtype) {
+    case GSV_DTYPE_F32:
+      memcpy(out.data(), t->data, sizeof(float) * (size_t)n);
+      return GSV_OK;
+    case GSV_DTYPE_F16: {
+      const uint16_t* p = static_cast<const uint16_t*>(t->data);
+      for (int64_t i = 0; i < n; ++i) out[i] = half_to_float(p[i]);
+      return GSV_OK;
+    }
+    case GSV_DTYPE_BF16: {
+      const uint16_t* p = static_cast<const uint16_t*>(t->data);
+      for (int64_t i = 0; i < n; ++i) out[i] = bf16_to_float(p[i]);
+      return GSV_OK;
+    }
+    default:
+      return set_err(GSV_E_DTYPE, "tensor %s: unsupported dtype %d", t->name, t->dtype);
+  }
+}
+
+// Plain conv: "<pfx>.weight" [O, I, K], optional "<pfx>.bias"; pad (K-1)/2
+// (src/models/sovits_decoder.rs:295-321, 356-383).
+int load_plain(const TensorMap& tm, const std::string& pfx, HostConv& c) {
+  const gsvdec_tensor* w = tm.get(pfx + ".weight");
+  if (!w) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight' not found in state dict", pfx.c_str());
+  if (w->ndim != 3) return set_err(GSV_E_SHAPE, "%s.weight must be 3-d", pfx.c_str());
+  GSV_TRY(to_f32(w, c.w));
+  c.d0 = (int)w->shape[0];
+  c.d1 = (int)w->shape[1];
+  c.K = (int)w->shape[2];
+  if (const gsvdec_tensor* b = tm.get(pfx + ".bias")) {
+    if (numel(b) != c.d0) return set_err(GSV_E_SHAPE, "%s.bias must have %d values", pfx.c_str(), c.d0);
+    GSV_TRY(to_f32(b, c.b));
+  }
+  c.pad = (c.K - 1) / 2;
+  return GSV_OK;
+}
+
+// Weight-norm conv: w = g * v / ||v||, norm over dims (1, 2) of each dim-0
+// slice, folded once at load (src/utils/weights.rs:589-614).
+int load_wn(const TensorMap& tm, const std::string& pfx, HostConv& c) {
+  const gsvdec_tensor* v = tm.get(pfx + ".weight_v");
+  const gsvdec_tensor* g = tm.get(pfx + ".weight_g");
+  if (!v) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight_v' not found in state dict", pfx.c_str());
+  if (!g) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight_g' not found in state dict", pfx.c_str());
+  if (v->ndim != 3) return set_err(GSV_E_SHAPE, "%s.weight_v must be 3-d", pfx.c_str());
+  c.d0 = (int)v->shape[0];
+  c.d1 = (int)v->shape[1];
+  c.K = (int)v->shape[2];
+  if (numel(g) != c.d0)
+    return set_err(GSV_E_SHAPE, "%s.weight_g must hold %d values (one per dim-0 slice)", pfx.c_str(), c.d0);
+  std::vector<float> vv, gg;
+  GSV_TRY(to_f32(v, vv));
+  GSV_TRY(to_f32(g, gg));
+  const size_t per = (size_t)c.d1 * c.K;
+  c.w.resize(vv.size());
+  for (int o = 0; o < c.d0; ++o) {
+    double ss = 0.0;
+    for (size_t j = 0; j < per; ++j) ss += (double)vv[o * per + j] * vv[o * per + j];
+    const float norm = (float)std::sqrt(ss);
+    for (size_t j = 0; j < per; ++j) c.w[o * per + j] = (vv[o * per + j] / norm) * gg[o];
+  }
+  if (const gsvdec_tensor* b = tm.get(pfx + ".bias")) GSV_TRY(to_f32(b, c.b));
+  c.pad = (c.K - 1) / 2;
+  return GSV_OK;
+}
+
+int load_model(const gsvdec_tensor* ts, int n, HostModel& m) {
+  TensorMap tm;
+  for (int i = 0; i < n; ++i) {
+    if (!ts[i].name) return set_err(GSV_E_INVALID_ARG, "tensor %d has no name", i);
+    if (ts[i].ndim < 1 || ts[i].ndim > 4)
+      return set_err(GSV_E_SHAPE, "tensor %s: ndim %d out of range", ts[i].name, ts[i].ndim);
+    tm.m[ts[i].name] = &ts[i];
+  }
+  GSV_TRY(load_plain(tm, "dec.conv_pre", m.pre));
+  GSV_TRY(load_plain(tm, "dec.conv_post", m.post));
+  if (tm.get("dec.cond.weight")) {
+    GSV_TRY(load_plain(tm, "dec.cond", m.cond));
+    m.has_cond = true;
+    if (m.cond.K != 1) return set_err(GSV_E_SHAPE, "dec.cond.weight must have kernel size 1");
+    if (m.cond.d0 != m.pre.d0)
+      return set_err(GSV_E_SHAPE, "dec.cond output width %d != conv_pre width %d", m.cond.d0, m.pre.d0);
+  }
+  // Strides are training config: [10, 8, 2, 2, 2], fallback 2 (:252-270).
+  static const int kRates[5] = {10, 8, 2, 2, 2};
+  int C = m.pre.d0;
+  for (int i = 0; i < 10; ++i) {
+    const std::string pfx = "dec.ups." + std::to_string(i);
+    if (!tm.get(pfx + ".weight_v")) continue;
+    HostConv u;
+    GSV_TRY(load_wn(tm, pfx, u));
+    const int idx = (int)m.ups.size();
+    u.stride = idx < 5 ? kRates[idx] : 2;
+    if (u.K < u.stride) return set_err(GSV_E_SHAPE, "%s: kernel %d shorter than stride %d", pfx.c_str(), u.K, u.stride);
+    u.pad = (u.K - u.stride) / 2;  // (:564)
+    if (u.d0 != C) return set_err(GSV_E_SHAPE, "%s: input width %d != %d", pfx.c_str(), u.d0, C);
+    C = u.d1;
+    m.ups.push_back(std::move(u));
+  }
+  // ResBlock1: k = [3,7,11][rb % 3], convs1 dilation [1,3,5][i] (pad d(k-1)/2),
+  // convs2 dilation 1 (pad (k-1)/2) (src/models/sovits_decoder.rs:146-194).
+  static const int kKs[3] = {3, 7, 11}, kDil[3] = {1, 3, 5};
+  for (int r = 0; r < 15; ++r) {
+    const std::string pfx = "dec.resblocks." + std::to_string(r);
+    if (!tm.get(pfx + ".convs1.0.weight_v")) continue;
+    HostModel::RB rb;
+    for (int s = 0; s < 2; ++s) {
+      for (int j = 0; j < 3; ++j) {
+        const std::string cp = pfx + ".convs" + std::to_string(s + 1) + "." + std::to_string(j);
+        if (!tm.get(cp + ".weight_v")) continue;
+        HostConv c;
+        GSV_TRY(load_wn(tm, cp, c));
+        const int k = kKs[r % 3];
+        if (c.K != k)
+          return set_err(GSV_E_SHAPE, "%s: kernel %d disagrees with [3,7,11][rb %% 3] = %d", cp.c_str(), c.K, k);
+        if (c.d0 != c.d1) return set_err(GSV_E_SHAPE, "%s: resblock conv must be square", cp.c_str());
+        if (s == 0) { c.dil = kDil[j]; c.pad = kDil[j] * (k - 1) / 2; }
+        else { c.dil = 1; c.pad = (k - 1) / 2; }
+        (s == 0 ? rb.c1 : rb.c2).push_back(std::move(c));
+      }
+    }
+    if (rb.c1.size() != rb.c2.size() || rb.c1.empty())
+      return set_err(GSV_E_SHAPE, "%s: convs1 / convs2 counts differ", pfx.c_str());
+    m.rbs.push_back(std::move(rb));
+  }
+  // Resblock widths must match their stage.
+  C = m.pre.d0;
+  for (size_t i = 0; i < m.ups.size(); ++i) {
+    C = m.ups[i].d1;
+    for (size_t r = 3 * i; r < std::min(3 * i + 3, m.rbs.size()); ++r)
+      if (m.rbs[r].c1[0].d0 != C)
+        return set_err(GSV_E_SHAPE, "dec.resblocks.%zu width %d != stage width %d", r, m.rbs[r].c1[0].d0, C);
+  }
+  if (m.post.d1 != C) return set_err(GSV_E_SHAPE, "dec.conv_post input width %d != %d", m.post.d1, C);
+  if (m.post.d0 != 1) return set_err(GSV_E_SHAPE, "dec.conv_post must have one output channel");
+  return GSV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Packed device form of one conv as a tap GEMM (see gsv_internal.h).
+
+struct GemmConv {
+  int Cin = 0, Cout = 0, N = 0, ntaps = 0, off0 = 0, offstep = 1;
+  int stride = 1, pad = 0, K = 0;  // ConvT: Q/crop/Lout derive from these
+  bool transposed = false;
+  size_t w_off = 0;  // byte offset in the weight arena
+  size_t b_off = 0;  // float offset in the bias arena
+  int Lout(int Lin) const {
+    return transposed ? (Lin - 1) * stride + K - 2 * pad : Lin + 2 * pad - (ntaps - 1) * offstep;
+  }
+  int Q(int Lin) const { return transposed ? (Lout(Lin) + pad - 1) / stride + 1 : Lout(Lin); }
+};
+
+struct Packer {
+  Dt dt;
+  std::vector<uint8_t> wbytes;
+  std::vector<float> biases;
+
+  size_t align(size_t a) {
+    size_t r = (wbytes.size() + a - 1) / a * a;
+    wbytes.resize(r);
+    return r;
+  }
+  // Element (tap j, column n, channel c) of the packed weight.
+  void put(size_t base, int ntaps, int N, int Cin, int j, int n, int c, float v) {
+    size_t idx = dt == Dt::F32 ? ((size_t)j * Cin + c) * N + n   // [tap][Cin][N]
+                               : ((size_t)j * N + n) * Cin + c;  // [tap][N][Cin] (K-major)
+    (void)ntaps;
+    if (dt == Dt::F32) {
+      memcpy(&wbytes[base + idx * 4], &v, 4);
+    } else {
+      __nv_bfloat16 h = __float2bfloat16_rn(v);
+      memcpy(&wbytes[base + idx * 2], &h, 2);
+    }
+  }
+  size_t esize() const { return dt == Dt::F32 ? 4 : 2; }
+
+  GemmConv conv(const HostConv& c) {
+    GemmConv g;
+    g.Cin = c.d1; g.Cout = c.d0; g.N = c.d0; g.ntaps = c.K;
+    g.off0 = -c.pad; g.offstep = c.dil; g.pad = c.pad; g.K = c.K;
+    g.w_off = align(1024);
+    wbytes.resize(g.w_off + (size_t)g.ntaps * g.N * g.Cin * esize());
+    for (int n = 0; n < g.N; ++n)
+      for (int ci = 0; ci < g.Cin; ++ci)
+        for (int j = 0; j < c.K; ++j)
+          put(g.w_off, g.ntaps, g.N, g.Cin, j, n, ci, c.w[((size_t)n * g.Cin + ci) * c.K + j]);
+    g.b_off = biases.size();
+    for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
+    return g;
+  }
+  // Polyphase ConvTranspose1d: tap m, column n = phi*Cout + o, channel c holds
+  // w[c][o][phi + m*s] (zero past the kernel).
+  GemmConv convT(const HostConv& c) {
+    GemmConv g;
+    g.transposed = true;
+    g.Cin = c.d0; g.Cout = c.d1; g.stride = c.stride; g.pad = c.pad; g.K = c.K;
+    g.ntaps = (c.K + c.stride - 1) / c.stride;
+    g.N = c.stride * g.Cout; g.off0 = 0; g.offstep = -1;
+    g.w_off = align(1024);
+    wbytes.resize(g.w_off + (size_t)g.ntaps * g.N * g.Cin * esize());
+    for (int m = 0; m < g.ntaps; ++m)
+      for (int phi = 0; phi < c.stride; ++phi)
+        for (int o = 0; o < g.Cout; ++o)
+          for (int ci = 0; ci < g.Cin; ++ci) {
+            const int kk = phi + m * c.stride;
+            const float v = kk < c.K ? c.w[((size_t)ci * g.Cout + o) * c.K + kk] : 0.0f;
+            put(g.w_off, g.ntaps, g.N, g.Cin, m, phi * g.Cout + o, ci, v);
+          }
+    g.b_off = biases.size();
+    for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
+    return g;
+  }
+};
+
+struct Stage {
+  GemmConv up;
+  std::vector<std::vector<GemmConv>> c1, c2;  // [branch][step]
+};
+
+}  // namespace
+}  // namespace gsv
+
+using namespace gsv;
+
+struct gsvdec {
+  int mode = GSV_MODE_FP32;
+  int device = 0;
+  Dt dt = Dt::F32;
+  int in_ch = 0, C0 = 0, gin = 0, hop = 1;
+  bool has_cond = false;
+  GemmConv pre;
+  std::vector<Stage> stages;
+  // conv_post (one output channel): weights [K][C] fp32 on device
+  int post_K = 0, post_pad = 0, post_C = 0;
+  float post_bias = 0.0f;
+  // device arenas
+  void* d_w = nullptr;
+  float* d_bias = nullptr;
+  float* d_cond_w = nullptr;  // [C0][gin]
+  float* d_cond_b = nullptr;
+  float* d_post_w = nullptr;
+  size_t w_bytes = 0;
+  // workspace
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  // stage timing (level 1) and per-launch profile (level 2)
+  int timing = 0;
+  cudaEvent_t ev[32] = {};
+  int n_ev = 0;
+  float stage_ms[5] = {0, 0, 0, 0, 0};
+  int launches = 0;
+  struct Rec {
+    std::string name;
+    int kind, nconv;
+    double flops, bytes;
+  };
+  // Level 2 keeps one event list per forward until the stats are read, so a
+  // timed loop of forwards needs no host sync: runs[k][0] starts forward k,
+  // runs[k][i + 1] ends its launch i.
+  std::vector<std::vector<cudaEvent_t>> runs;
+  std::vector<std::vector<Rec>> run_recs;
+  std::vector<cudaEvent_t> pool;
+  std::vector<gsvdec_launch_stat> stats;
+};
+
+namespace gsv {
+namespace {
+
+size_t act_bytes(const gsvdec* h) { return h->dt == Dt::F32 ? 4 : 2; }
+
+// Largest activation (elements per utterance) over all layers, for T0 frames.
+size_t max_act_elems(const gsvdec* h, int T0) {
+  size_t m = (size_t)T0 * std::max(h->C0, h->in_ch);
+  int L = T0;
+  for (const Stage& s : h->stages) {
+    L = s.up.Lout(L);
+    m = std::max(m, (size_t)L * s.up.Cout);
+  }
+  return m;
+}
+
+int out_len(const gsvdec* h, int T0) {
+  int L = T0;
+  for (const Stage& s : h->stages) L = s.up.Lout(L);
+  return L;
+}
+
+struct Workspace {
+  void* zin;
+  void* buf[12];  // X, AX, OUT, XR0-2, AXR0-2, T0-2
+  float* bias_bc;
+  int* lens;
+  float* zstage;  // host-mode staging of z / g / wav
+  float* gstage;
+  int* lstage;
+  float* wav;
+  float* tap;     // fp32 time-major tap scratch (debug taps only)
+};
+
+int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w) {
+  const size_t act = max_act_elems(h, T0) * (size_t)B;
+  const size_t eb = act_bytes(h);
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const int L = out_len(h, T0);
+  size_t need = 0;
+  size_t o_zin = need; need += al((size_t)B * T0 * h->in_ch * eb);
+  size_t o_buf = need; need += 12 * al(act * eb);
+  size_t o_bbc = need; need += al((size_t)B * h->C0 * 4);
+  size_t o_len = need; need += al((size_t)B * 16 * 4);
+  size_t o_zs = need; need += al((size_t)B * T0 * h->in_ch * 4);
+  size_t o_gs = need; need += al((size_t)B * std::max(h->gin, 1) * 4);
+  size_t o_ls = need; need += al((size_t)B * 4);
+  size_t o_wav = need; need += al((size_t)B * L * 4);
+  size_t o_tap = need; if (with_tap) need += al(act * 4);
+  if (need > h->ws_bytes) {
+    if (h->ws) CUDA_TRY(cudaFree(h->ws));
+    h->ws = nullptr;
+    h->ws_bytes = 0;
+    CUDA_TRY(cudaMalloc(&h->ws, need));
+    h->ws_bytes = need;
+  }
+  char* p = static_cast<char*>(h->ws);
+  w.zin = p + o_zin;
+  for (int i = 0; i < 12; ++i) w.buf[i] = p + o_buf + i * al(act * eb);
+  w.bias_bc = reinterpret_cast<float*>(p + o_bbc);
+  w.lens = reinterpret_cast<int*>(p + o_len);
+  w.zstage = reinterpret_cast<float*>(p + o_zs);
+  w.gstage = reinterpret_cast<float*>(p + o_gs);
+  w.lstage = reinterpret_cast<int*>(p + o_ls);
+  w.wav = reinterpret_cast<float*>(p + o_wav);
+  w.tap = with_tap ? reinterpret_cast<float*>(p + o_tap) : nullptr;
+  return GSV_OK;
+}
+
+TapSeg make_seg(const gsvdec* h, const GemmConv& g, const void* x, int Lin) {
+  TapSeg s{};
+  s.x = x;
+  s.w = static_cast<const char*>(h->d_w) + g.w_off;
+  s.Lin = Lin;
+  s.Cin = g.Cin;
+  s.ntaps = g.ntaps;
+  s.off0 = g.off0;
+  s.offstep = g.offstep;
+  return s;
+}
+
+TapConv make_op(const gsvdec* h, const GemmConv& g, int B, const void* x, int Lin) {
+  TapConv op{};
+  op.seg[0] = make_seg(h, g, x, Lin);
+  op.nseg = 1;
+  op.B = B;
+  op.Q = g.Q(Lin);
+  op.N = g.N;
+  op.Cout = g.Cout;
+  op.Lout = g.Lout(Lin);
+  op.crop = g.transposed ? g.pad * g.Cout : 0;
+  op.bias = h->d_bias + g.b_off;
+  op.div = 1.0f;
+  op.slope = 0.1f;
+  return op;
+}
+
+// Records the end of one kernel launch (per-launch profile, timing level 2).
+int after_launch(gsvdec* h, cudaStream_t st, const std::string& name, int kind, int nconv,
+                 double flops, double bytes) {
+  h->launches++;
+  if (h->timing < 2 || h->runs.empty()) return GSV_OK;
+  cudaEvent_t e;
+  if (!h->pool.empty()) {
+    e = h->pool.back();
+    h->pool.pop_back();
+  } else {
+    CUDA_TRY(cudaEventCreate(&e));
+  }
+  CUDA_TRY(cudaEventRecord(e, st));
+  h->runs.back().push_back(e);
+  h->run_recs.back().push_back({name, kind, nconv, flops, bytes});
+  return GSV_OK;
+}
+
+// Algorithmic work of one reference conv inside a tap GEMM (see gsvdec.h).
+struct Work {
+  double flops = 0, bytes = 0;
+  int nconv = 0;
+  void add(const GemmConv& g, int B, int Lin, int nres, double e) {
+    const int Lout = g.Lout(Lin);
+    flops += 2.0 * g.Cin * g.Cout * g.K * (double)Lin * B;
+    bytes += e * B * ((double)g.Cin * Lin + (double)g.Cout * Lout) + e * (double)g.Cin * g.Cout * g.K;
+    bytes += e * B * (double)g.Cout * Lout * nres;
+    nconv++;
+  }
+};
+
+int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& name,
+              const Work& wk) {
+  cudaError_t e;
+  if (h->dt == Dt::F32) {
+    e = launch_tapconv_f32(grp, st);
+  } else {
+    bool tc = true;
+    for (int i = 0; i < grp.n; ++i) tc = tc && tapconv_tc_supported(grp.op[i]);
+    e = tc ? launch_tapconv_tc(grp, st) : cudaErrorNotSupported;
+    if (!tc) return set_err(GSV_E_UNSUPPORTED, "layer geometry not supported by the tcgen05 kernel");
+  }
+  if (e != cudaSuccess) return set_err(GSV_E_CUDA, "tap-conv launch failed: %s", cudaGetErrorString(e));
+  return after_launch(h, st, name, 0, wk.nconv, wk.flops, wk.bytes);
+}
+
+int run_one(gsvdec* h, const TapConv& op, cudaStream_t st, const std::string& name,
+            const Work& wk) {
+  TapConvGroup g{};
+  g.op[0] = op;
+  g.n = 1;
+  return run_group(h, g, st, name, wk);
+}
+
+void mark(gsvdec* h, cudaStream_t st) {
+  if (h->timing == 1 && h->n_ev < 32) cudaEventRecord(h->ev[h->n_ev++], st);
+}
+
+// The whole forward on device buffers.  zsrc is NCL fp32 [B][in_ch][Tsrc]
+// (frames t_off .. t_off+T0), gdev [B][gin] or null, lens_in [B] or null.
+// taps (host, optional): reference-layout copies of each stage.
+int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const float* gdev,
+                   const int* lens_in, int B, int T0, float* wav_dev, Workspace& w,
+                   float* const* taps, cudaStream_t st) {
+  h->launches = 0;
+  h->n_ev = 0;
+  if (h->timing >= 2) {
+    cudaEvent_t e;
+    if (!h->pool.empty()) {
+      e = h->pool.back();
+      h->pool.pop_back();
+    } else {
+      CUDA_TRY(cudaEventCreate(&e));
+    }
+    CUDA_TRY(cudaEventRecord(e, st));
+    h->runs.push_back({e});
+    h->run_recs.push_back({});
+  }
+  mark(h, st);
+  const double eb = (double)act_bytes(h);
+  void* X = w.buf[0];
+  void* AX = w.buf[1];
+  void* OUT = w.buf[2];
+  void* XR[3] = {w.buf[3], w.buf[4], w.buf[5]};
+  void* AXR[3] = {w.buf[6], w.buf[7], w.buf[8]};
+  void* TT[3] = {w.buf[9], w.buf[10], w.buf[11]};
+  const int nst = (int)h->stages.size();
+  // Per-stage valid lengths (only when masking).
+  const int* lens = nullptr;
+  if (lens_in) {
+    int mul[16], add[16];
+    if (nst > 15) return set_err(GSV_E_UNSUPPORTED, "more than 15 upsample stages");
+    for (int s = 0; s < nst; ++s) {
+      const GemmConv& u = h->stages[s].up;
+      mul[s] = u.stride;
+      add[s] = u.K - 2 * u.pad - u.stride;
+    }
+    CUDA_TRY(launch_lengths(lens_in, B, T0, mul, add, nst, w.lens, st));
+    GSV_TRY(after_launch(h, st, "lengths", 1, 0, 0.0, 8.0 * B * (nst + 1)));
+    lens = w.lens;
+  }
+  auto stage_len = [&](int s) -> const int* { return lens ? lens + (size_t)s * B : nullptr; };
+
+  CUDA_TRY(launch_transpose_in(zsrc, B, h->in_ch, Tsrc, t_off, T0, lens ? lens : nullptr, w.zin, h->dt, st));
+  GSV_TRY(after_launch(h, st, "input_relayout", 1, 0, 0.0, (4.0 + eb) * B * h->in_ch * T0));
+  const float* bias_bc = nullptr;
+  if (h->has_cond && gdev) {
+    CUDA_TRY(launch_cond(gdev, h->d_cond_w, h->d_cond_b, B, h->gin, h->C0, w.bias_bc, st));
+    GSV_TRY(after_launch(h, st, "cond", 1, 1, 2.0 * B * h->gin * h->C0,
+                         4.0 * ((double)B * h->gin + (double)h->gin * h->C0 + (double)B * h->C0)));
+    bias_bc = w.bias_bc;
+  }
+  auto tap_out = [&](int idx, const void* src, int L, int C) -> int {
+    if (!taps || !taps[idx]) return GSV_OK;
+    CUDA_TRY(launch_to_ncl(src, h->dt, B, L, C, w.tap, st));
+    CUDA_TRY(cudaMemcpyAsync(taps[idx], w.tap, sizeof(float) * (size_t)B * L * C, cudaMemcpyDeviceToHost, st));
+    return GSV_OK;
+  };
+  // conv_pre (+ cond, folded into a per-utterance bias), LeakyReLU for the
+  // first upsample (:390-408).
+  int L = T0;
+  {
+    TapConv op = make_op(h, h->pre, B, w.zin, L);
+    op.bias_bc = bias_bc;
+    op.len = stage_len(0);
+    op.out_act = OUT;
+    op.slope = nst > 0 ? 0.1f : 0.01f;
+    if (taps && taps[0]) op.out_raw = X;
+    Work wk;
+    wk.add(h->pre, B, L, 0, eb);
+    GSV_TRY(run_one(h, op, st, "conv_pre", wk));
+    GSV_TRY(tap_out(0, X, L, h->C0));
+  }
+  mark(h, st);
+  for (int i = 0; i < nst; ++i) {
+    const Stage& sg = h->stages[i];
+    const bool last = i + 1 == nst;
+    const float next_slope = last ? 0.01f : 0.1f;
+    const int nb = (int)sg.c1.size();
+    const int Lin = L;
+    L = sg.up.Lout(Lin);
+    const int C = sg.up.Cout;
+    const int* len = stage_len(i + 1);
+    {
+      TapConv op = make_op(h, sg.up, B, OUT, Lin);
+      op.len = len;
+      op.out_raw = X;
+      op.out_act = nb > 0 ? AX : nullptr;
+      if (nb == 0) { op.out_act = AX; op.slope = next_slope; }
+      Work wk;
+      wk.add(sg.up, B, Lin, 0, eb);
+      GSV_TRY(run_one(h, op, st, "ups" + std::to_string(i), wk));
+    }
+    GSV_TRY(tap_out(1 + 2 * i, X, L, C));
+    mark(h, st);
+    if (nb == 0) {
+      std::swap(OUT, AX);
+      mark(h, st);
+      continue;
+    }
+    int max_steps = 0;
+    for (int r = 0; r < nb; ++r) max_steps = std::max(max_steps, (int)sg.c1[r].size());
+    for (int j = 0; j < max_steps; ++j) {
+      TapConvGroup g1{}, g2{};
+      Work w1, w2;
+      for (int r = 0; r < nb; ++r) {
+        const int S = (int)sg.c1[r].size();
+        if (j >= S) continue;
+        TapConv a = make_op(h, sg.c1[r][j], B, j == 0 ? AX : AXR[r], L);
+        a.len = len;
+        a.out_act = TT[r];
+        g1.op[g1.n++] = a;
+        w1.add(sg.c1[r][j], B, L, 0, eb);
+        if (j < S - 1) {
+          TapConv c = make_op(h, sg.c2[r][j], B, TT[r], L);
+          c.len = len;
+          c.res[0] = j == 0 ? X : XR[r];
+          c.nres = 1;
+          c.out_raw = XR[r];
+          c.out_act = AXR[r];
+          g2.op[g2.n++] = c;
+          w2.add(sg.c2[r][j], B, L, 1, eb);
+        }
+      }
+      const std::string nm = "rb" + std::to_string(i) + ".step" + std::to_string(j);
+      if (g1.n) GSV_TRY(run_group(h, g1, st, nm + ".conv1", w1));
+      if (g2.n) GSV_TRY(run_group(h, g2, st, nm + ".conv2", w2));
+    }
+    // Last step of every branch in one op: the branch sum and the true
+    // division by the branch count (:418-442) plus the next LeakyReLU.
+    {
+      TapConv f{};
+      Work wf;
+      for (int r = 0; r < nb; ++r) {
+        const int S = (int)sg.c1[r].size();
+        const GemmConv& g = sg.c2[r][S - 1];
+        wf.add(g, B, L, 1, eb);
+        if (r == 0) f = make_op(h, g, B, TT[r], L);
+        else f.seg[r] = make_seg(h, g, TT[r], L);
+        f.res[r] = S == 1 ? X : XR[r];
+      }
+      f.nseg = nb;
+      f.nres = nb;
+      f.bias = h->d_bias + sg.c2[0][sg.c2[0].size() - 1].b_off;  // replaced below when nb > 1
+      f.div = (float)nb;
+      f.len = len;
+      f.out_act = OUT;
+      f.slope = next_slope;
+      if (taps && taps[2 + 2 * i]) f.out_raw = AX;  // AX is dead by now
+      if (nb > 1) {
+        // Summed bias of the branches' last convs lives right after the stage's
+        // packed biases (set up at create time).
+        f.bias = h->d_bias + sg.c2.back().back().b_off + sg.c2.back().back().Cout;
+      }
+      GSV_TRY(run_one(h, f, st, "rb" + std::to_string(i) + ".final", wf));
+      GSV_TRY(tap_out(2 + 2 * i, AX, L, C));
+    }
+    mark(h, st);
+  }
+  // LeakyReLU(0.01) was applied by the producer; conv_post + tanh (:449-455).
+  CUDA_TRY(launch_post(OUT, h->dt, B, L, h->post_C, h->d_post_w, h->post_K, h->post_pad,
+                       h->post_bias, stage_len(nst), wav_dev, taps && taps[1 + 2 * nst] ? w.tap : nullptr, st));
+  GSV_TRY(after_launch(h, st, "conv_post", 2, 1, 2.0 * h->post_C * h->post_K * (double)L * B,
+                       eb * B * (double)h->post_C * L + 4.0 * B * (double)L + 4.0 * h->post_C * h->post_K));
+  if (taps && taps[1 + 2 * nst])
+    CUDA_TRY(cudaMemcpyAsync(taps[1 + 2 * nst], w.tap, sizeof(float) * (size_t)B * L, cudaMemcpyDeviceToHost, st));
+  mark(h, st);
+  return GSV_OK;
+}
+
+int collect_timing(gsvdec* h, cudaStream_t st) {
+  if (h->timing != 1 || h->n_ev < 3) return GSV_OK;
+  CUDA_TRY(cudaStreamSynchronize(st));
+  // events: [start, after pre, (after up_i, after rb_i) x nst, after post]
+  float pre = 0, up = 0, rb = 0, post = 0, tot = 0;
+  cudaEventElapsedTime(&pre, h->ev[0], h->ev[1]);
+  int k = 1;
+  for (size_t i = 0; i < h->stages.size() && k + 2 < h->n_ev; ++i) {
+    float a = 0, b = 0;
+    cudaEventElapsedTime(&a, h->ev[k], h->ev[k + 1]);
+    cudaEventElapsedTime(&b, h->ev[k + 1], h->ev[k + 2]);
+    up += a;
+    rb += b;
+    k += 2;
+  }
+  cudaEventElapsedTime(&post, h->ev[k], h->ev[h->n_ev - 1]);
+  cudaEventElapsedTime(&tot, h->ev[0], h->ev[h->n_ev - 1]);
+  h->stage_ms[0] = pre; h->stage_ms[1] = up; h->stage_ms[2] = rb; h->stage_ms[3] = post; h->stage_ms[4] = tot;
+  return GSV_OK;
+}
+
+int check_device(int device) {
+  int n = 0;
+  CUDA_TRY(cudaGetDeviceCount(&n));
+  if (device < 0 || device >= n) return set_err(GSV_E_INVALID_ARG, "device %d out of range (%d devices)", device, n);
+  cudaDeviceProp p;
+  CUDA_TRY(cudaGetDeviceProperties(&p, device));
+  if (p.major != 10)
+    return set_err(GSV_E_UNSUPPORTED, "device %d is sm_%d%d; libgsvdec is built for sm_100a (B200)", device, p.major, p.minor);
+  return GSV_OK;
+}
+
+int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t** out) {
+  if (!out) return set_err(GSV_E_INVALID_ARG, "out is NULL");
+  *out = nullptr;
+  if (!ts || n <= 0) return set_err(GSV_E_INVALID_ARG, "no tensors given");
+  if (mode != GSV_MODE_FP32 && mode != GSV_MODE_BF16) return set_err(GSV_E_INVALID_ARG, "bad mode %d", mode);
+  HostModel m;
+  GSV_TRY(load_model(ts, n, m));
+  GSV_TRY(check_device(device));
+  CUDA_TRY(cudaSetDevice(device));
+  std::unique_ptr<gsvdec> h(new gsvdec());
+  h->mode = mode;
+  h->device = device;
+  h->dt = mode == GSV_MODE_FP32 ? Dt::F32 : Dt::BF16;
+  h->in_ch = m.pre.d1;
+  h->C0 = m.pre.d0;
+  h->has_cond = m.has_cond;
+  h->gin = m.has_cond ? m.cond.d1 : 0;
+  Packer pk{h->dt};
+  h->pre = pk.conv(m.pre);
+  h->hop = 1;
+  for (size_t i = 0; i < m.ups.size(); ++i) {
+    Stage s;
+    s.up = pk.convT(m.ups[i]);
+    h->hop *= m.ups[i].stride;
+    for (size_t r = 3 * i; r < std::min(3 * i + 3, m.rbs.size()); ++r) {
+      std::vector<GemmConv> a, b;
+      for (auto& c : m.rbs[r].c1) a.push_back(pk.conv(c));
+      for (auto& c : m.rbs[r].c2) b.push_back(pk.conv(c));
+      s.c1.push_back(std::move(a));
+      s.c2.push_back(std::move(b));
+    }
+    // Summed bias of the branches' last convs (the fused 3-branch op).
+    if (s.c2.size() > 1) {
+      const int C = s.up.Cout;
+      std::vector<float> sum(C, 0.0f);
+      for (auto& br : s.c2)
+        for (int c = 0; c < C; ++c) sum[c] += pk.biases[br.back().b_off + c];
+      // Appended right after the last branch's last bias (see forward_device).
+      const size_t expect = s.c2.back().back().b_off + C;
+      if (pk.biases.size() != expect) return set_err(GSV_E_SHAPE, "internal bias layout error");
+      pk.biases.insert(pk.biases.end(), sum.begin(), sum.end());
+    }
+    h->stages.push_back(std::move(s));
+  }
+  if (h->dt == Dt::BF16) {
+    // Check every op geometry against the tcgen05 kernel at create time.
+    auto ok = [&](const GemmConv& g) {
+      TapConv op{};
+      op.nseg = 1; op.seg[0].Cin = g.Cin; op.seg[0].ntaps = g.ntaps; op.seg[0].offstep = g.offstep;
+      op.seg[0].off0 = g.off0; op.N = g.N; op.Cout = g.Cout;
+      return tapconv_tc_supported(op);
+    };
+    bool all = ok(h->pre);
+    for (auto& s : h->stages) {
+      all = all && ok(s.up);
+      for (auto& br : s.c1) for (auto& g : br) all = all && ok(g);
+      for (auto& br : s.c2) for (auto& g : br) all = all && ok(g);
+    }
+    if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the bf16 tcgen05 kernel");
+  }
+  h->post_K = m.post.K;
+  h->post_pad = m.post.pad;
+  h->post_C = m.post.d1;
+  h->post_bias = m.post.b.empty() ? 0.0f : m.post.b[0];
+  if (h->post_C != 16 || h->post_K > 64)
+    return set_err(GSV_E_UNSUPPORTED, "conv_post with %d input channels / kernel %d is not supported", h->post_C, h->post_K);
+  std::vector<float> post_w((size_t)h->post_K * h->post_C);  // [K][C]
+  for (int c = 0; c < h->post_C; ++c)
+    for (int j = 0; j < h->post_K; ++j) post_w[(size_t)j * h->post_C + c] = m.post.w[(size_t)c * h->post_K + j];
+  // Upload.
+  h->w_bytes = pk.wbytes.size();
+  CUDA_TRY(cudaMalloc(&h->d_w, std::max<size_t>(h->w_bytes, 256)));
+  CUDA_TRY(cudaMemcpy(h->d_w, pk.wbytes.data(), h->w_bytes, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMalloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
+  CUDA_TRY(cudaMemcpy(h->d_bias, pk.biases.data(), sizeof(float) * pk.biases.size(), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMalloc(&h->d_post_w, sizeof(float) * post_w.size()));
+  CUDA_TRY(cudaMemcpy(h->d_post_w, post_w.data(), sizeof(float) * post_w.size(), cudaMemcpyHostToDevice));
+  if (h->has_cond) {
+    CUDA_TRY(cudaMalloc(&h->d_cond_w, sizeof(float) * m.cond.w.size()));
+    CUDA_TRY(cudaMemcpy(h->d_cond_w, m.cond.w.data(), sizeof(float) * m.cond.w.size(), cudaMemcpyHostToDevice));
+    std::vector<float> cb(h->C0, 0.0f);
+    if (!m.cond.b.empty()) cb = m.cond.b;
+    CUDA_TRY(cudaMalloc(&h->d_cond_b, sizeof(float) * cb.size()));
+    CUDA_TRY(cudaMemcpy(h->d_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
+  }
+  for (auto& e : h->ev) CUDA_TRY(cudaEventCreate(&e));
+  *out = h.release();
+  return GSV_OK;
+}
+
+void destroy_impl(gsvdec* h) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(h->device);
+  cudaFree(h->d_w);
+  cudaFree(h->d_bias);
+  cudaFree(h->d_cond_w);
+  cudaFree(h->d_cond_b);
+  cudaFree(h->d_post_w);
+  cudaFree(h->ws);
+  for (auto& e : h->ev)
+    if (e) cudaEventDestroy(e);
+  for (auto& run : h->runs)
+    for (auto& e : run) cudaEventDestroy(e);
+  for (auto& e : h->pool) cudaEventDestroy(e);
+  cudaSetDevice(prev);
+  delete h;
+}
+
+int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengths, int B,
+                 int Tsrc, int t_off, int T0, float* wav, int mem_kind, cudaStream_t st,
+                 float* const* taps, int64_t wav_skip, int64_t wav_count) {
+  if (!h) return set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (!z || !wav) return set_err(GSV_E_INVALID_ARG, "z and wav must not be NULL");
+  if (B <= 0 || T0 <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+    return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
+  if ((int64_t)B * max_act_elems(h, T0) > (int64_t)1 << 40)
+    return set_err(GSV_E_INVALID_ARG, "request too large");
+  CUDA_TRY(cudaSetDevice(h->device));
+  Workspace w;
+  GSV_TRY(ensure_ws(h, B, T0, taps != nullptr, w));
+  const int L = out_len(h, T0);
+  const float* zd = z;
+  const float* gd = (h->has_cond && g) ? g : nullptr;
+  const int* ld = lengths;
+  float* wd = wav;
+  if (mem_kind == GSV_MEM_HOST) {
+    // Copy only the requested frames of each channel row.
+    CUDA_TRY(cudaMemcpy2DAsync(w.zstage, sizeof(float) * T0, z + t_off, sizeof(float) * Tsrc,
+                               sizeof(float) * T0, (size_t)B * h->in_ch, cudaMemcpyHostToDevice, st));
+    zd = w.zstage;
+    Tsrc = T0;
+    t_off = 0;
+    if (gd) {
+      CUDA_TRY(cudaMemcpyAsync(w.gstage, g, sizeof(float) * (size_t)B * h->gin, cudaMemcpyHostToDevice, st));
+      gd = w.gstage;
+    }
+    if (lengths) {
+      CUDA_TRY(cudaMemcpyAsync(w.lstage, lengths, sizeof(int) * (size_t)B, cudaMemcpyHostToDevice, st));
+      ld = w.lstage;
+    }
+  }
+  const bool direct = mem_kind == GSV_MEM_DEVICE && wav_skip == 0 && wav_count == (int64_t)B * L;
+  GSV_TRY(forward_device(h, zd, Tsrc, t_off, gd, ld, B, T0, direct ? wd : w.wav, w, taps, st));
+  if (!direct) {
+    CUDA_TRY(cudaMemcpyAsync(wav, w.wav + wav_skip, sizeof(float) * (size_t)wav_count,
+                             mem_kind == GSV_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
+  }
+  if (mem_kind == GSV_MEM_HOST || taps) CUDA_TRY(cudaStreamSynchronize(st));
+  GSV_TRY(collect_timing(h, st));
+  return GSV_OK;
+}
+
+}  // namespace
+}  // namespace gsv
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+const char* gsvdec_last_error(void) { return gsv::g_last_error.c_str(); }
+
+int gsvdec_create(const gsvdec_tensor* tensors, int n_tensors, int mode, int device, gsvdec_t** out) {
+  try {
+    return gsv::create_impl(tensors, n_tensors, mode, device, out);
+  } catch (const std::bad_alloc&) {
+    return gsv::set_err(GSV_E_OOM, "host allocation failed");
+  } catch (const std::exception& e) {
+    return gsv::set_err(GSV_E_INVALID_ARG, "%s", e.what());
+  }
+}
+
+int gsvdec_create_from_file(const char* path, int mode, int device, gsvdec_t** out) {
+  if (!path || !out) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  try {
+    gsv::StFile f;
+    std::string err;
+    if (!f.open(path, err)) return gsv::set_err(GSV_E_INVALID_ARG, "%s", err.c_str());
+    // Only the decoder's tensors; float dtypes as in src/utils/weights.rs:140-151.
+    std::vector<gsvdec_tensor> ts;
+    for (const gsv::StEntry& e : f.entries()) {
+      if (e.name.compare(0, 4, "dec.") != 0) continue;
+      gsvdec_tensor t{};
+      t.name = e.name.c_str();
+      if (e.dtype == "F32") t.dtype = GSV_DTYPE_F32;
+      else if (e.dtype == "F16") t.dtype = GSV_DTYPE_F16;
+      else if (e.dtype == "BF16") t.dtype = GSV_DTYPE_BF16;
+      else return gsv::set_err(GSV_E_DTYPE, "Unsupported dtype %s for %s", e.dtype.c_str(), e.name.c_str());
+      if (e.shape.empty() || e.shape.size() > 4)
+        return gsv::set_err(GSV_E_SHAPE, "%s: rank %zu not supported", e.name.c_str(), e.shape.size());
+      t.ndim = (int)e.shape.size();
+      for (int d = 0; d < t.ndim; ++d) t.shape[d] = e.shape[d];
+      t.data = e.data;
+      ts.push_back(t);
+    }
+    if (ts.empty()) return gsv::set_err(GSV_E_MISSING_KEY, "no dec.* tensors in %s", path);
+    return gsv::create_impl(ts.data(), (int)ts.size(), mode, device, out);
+  } catch (const std::bad_alloc&) {
+    return gsv::set_err(GSV_E_OOM, "host allocation failed");
+  }
+}
+
+int gsvdec_destroy(gsvdec_t* h) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  gsv::destroy_impl(h);
+  return GSV_OK;
+}
+
+int gsvdec_get_info(const gsvdec_t* h, gsvdec_info* info) {
+  if (!h || !info) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  info->mode = h->mode;
+  info->device = h->device;
+  info->in_channels = h->in_ch;
+  info->gin_channels = h->gin;
+  info->n_upsamples = (int)h->stages.size();
+  int nrb = 0;
+  for (auto& s : h->stages) nrb += (int)s.c1.size();
+  info->n_resblocks = nrb;
+  info->hop = h->hop;
+  // Receptive field in input frames: conv_pre pad, then each stage's ConvT
+  // taps and resblock halo scaled back by the cumulative stride (rounded up).
+  double halo = h->pre.pad;
+  double rate = 1.0;
+  for (auto& s : h->stages) {
+    halo += (double)(s.up.ntaps) / 1.0 / rate;
+    rate *= s.up.stride;
+    int rbh = 0;
+    for (size_t r = 0; r < s.c1.size(); ++r) {
+      int hh = 0;
+      for (size_t j = 0; j < s.c1[r].size(); ++j)
+        hh += (s.c1[r][j].ntaps - 1) * s.c1[r][j].offstep / 2 + (s.c2[r][j].ntaps - 1) / 2;
+      rbh = std::max(rbh, hh);
+    }
+    halo += rbh / rate;
+  }
+  halo += (double)h->post_pad / rate;
+  info->receptive_halo = (int)std::ceil(halo);
+  info->weight_bytes = (int64_t)h->w_bytes;
+  return GSV_OK;
+}
+
+int gsvdec_forward(gsvdec_t* h, const float* z, const float* g, const int32_t* lengths, int B,
+                   int T0, float* wav, int mem_kind, void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  const int64_t L = gsv::out_len(h, T0 > 0 ? T0 : 1);
+  return gsv::forward_impl(h, z, g, lengths, B, T0, 0, T0, wav, mem_kind,
+                           static_cast<cudaStream_t>(stream), nullptr, 0, (int64_t)B * L);
+}
+
+int gsvdec_forward_chunk(gsvdec_t* h, const float* z, const float* g, int T0, int frame_begin,
+                         int frame_end, int halo, float* wav, int mem_kind, void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (T0 <= 0 || frame_begin < 0 || frame_end > T0 || frame_begin >= frame_end || halo < 0)
+    return gsv::set_err(GSV_E_INVALID_ARG, "bad chunk [%d, %d) of %d frames (halo %d)", frame_begin, frame_end, T0, halo);
+  const int lo = std::max(0, frame_begin - halo), hi = std::min(T0, frame_end + halo);
+  const int64_t skip = (int64_t)(frame_begin - lo) * h->hop;
+  const int64_t count = (int64_t)(frame_end - frame_begin) * h->hop;
+  return gsv::forward_impl(h, z, g, nullptr, 1, T0, lo, hi - lo, wav, mem_kind,
+                           static_cast<cudaStream_t>(stream), nullptr, skip, count);
+}
+
+int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int T0, float* wav,
+                        float* const* taps, int n_taps) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (!taps || n_taps != 2 + 2 * (int)h->stages.size())
+    return gsv::set_err(GSV_E_INVALID_ARG, "n_taps must be %d", 2 + 2 * (int)h->stages.size());
+  const int64_t L = gsv::out_len(h, T0 > 0 ? T0 : 1);
+  return gsv::forward_impl(h, z, g, nullptr, B, T0, 0, T0, wav, GSV_MEM_HOST, nullptr, taps, 0,
+                           (int64_t)B * L);
+}
+
+int gsvdec_set_stage_timing(gsvdec_t* h, int enable) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (enable < 0 || enable > 2) return gsv::set_err(GSV_E_INVALID_ARG, "timing level must be 0, 1 or 2");
+  h->timing = enable;
+  return GSV_OK;
+}
+
+int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* n) {
+  if (!h || !n || (max > 0 && !out)) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  // Fold the pending forwards into per-launch averages (only forwards whose
+  // launch sequence matches the last one are averaged), then recycle events.
+  if (!h->runs.empty()) {
+    CUDA_TRY(cudaSetDevice(h->device));
+    const auto& ref = h->run_recs.back();
+    std::vector<double> ms(ref.size(), 0.0);
+    int used = 0;
+    for (size_t k = 0; k < h->runs.size(); ++k) {
+      const auto& ev = h->runs[k];
+      const auto& rc = h->run_recs[k];
+      if (rc.size() != ref.size() || ev.size() != rc.size() + 1) continue;
+      bool same = true;
+      for (size_t i = 0; i < rc.size() && same; ++i) same = rc[i].name == ref[i].name;
+      if (!same) continue;
+      CUDA_TRY(cudaEventSynchronize(ev.back()));
+      for (size_t i = 0; i < rc.size(); ++i) {
+        float t = 0.0f;
+        CUDA_TRY(cudaEventElapsedTime(&t, ev[i], ev[i + 1]));
+        ms[i] += t;
+      }
+      used++;
+    }
+    h->stats.clear();
+    for (size_t i = 0; i < ref.size(); ++i) {
+      gsvdec_launch_stat s{};
+      snprintf(s.name, sizeof s.name, "%s", ref[i].name.c_str());
+      s.kind = ref[i].kind;
+      s.n_convs = ref[i].nconv;
+      s.flops = ref[i].flops;
+      s.bytes = ref[i].bytes;
+      s.ms = used ? (float)(ms[i] / used) : 0.0f;
+      h->stats.push_back(s);
+    }
+    for (auto& run : h->runs)
+      for (auto& e : run) h->pool.push_back(e);
+    h->runs.clear();
+    h->run_recs.clear();
+  }
+  *n = (int)h->stats.size();
+  for (int i = 0; i < max && i < *n; ++i) out[i] = h->stats[i];
+  return GSV_OK;
+}
+
+int gsvdec_get_stage_times(gsvdec_t* h, float ms[5]) {
+  if (!h || !ms) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  for (int i = 0; i < 5; ++i) ms[i] = h->stage_ms[i];
+  return GSV_OK;
+}
+
+int gsvdec_launch_count(gsvdec_t* h, int B, int T0, int* count) {
+  if (!h || !count) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  (void)B;
+  (void)T0;
+  *count = h->launches;
+  return GSV_OK;
+}
+
+}  // extern "C"

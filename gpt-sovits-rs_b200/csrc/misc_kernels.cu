@@ -1,0 +1,170 @@
+// misc_kernels.cu -- the small memory-bound kernels around the conv stack:
+// input relayout, the speaker-cond 1x1 conv, per-stage lengths, conv_post +
+// tanh, and the time-major -> reference-layout copy used by the debug taps.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "gsv_epilogue.cuh"
+#include "gsv_kernels.h"
+
+namespace gsv {
+
+namespace {
+
+// 32x32 tiled transpose of z [B][Cin][Tsrc] (frames t_off..t_off+T) into
+// [B][T][Cin]; frames past len[b] become 0 (the masked utterance end).
+template <typename T>
+__global__ void transpose_in_kernel(const float* __restrict__ z, int Cin, int Tsrc, int t_off,
+                                    int Tn, const int* __restrict__ len, T* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const int lim = len ? len[b] : Tn;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + threadIdx.x;
+    float v = 0.0f;
+    if (c < Cin && t < Tn && t < lim) v = z[((size_t)b * Cin + c) * Tsrc + t_off + t];
+    tile[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + threadIdx.x;
+    if (t < Tn && c < Cin) st_act<T>(out, ((size_t)b * Tn + t) * Cin + c, tile[threadIdx.x][i]);
+  }
+}
+
+// One warp per output channel: bias_bc[b][c] = bc[c] + sum_i wc[c][i] g[b][i].
+__global__ void cond_kernel(const float* __restrict__ g, const float* __restrict__ wc,
+                            const float* __restrict__ bc, int B, int gin, int C,
+                            float* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (warp >= B * C) return;
+  const int b = warp / C, c = warp % C;
+  float s = 0.0f;
+  for (int i = lane; i < gin; i += 32) s = fmaf(wc[(size_t)c * gin + i], g[(size_t)b * gin + i], s);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[(size_t)b * C + c] = s + (bc ? bc[c] : 0.0f);
+}
+
+struct StageLen {
+  int mul[16];
+  int add[16];
+};
+
+__global__ void lengths_kernel(const int* __restrict__ len_in, int B, int T0, StageLen sl,
+                               int nstage, int* __restrict__ lens) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  int l = len_in ? len_in[b] : T0;
+  l = l < 0 ? 0 : (l > T0 ? T0 : l);
+  lens[b] = l;
+  for (int s = 0; s < nstage; ++s) {
+    l = l > 0 ? l * sl.mul[s] + sl.add[s] : 0;
+    lens[(s + 1) * B + b] = l;
+  }
+}
+
+// conv_post: Cout 1, so one thread per output sample; the CTA stages its
+// haloed window of x (time-major, C channels) in shared memory.
+template <typename T, int C>
+__global__ void post_kernel(const T* __restrict__ x, int L, const float* __restrict__ w, int K,
+                            int pad, float bias, const int* __restrict__ len,
+                            float* __restrict__ wav, float* __restrict__ pre) {
+  constexpr int TT = 256;
+  extern __shared__ float sx[];  // [(TT + K - 1)][C]
+  __shared__ float sw[64 * C];
+  const int b = blockIdx.y;
+  const int t0 = blockIdx.x * TT;
+  const int rows = TT + K - 1;
+  for (int i = threadIdx.x; i < K * C; i += blockDim.x) sw[i] = w[i];
+  const T* xb = x + (size_t)b * L * C;
+  for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
+    const int r = i / C, c = i % C;
+    const int t = t0 - pad + r;
+    sx[i] = (t >= 0 && t < L) ? ld_act<T>(xb, (size_t)t * C + c) : 0.0f;
+  }
+  __syncthreads();
+  const int t = t0 + threadIdx.x;
+  if (t >= L) return;
+  float s = 0.0f;
+  for (int j = 0; j < K; ++j)
+#pragma unroll
+    for (int c = 0; c < C; ++c) s = fmaf(sx[(threadIdx.x + j) * C + c], sw[j * C + c], s);
+  s += bias;
+  const bool dead = len && t >= len[b];
+  if (pre) pre[(size_t)b * L + t] = dead ? 0.0f : s;
+  wav[(size_t)b * L + t] = dead ? 0.0f : tanhf(s);
+}
+
+template <typename T>
+__global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __restrict__ y) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (t < L && c < C) ? ld_act<T>(x, ((size_t)b * L + t) * C + c) : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + threadIdx.x;
+    if (c < C && t < L) y[((size_t)b * C + c) * L + t] = tile[threadIdx.x][i];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_off, int T,
+                                const int* len, void* zt, Dt dt, cudaStream_t st) {
+  dim3 grid(cdiv(T, 32), cdiv(Cin, 32), B), block(32, 8);
+  if (dt == Dt::F32)
+    transpose_in_kernel<float><<<grid, block, 0, st>>>(z, Cin, Tsrc, t_off, T, len,
+                                                       static_cast<float*>(zt));
+  else
+    transpose_in_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(
+        z, Cin, Tsrc, t_off, T, len, static_cast<__nv_bfloat16*>(zt));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_cond(const float* g, const float* wc, const float* bc, int B, int gin, int C,
+                        float* bias_bc, cudaStream_t st) {
+  const int warps = B * C;
+  cond_kernel<<<cdiv(warps * 32, 256), 256, 0, st>>>(g, wc, bc, B, gin, C, bias_bc);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, const int* add,
+                           int nstage, int* lens, cudaStream_t st) {
+  if (nstage > 15) return cudaErrorInvalidValue;
+  StageLen sl{};
+  for (int s = 0; s < nstage; ++s) { sl.mul[s] = mul[s]; sl.add[s] = add[s]; }
+  lengths_kernel<<<cdiv(B, 128), 128, 0, st>>>(len_in, B, T0, sl, nstage, lens);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, int K, int pad,
+                        float bias, const int* len, float* wav, float* pre, cudaStream_t st) {
+  if (K > 64 || C != 16) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (size_t)(256 + K - 1) * C;
+  dim3 grid(cdiv(L, 256), B);
+  if (dt == Dt::F32)
+    post_kernel<float, 16><<<grid, 256, smem, st>>>(static_cast<const float*>(x), L, w, K, pad,
+                                                    bias, len, wav, pre);
+  else
+    post_kernel<__nv_bfloat16, 16><<<grid, 256, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), L, w, K, pad, bias, len, wav, pre);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st) {
+  dim3 grid(cdiv(L, 32), cdiv(C, 32), B), block(32, 8);
+  if (dt == Dt::F32)
+    to_ncl_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(x), L, C, y);
+  else
+    to_ncl_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(x), L,
+                                                         C, y);
+  return cudaGetLastError();
+}
+
+}  // namespace gsv

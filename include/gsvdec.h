@@ -1,0 +1,173 @@
+/*
+ * gsvdec.h -- C ABI of libgsvdec, the B200 (sm_100a) SoVITS v2 Generator
+ * (HiFi-GAN style vocoder) of gpt-sovits-rs.
+ *
+ * The library replaces the reference crate's decoder call path:
+ *   Decoder::load(&StateDict, &Device, DType)   src/models/sovits_decoder.rs:231
+ *   Decoder::forward(&self, &Tensor, Option<&Tensor>) -> Result<Vec<f32>>
+ *                                                src/models/sovits_decoder.rs:386
+ * called by SoVITSModel::synthesize_with_speed_and_sv (src/models/sovits.rs:400).
+ * Weights are consumed as the unchanged safetensors `dec.*` tensors
+ * (src/models/sovits_decoder.rs:231-293, src/utils/weights.rs:116-162).
+ *
+ * Conventions: every call returns GSV_OK (0) or a negative GSV_E_* code and
+ * leaves a thread-local message for gsvdec_last_error().  No torch or CUDA
+ * types appear in the signatures: a stream is passed as `void*`
+ * (a cudaStream_t, NULL = the legacy default stream).  One handle owns one
+ * device's packed weights and workspace; calls on one handle must not
+ * overlap (the reference serialises forward behind a mutex,
+ * src/server/pipeline_registry.rs:204-205); distinct handles are independent.
+ */
+#ifndef GSVDEC_H
+#define GSVDEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  The reference reports these cases as crate::Error values
+ * (src/lib.rs:76-97): ModelLoadError for missing keys / bad shapes,
+ * InferenceError for runtime failures. */
+#define GSV_OK 0
+#define GSV_E_INVALID_ARG (-1)  /* null pointer, bad size, bad enum */
+#define GSV_E_MISSING_KEY (-2)  /* a required dec.* tensor is absent */
+#define GSV_E_SHAPE (-3)        /* tensor shapes disagree with the Generator layout */
+#define GSV_E_DTYPE (-4)        /* tensor dtype not in {F32, F16, BF16} */
+#define GSV_E_CUDA (-5)         /* CUDA runtime / driver error */
+#define GSV_E_OOM (-6)          /* device allocation failed */
+#define GSV_E_UNSUPPORTED (-7)  /* device is not sm_100 / feature not built */
+#define GSV_E_TIMEOUT (-8)      /* a bounded device wait gave up */
+
+/* Element types of a weight tensor: the safetensors dtypes the reference
+ * loader accepts for float weights (src/utils/weights.rs:140-151). */
+#define GSV_DTYPE_F32 0
+#define GSV_DTYPE_F16 1
+#define GSV_DTYPE_BF16 2
+
+/* Arithmetic modes.  FP32: fp32 CUDA-core convolutions (the reference's own
+ * F32 arithmetic, src/config/mod.rs:52-58).  BF16: bf16 operands and
+ * activations, fp32 accumulation on tcgen05 tensor cores. */
+#define GSV_MODE_FP32 0
+#define GSV_MODE_BF16 1
+
+/* Where the z / g / lengths / wav pointers of a forward call live. */
+#define GSV_MEM_HOST 0    /* host memory; the call copies in and out and syncs the stream */
+#define GSV_MEM_DEVICE 1  /* device memory on the handle's device; the call is stream-async */
+
+typedef struct gsvdec_tensor {
+  const char* name;   /* safetensors key, e.g. "dec.ups.0.weight_v" */
+  int dtype;          /* GSV_DTYPE_* */
+  int ndim;           /* 1..4 */
+  int64_t shape[4];
+  const void* data;   /* host pointer, contiguous row-major */
+} gsvdec_tensor;
+
+typedef struct gsvdec gsvdec_t;
+
+typedef struct gsvdec_info {
+  int mode;             /* GSV_MODE_* */
+  int device;
+  int in_channels;      /* conv_pre input width (192 for v2) */
+  int gin_channels;     /* cond input width, 0 when dec.cond is absent */
+  int n_upsamples;      /* 5 for v2 */
+  int n_resblocks;      /* 15 for v2 */
+  int hop;              /* product of the upsample strides: samples per frame (640) */
+  int receptive_halo;   /* input frames each side that influence one output frame */
+  int64_t weight_bytes; /* packed device weight bytes */
+} gsvdec_info;
+
+/* Decoder::load (src/models/sovits_decoder.rs:231-293): folds weight norm
+ * (src/utils/weights.rs:589-614), packs the weights for `mode` and uploads
+ * them to `device`.  The tensors are only read during the call. */
+int gsvdec_create(const gsvdec_tensor* tensors, int n_tensors, int mode, int device,
+                  gsvdec_t** out);
+
+/* Same as gsvdec_create, reading the tensors from a safetensors file
+ * (the format written by src/bin/gpt-sovits-convert.rs:282-309 and read by
+ * src/utils/weights.rs:116-162).  Non-`dec.` tensors are ignored. */
+int gsvdec_create_from_file(const char* safetensors_path, int mode, int device, gsvdec_t** out);
+
+int gsvdec_destroy(gsvdec_t* h);
+
+int gsvdec_get_info(const gsvdec_t* h, gsvdec_info* info);
+
+/* Decoder::forward (src/models/sovits_decoder.rs:386-458).
+ *   z       [B, in_channels, T0] fp32 (the flow output times y_mask)
+ *   g       [B, gin_channels, 1] fp32, or NULL (no cond add, :393-399)
+ *   lengths [B] valid frame counts, or NULL (all T0, the reference's
+ *           behaviour).  With lengths, utterance b is decoded exactly as if it
+ *           were alone with length lengths[b]; its samples past
+ *           hop*lengths[b] are written as 0.
+ *   wav     [B, hop*T0] fp32, utterances concatenated (the flattened Vec<f32>
+ *           of :458).
+ * mem_kind says where z/g/lengths/wav live (GSV_MEM_*). */
+int gsvdec_forward(gsvdec_t* h, const float* z, const float* g, const int32_t* lengths, int B,
+                   int T0, float* wav, int mem_kind, void* stream);
+
+/* One time chunk of a single long utterance (z [1, in_channels, T0]):
+ * decodes frames [frame_begin, frame_end) using `halo` extra input frames on
+ * each side (clamped to the utterance) and writes the hop*(frame_end -
+ * frame_begin) samples of that span to wav.  With halo >= receptive_halo the
+ * samples equal those of the whole-utterance forward.  No reference
+ * counterpart: the reference decodes an utterance whole
+ * (src/models/sovits_decoder.rs:386). */
+int gsvdec_forward_chunk(gsvdec_t* h, const float* z, const float* g, int T0, int frame_begin,
+                         int frame_end, int halo, float* wav, int mem_kind, void* stream);
+
+/* Per-layer taps of Decoder::forward_debug (src/models/sovits_decoder.rs:
+ * 473-526), in the reference's [B, C, T] layout, fp32, host memory:
+ *   taps[0]          conv_pre (+cond)            [B, 512, T0]
+ *   taps[1 + 2i]     after upsample i            [B, C_i, L_i]
+ *   taps[2 + 2i]     resblock average, stage i   [B, C_i, L_i]
+ *   taps[1 + 2 n_up] conv_post before tanh       [B, 1, L]
+ * n_taps must be 2 + 2 n_upsamples; any entry may be NULL. */
+int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int T0,
+                        float* wav, float* const* taps, int n_taps);
+
+/* Stage timers, the counterpart of the reference's "profile decoder
+ * pre/upsample/resblocks/post" line (src/models/sovits_decoder.rs:459-468):
+ * with enable = 1 the following forwards record CUDA events between stages,
+ * with enable = 2 also one event after every kernel launch (see
+ * gsvdec_get_launch_stats); 0 switches it off.  No host sync is added inside
+ * the launch sequence; the times are read back when the forward returns.
+ * ms[0] pre, ms[1] upsample (sum), ms[2] resblocks (sum), ms[3] post,
+ * ms[4] total. */
+int gsvdec_set_stage_timing(gsvdec_t* h, int enable);
+int gsvdec_get_stage_times(gsvdec_t* h, float ms[5]);
+
+/* Number of kernels the most recent forward on this handle launched
+ * (B and T0 are accepted for future shape queries and ignored today). */
+int gsvdec_launch_count(gsvdec_t* h, int B, int T0, int* count);
+
+/* Per-launch profile, recorded when stage timing is enabled with level 2
+ * (gsvdec_set_stage_timing(h, 2)): one CUDA-event interval per kernel launch
+ * on the forward's stream.  Forwards accumulate without any host sync until
+ * this call, which waits for them and returns each launch's duration
+ * averaged over the accumulated forwards (those with the same launch
+ * sequence as the most recent one), then starts a new accumulation.  flops and bytes are
+ * the ALGORITHMIC work of the reference layers the launch computes
+ * (F = 2 Cin Cout k L_in B per conv, ConvTranspose counted on input
+ * samples; bytes = e B (Cin L_in + Cout L_out) + e Cin Cout k per conv plus
+ * e B Cout L_out per residual read, e = activation element size), so that
+ * the layer roofline max(F / peak, bytes / bandwidth) can be formed.
+ * No reference counterpart beyond its stage timer line. */
+typedef struct gsvdec_launch_stat {
+  char name[48];   /* e.g. "conv_pre", "ups2", "rb3.step1.conv1", "rb3.final" */
+  int kind;        /* 0 tap-GEMM conv, 1 relayout / cond / lengths, 2 conv_post */
+  int n_convs;     /* reference conv layers inside this launch */
+  double flops;
+  double bytes;
+  float ms;
+} gsvdec_launch_stat;
+int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* n);
+
+/* Thread-local message describing the last error on this thread. */
+const char* gsvdec_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSVDEC_H */

@@ -1,0 +1,31 @@
+/* gsv_oracle.h -- test-infrastructure CPU restatement of the gpt-sovits-rs
+ * SoVITS v2 Generator.  Only tests/, the smoke check and the CPU-baseline leg
+ * of bench.py may use it; the product never does. */
+#ifndef GSV_ORACLE_H
+#define GSV_ORACLE_H
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+  const char* name;   /* safetensors key, e.g. "dec.ups.0.weight_v" */
+  const float* data;  /* host fp32, contiguous */
+  int ndim;
+  int64_t shape[4];
+} gsvo_tensor;
+
+const char* gsvo_last_error(void);
+void gsvo_leaky_relu(float* x, int64_t n, float slope);
+void gsvo_weight_norm(const float* v, const float* g, int O, int I, int K, float* w);
+int gsvo_conv1d(const float* x, int B, int Cin, int L, const float* w, int Cout, int K, int pad,
+                int dil, const float* bias, float* y, int acc64);
+int gsvo_conv_transpose1d(const float* x, int B, int Cin, int L, const float* w, int Cout, int K,
+                          int stride, int pad, const float* bias, float* y, int acc64);
+int gsvo_decoder_forward(const gsvo_tensor* ts, int n_tensors, const float* z, const float* g,
+                         int B, int T0, float* wav, float** taps, int acc64, int nthreads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

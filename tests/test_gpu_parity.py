@@ -1,0 +1,161 @@
+"""Parity of the CUDA Generator (through the C ABI) with the CPU oracle.
+
+FP32 mode: the spec bar is waveform max-abs <= 1e-4; because N(0, 0.01)
+weights shrink the waveform to ~1e-6, every case is also held to a relative
+bar (max |err| / max |ref| <= 1e-4) and run with O(1)-gain weights too.
+BF16 mode (bf16 operands/activations, fp32 accumulation): waveform SNR >=
+30 dB and per-layer relative L2 <= 1e-2.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_l2, rel_max, snr_db
+
+pytestmark = pytest.mark.gpu
+
+FP32_ABS = 1e-4
+FP32_REL = 1e-4
+BF16_SNR_DB = 30.0
+BF16_LAYER_REL_L2 = 1e-2
+
+
+@pytest.fixture(scope="module")
+def sd_unit(gsv):
+    return gsv.synth.make_state_dict(0, init="unit", bias="rand")
+
+
+@pytest.fixture(scope="module")
+def sd_n001(gsv):
+    return gsv.synth.make_state_dict(0, init="n001", bias="zero")
+
+
+@pytest.fixture(scope="module")
+def dec_fp32(gsv, sd_unit):
+    d = gsv.Decoder.load(sd_unit, device=0, mode="fp32")
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("T0", [1, 2, 3, 7])
+@pytest.mark.parametrize("init,bias", [("unit", "rand"), ("n001", "zero")])
+def test_fp32_tiny_matches_golden(gsv, tiny, init, bias, T0):
+    sd = gsv.synth.make_state_dict(0, init=init, bias=bias)
+    dec = gsv.Decoder.load(sd, device=0, mode="fp32")
+    z, g = gsv.synth.make_inputs(2, T0)
+    wav = dec.forward(z, g)
+    ref = tiny[f"{init}_T{T0}_wav"]
+    assert wav.shape == ref.shape
+    assert np.abs(wav - ref).max() <= FP32_ABS
+    assert rel_max(wav, ref) <= FP32_REL
+    dec.close()
+
+
+def test_fp32_cfg1_matches_oracle(gsv, sd_n001):
+    """The fp32 batch-1 5 s workload: z [1,192,250], N(0,0.01) weights, zero bias."""
+    dec = gsv.Decoder.load(sd_n001, device=0, mode="fp32")
+    z, g = gsv.synth.make_inputs(1, 250)
+    wav = dec.forward(z, g)
+    ref = oracle.decoder_forward(sd_n001, z, g)
+    assert wav.shape == (160000,)
+    assert np.abs(wav - ref).max() <= FP32_ABS
+    assert rel_max(wav, ref) <= FP32_REL
+    dec.close()
+
+
+def test_fp32_unit_gain_matches_oracle(gsv, dec_fp32, sd_unit):
+    z, g = gsv.synth.make_inputs(2, 40, seed_z=11, seed_g=12)
+    wav = dec_fp32.forward(z, g)
+    ref = oracle.decoder_forward(sd_unit, z, g)
+    assert np.abs(wav - ref).max() <= FP32_ABS
+    assert rel_max(wav, ref) <= FP32_REL
+
+
+def test_fp32_per_layer_taps(gsv, dec_fp32, sd_unit):
+    z, g = gsv.synth.make_inputs(1, 9, seed_z=21, seed_g=22)
+    wav, taps = dec_fp32.forward_debug(z, g)
+    rwav, rtaps = oracle.decoder_forward(sd_unit, z, g, taps=True)
+    assert len(taps) == len(rtaps) == 12
+    for i, (a, b) in enumerate(zip(taps, rtaps)):
+        assert a.shape == b.shape, i
+        assert rel_max(a, b) <= FP32_REL, i
+    assert rel_max(wav, rwav) <= FP32_REL
+
+
+def test_fp32_without_g_and_without_cond(gsv, dec_fp32, sd_unit):
+    z, g = gsv.synth.make_inputs(1, 5)
+    assert rel_max(dec_fp32.forward(z, None), oracle.decoder_forward(sd_unit, z, None)) <= FP32_REL
+    sd = gsv.synth.make_state_dict(4, init="unit", bias="rand", with_cond=False)
+    dec = gsv.Decoder.load(sd, device=0, mode="fp32")
+    assert dec.info["gin_channels"] == 0
+    a = dec.forward(z, g)
+    assert np.array_equal(a, dec.forward(z, None))
+    assert rel_max(a, oracle.decoder_forward(sd, z, None)) <= FP32_REL
+    dec.close()
+
+
+def test_fp32_length_masking(gsv, dec_fp32, sd_unit):
+    """Each utterance of a right-padded batch decodes as if it were alone."""
+    T0 = 12
+    lens = [12, 9, 1]
+    z, g = gsv.synth.make_inputs(3, T0, seed_z=31, seed_g=32)
+    wav = dec_fp32.forward(z, g, lengths=lens).reshape(3, -1)
+    for b, n in enumerate(lens):
+        ref = oracle.decoder_forward(sd_unit, z[b:b + 1, :, :n], g[b:b + 1])
+        assert rel_max(wav[b, :640 * n], ref) <= FP32_REL
+        assert not wav[b, 640 * n:].any()
+
+
+def test_fp32_chunked_equals_whole(gsv, dec_fp32):
+    T0 = 60
+    z, g = gsv.synth.make_inputs(1, T0, seed_z=41, seed_g=42)
+    whole = dec_fp32.forward(z, g)
+    halo = dec_fp32.info["receptive_halo"]
+    assert halo <= 16
+    parts = [dec_fp32.forward_chunk(z, g, a, b, halo=16) for a, b in ((0, 17), (17, 38), (38, 60))]
+    chunked = np.concatenate(parts)
+    assert chunked.shape == whole.shape
+    assert rel_max(chunked, whole) <= 1e-6
+
+
+def test_fp32_device_memory_path(gsv, dec_fp32):
+    import torch
+    z, g = gsv.synth.make_inputs(2, 8, seed_z=51, seed_g=52)
+    host = dec_fp32.forward(z, g)
+    zt = torch.from_numpy(z).cuda()
+    gt = torch.from_numpy(g).cuda()
+    dev = dec_fp32.forward_device(zt, gt)
+    torch.cuda.synchronize()
+    assert np.array_equal(dev.cpu().numpy(), host)
+
+
+def test_stage_timing_and_launch_count(gsv, dec_fp32):
+    z, g = gsv.synth.make_inputs(1, 20)
+    dec_fp32.set_stage_timing(True)
+    dec_fp32.forward(z, g)
+    t = dec_fp32.stage_times()
+    dec_fp32.set_stage_timing(False)
+    assert t["total"] > 0 and t["resblocks"] > 0 and t["upsample"] > 0
+    assert t["total"] >= t["resblocks"]
+    assert dec_fp32.launch_count() >= 30
+
+
+def test_invalid_forward_arguments(gsv, dec_fp32):
+    z, g = gsv.synth.make_inputs(1, 4)
+    with pytest.raises(gsv.GsvDecError) as e:
+        dec_fp32.forward(z[:, :, :0], g)
+    assert e.value.status == "GSV_E_INVALID_ARG"
+    with pytest.raises(gsv.GsvDecError):
+        dec_fp32.forward_chunk(z, g, 3, 2)
+
+
+def test_load_file_matches_in_memory(gsv, sd_unit, dec_fp32, tmp_path):
+    from safetensors.numpy import save_file
+    p = tmp_path / "m.safetensors"
+    save_file({k: np.ascontiguousarray(v) for k, v in sd_unit.items()}, str(p))
+    d2 = gsv.Decoder.load_file(p, device=0, mode="fp32")
+    z, g = gsv.synth.make_inputs(1, 6)
+    assert np.array_equal(d2.forward(z, g), dec_fp32.forward(z, g))
+    d2.close()

@@ -1,0 +1,76 @@
+"""Independent float64 PyTorch restatement of the reference Generator forward.
+
+Used only to cross-check the C oracle (and to generate golden fixtures): it
+shares no code with the oracle or the CUDA library.  Follows
+src/models/sovits_decoder.rs:386-458 of the reference crate, with
+torch.nn.functional conv semantics (the PyTorch semantics the reference was
+aligned to, IMPLEMENTATION.md:3).
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+RATES = (10, 8, 2, 2, 2)
+
+
+def lrelu(x, slope):
+    # Sign-bit LeakyReLU of the reference's CPU op (sovits_decoder.rs:46-53).
+    return torch.where(torch.signbit(x), x * slope, x)
+
+
+def fold(sd, p):
+    v = torch.as_tensor(np.asarray(sd[p + ".weight_v"]), dtype=torch.float64)
+    g = torch.as_tensor(np.asarray(sd[p + ".weight_g"]), dtype=torch.float64).reshape(-1, 1, 1)
+    return v / v.pow(2).sum(dim=(1, 2), keepdim=True).sqrt() * g
+
+
+def t64(sd, k):
+    return torch.as_tensor(np.asarray(sd[k]), dtype=torch.float64) if k in sd else None
+
+
+def decoder_forward(sd, z, g=None, taps=False):
+    z = torch.as_tensor(np.asarray(z), dtype=torch.float64)
+    out_taps = []
+    x = F.conv1d(z, t64(sd, "dec.conv_pre.weight"), t64(sd, "dec.conv_pre.bias"), padding=3)
+    if g is not None and "dec.cond.weight" in sd:
+        gg = torch.as_tensor(np.asarray(g), dtype=torch.float64)
+        x = x + F.conv1d(gg, t64(sd, "dec.cond.weight"), t64(sd, "dec.cond.bias"))
+    out_taps.append(x)
+    n_up = 0
+    ups = [i for i in range(10) if f"dec.ups.{i}.weight_v" in sd]
+    rbs = [r for r in range(15) if f"dec.resblocks.{r}.convs1.0.weight_v" in sd]
+    for i, u in enumerate(ups):
+        x = lrelu(x, 0.1)
+        w = fold(sd, f"dec.ups.{u}")
+        s = RATES[i] if i < 5 else 2
+        k = w.shape[2]
+        x = F.conv_transpose1d(x, w, t64(sd, f"dec.ups.{u}.bias"), stride=s, padding=(k - s) // 2)
+        out_taps.append(x)
+        acc = None
+        sel = rbs[3 * i:3 * i + 3]
+        for rr, r in enumerate(sel):
+            kk = (3, 7, 11)[r % 3]
+            xo = x
+            for j in range(3):
+                p1 = f"dec.resblocks.{r}.convs1.{j}"
+                if p1 + ".weight_v" not in sd:
+                    continue
+                d = (1, 3, 5)[j]
+                t = F.conv1d(lrelu(xo, 0.1), fold(sd, p1), t64(sd, p1 + ".bias"),
+                             padding=d * (kk - 1) // 2, dilation=d)
+                p2 = f"dec.resblocks.{r}.convs2.{j}"
+                t = F.conv1d(lrelu(t, 0.1), fold(sd, p2), t64(sd, p2 + ".bias"), padding=(kk - 1) // 2)
+                xo = xo + t
+            acc = xo if acc is None else acc + xo
+        if acc is not None:
+            x = acc / len(sel)
+            out_taps.append(x)
+    x = lrelu(x, 0.01)
+    x = F.conv1d(x, t64(sd, "dec.conv_post.weight"), t64(sd, "dec.conv_post.bias"), padding=3)
+    out_taps.append(x)
+    wav = torch.tanh(x).flatten().numpy()
+    if taps:
+        return wav, [t.numpy() for t in out_taps]
+    return wav
