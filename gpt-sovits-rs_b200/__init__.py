@@ -242,7 +242,7 @@ class Decoder:
         if z.ndim != 3 or z.shape[0] != 1:
             raise ValueError("x must be [1, C, T]")
         gg = _host_f32(g)
-        wav = np.empty((frame_end - frame_begin) * self.hop, np.float32)
+        wav = np.empty(max(1, frame_end - frame_begin) * self.hop, np.float32)
         _check(library().gsvdec_forward_chunk(self._h, _ptr(z), _ptr(gg), z.shape[2], frame_begin,
                                               frame_end, halo, _ptr(wav), MEM_HOST, None))
         return wav

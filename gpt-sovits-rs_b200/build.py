@@ -54,7 +54,7 @@ def build(verbose: bool = False) -> Path:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     newest = max(o.stat().st_mtime for o in objs)
     if not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

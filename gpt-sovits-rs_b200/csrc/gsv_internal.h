@@ -63,6 +63,7 @@ struct TapConv {
 struct TapConvGroup {
   TapConv op[kMaxGroup];
   int n;
+  int* err;  // device error word set by a kernel whose bounded wait gave up (or null)
 };
 
 // Ceil-div helper usable on host and device.

@@ -336,6 +336,7 @@ struct gsvdec {
   float* d_cond_w = nullptr;  // [C0][gin]
   float* d_cond_b = nullptr;
   float* d_post_w = nullptr;
+  int* d_err = nullptr;  // error word of the bounded device waits
   size_t w_bytes = 0;
   // workspace
   void* ws = nullptr;
@@ -490,6 +491,7 @@ struct Work {
 
 int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& name,
               const Work& wk) {
+  grp.err = h->d_err;
   cudaError_t e;
   if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
@@ -687,6 +689,17 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   return GSV_OK;
 }
 
+// A kernel whose bounded wait gave up leaves a non-zero word in d_err.
+int check_device_error(gsvdec* h) {
+  int v = 0;
+  CUDA_TRY(cudaMemcpy(&v, h->d_err, sizeof v, cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
+    return set_err(GSV_E_TIMEOUT, "a device wait gave up (code %d); results are invalid", v);
+  }
+  return GSV_OK;
+}
+
 int collect_timing(gsvdec* h, cudaStream_t st) {
   if (h->timing != 1 || h->n_ev < 3) return GSV_OK;
   CUDA_TRY(cudaStreamSynchronize(st));
@@ -804,6 +817,8 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     CUDA_TRY(cudaMalloc(&h->d_cond_b, sizeof(float) * cb.size()));
     CUDA_TRY(cudaMemcpy(h->d_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
+  CUDA_TRY(cudaMalloc(&h->d_err, sizeof(int)));
+  CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
   for (auto& e : h->ev) CUDA_TRY(cudaEventCreate(&e));
   *out = h.release();
   return GSV_OK;
@@ -818,6 +833,7 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->d_cond_w);
   cudaFree(h->d_cond_b);
   cudaFree(h->d_post_w);
+  cudaFree(h->d_err);
   cudaFree(h->ws);
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
@@ -868,7 +884,10 @@ int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengt
     CUDA_TRY(cudaMemcpyAsync(wav, w.wav + wav_skip, sizeof(float) * (size_t)wav_count,
                              mem_kind == GSV_MEM_HOST ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice, st));
   }
-  if (mem_kind == GSV_MEM_HOST || taps) CUDA_TRY(cudaStreamSynchronize(st));
+  if (mem_kind == GSV_MEM_HOST || taps) {
+    CUDA_TRY(cudaStreamSynchronize(st));
+    GSV_TRY(check_device_error(h));
+  }
   GSV_TRY(collect_timing(h, st));
   return GSV_OK;
 }

@@ -159,3 +159,82 @@ def test_load_file_matches_in_memory(gsv, sd_unit, dec_fp32, tmp_path):
     z, g = gsv.synth.make_inputs(1, 6)
     assert np.array_equal(d2.forward(z, g), dec_fp32.forward(z, g))
     d2.close()
+
+
+# ----------------------------------------------------------------- BF16 mode
+
+
+@pytest.fixture(scope="module")
+def dec_bf16(gsv, sd_unit):
+    d = gsv.Decoder.load(sd_unit, device=0, mode="bf16")
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("T0", [1, 2, 3, 7])
+def test_bf16_tiny_matches_golden(gsv, tiny, dec_bf16, T0):
+    z, g = gsv.synth.make_inputs(2, T0)
+    wav = dec_bf16.forward(z, g)
+    ref = tiny[f"unit_T{T0}_wav"]
+    assert np.isfinite(wav).all()
+    assert snr_db(wav, ref) >= BF16_SNR_DB
+
+
+def test_bf16_waveform_snr_against_oracle(gsv, dec_bf16, sd_unit):
+    z, g = gsv.synth.make_inputs(2, 100, seed_z=61, seed_g=62)
+    wav = dec_bf16.forward(z, g)
+    ref = oracle.decoder_forward(sd_unit, z, g)
+    assert snr_db(wav, ref) >= BF16_SNR_DB
+
+
+def test_bf16_n001_weights_snr(gsv, sd_n001):
+    """The benchmark's own weight distribution, 5 s utterance."""
+    dec = gsv.Decoder.load(sd_n001, device=0, mode="bf16")
+    z, g = gsv.synth.make_inputs(1, 250)
+    wav = dec.forward(z, g)
+    ref = oracle.decoder_forward(sd_n001, z, g)
+    assert snr_db(wav, ref) >= BF16_SNR_DB
+    dec.close()
+
+
+def test_bf16_per_layer_rel_l2(gsv, dec_bf16, sd_unit):
+    z, g = gsv.synth.make_inputs(1, 30, seed_z=71, seed_g=72)
+    _, taps = dec_bf16.forward_debug(z, g)
+    _, rtaps = oracle.decoder_forward(sd_unit, z, g, taps=True)
+    for i, (a, b) in enumerate(zip(taps, rtaps)):
+        assert a.shape == b.shape, i
+        assert rel_l2(a, b) <= BF16_LAYER_REL_L2, (i, rel_l2(a, b))
+
+
+def test_bf16_full_batch_against_fp32(gsv, sd_n001):
+    """The full 16 x 10 s batch: bf16 against the fp32 CUDA path (itself pinned
+    to the oracle above), per utterance SNR >= 30 dB."""
+    z, g = gsv.synth.make_inputs(16, 500)
+    d16 = gsv.Decoder.load(sd_n001, device=0, mode="bf16")
+    d32 = gsv.Decoder.load(sd_n001, device=0, mode="fp32")
+    a = d16.forward(z, g).reshape(16, -1)
+    b = d32.forward(z, g).reshape(16, -1)
+    for u in range(16):
+        assert snr_db(a[u], b[u]) >= BF16_SNR_DB, u
+    d16.close()
+    d32.close()
+
+
+def test_bf16_length_masking_is_exact(gsv, dec_bf16):
+    T0 = 40
+    lens = [40, 23, 7, 1]
+    z, g = gsv.synth.make_inputs(4, T0, seed_z=81, seed_g=82)
+    wav = dec_bf16.forward(z, g, lengths=lens).reshape(4, -1)
+    for b, n in enumerate(lens):
+        alone = dec_bf16.forward(z[b:b + 1, :, :n], g[b:b + 1])
+        assert np.array_equal(wav[b, :640 * n], alone), b
+        assert not wav[b, 640 * n:].any()
+
+
+def test_bf16_chunked_equals_whole(gsv, dec_bf16):
+    T0 = 90
+    z, g = gsv.synth.make_inputs(1, T0, seed_z=91, seed_g=92)
+    whole = dec_bf16.forward(z, g)
+    cuts = [0, 20, 51, 90]
+    parts = [dec_bf16.forward_chunk(z, g, a, b, halo=16) for a, b in zip(cuts[:-1], cuts[1:])]
+    assert np.array_equal(np.concatenate(parts), whole)
