@@ -197,13 +197,20 @@ def test_bf16_n001_weights_snr(gsv, sd_n001):
     dec.close()
 
 
-def test_bf16_per_layer_rel_l2(gsv, dec_bf16, sd_unit):
+BF16_CUMULATIVE_REL_L2 = 2e-2
+
+
+def test_bf16_stage_taps_cumulative_drift(gsv, dec_bf16, sd_unit):
+    """Stage taps of a whole bf16 forward against the fp32 oracle.  These carry
+    the drift accumulated through every earlier layer (up to 98 bf16
+    roundings before conv_post), so the bar is 2e-2; the per-layer bar of
+    1e-2 applies to layers fed the same input (test_bf16_isolated_layers)."""
     z, g = gsv.synth.make_inputs(1, 30, seed_z=71, seed_g=72)
     _, taps = dec_bf16.forward_debug(z, g)
     _, rtaps = oracle.decoder_forward(sd_unit, z, g, taps=True)
     for i, (a, b) in enumerate(zip(taps, rtaps)):
         assert a.shape == b.shape, i
-        assert rel_l2(a, b) <= BF16_LAYER_REL_L2, (i, rel_l2(a, b))
+        assert rel_l2(a, b) <= BF16_CUMULATIVE_REL_L2, (i, rel_l2(a, b))
 
 
 def test_bf16_full_batch_against_fp32(gsv, sd_n001):
