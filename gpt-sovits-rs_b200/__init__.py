@@ -37,7 +37,7 @@ EXPORTS = (
     "gsvdec_create", "gsvdec_create_from_file", "gsvdec_destroy", "gsvdec_get_info",
     "gsvdec_forward", "gsvdec_forward_chunk", "gsvdec_forward_taps", "gsvdec_set_stage_timing",
     "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
-    "gsvdec_last_error",
+    "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_last_error",
 )
 
 
@@ -93,6 +93,8 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
     lib.gsvdec_get_stage_times.argtypes = [vp, fp]
     lib.gsvdec_launch_count.argtypes = [vp, i, i, ctypes.POINTER(i)]
     lib.gsvdec_get_launch_stats.argtypes = [vp, ctypes.POINTER(_LaunchStat), i, ctypes.POINTER(i)]
+    lib.gsvdec_forward_noalloc.argtypes = [vp, vp, vp, vp, i, i, vp, vp]
+    lib.gsvdec_noalloc_scratch_bytes.restype = ctypes.c_int64
     _lib = lib
     return lib
 
@@ -234,6 +236,24 @@ class Decoder:
             None if g is None else ctypes.c_void_p(g.data_ptr()),
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
             B, T0, ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    def forward_noalloc(self, z, g=None, lengths=None, out=None, stream=None):
+        """Allocation-free forward on CUDA tensors: the layers' scratch comes from
+        the library's static device array (for callers that cannot allocate
+        device memory at call time), so only small requests fit; ``out`` must
+        then be preallocated by the caller to stay allocation-free."""
+        import torch
+        B, _, T0 = z.shape
+        assert z.is_cuda and z.dtype == torch.float32 and z.is_contiguous()
+        if out is None:
+            out = torch.empty(B * self.out_len(T0), device=z.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream(z.device).cuda_stream
+        _check(library().gsvdec_forward_noalloc(
+            self._h, ctypes.c_void_p(z.data_ptr()),
+            None if g is None else ctypes.c_void_p(g.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
+            B, T0, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(st)))
         return out
 
     def forward_chunk(self, x, g, frame_begin: int, frame_end: int, halo: int = 16) -> np.ndarray:

@@ -11,6 +11,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1078,3 +1079,90 @@ int gsvdec_launch_count(gsvdec_t* h, int B, int T0, int* count) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward (gsvdec_forward_noalloc).
+//
+// Some callers cannot allocate device memory at call time: a real-time audio
+// callback or an inference server whose device memory is carved up by its
+// own pool allocator, where a cudaMalloc would block, fragment the pool or
+// fail.  For them the forward's per-call scratch (the activation buffers
+// between layers) comes from one statically sized device array instead of the
+// handle's cudaMalloc'd workspace.  The array is a file-scope __device__
+// object, so every GPU that loads this library holds it until process exit.
+
+namespace gsv {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device`.  In host code the symbol
+// name is only a host-side stand-in, so the address is fetched once per
+// device with that device current and cached.
+int noalloc_scratch(int device, void** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return set_err(GSV_E_INVALID_ARG, "device %d out of range for the static scratch", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess)
+      return set_err(GSV_E_CUDA, "cudaGetSymbolAddress(static scratch) failed on device %d: %s",
+                     device, cudaGetErrorString(e));
+    g_noalloc_addr[device] = p;
+  }
+  *out = g_noalloc_addr[device];
+  return GSV_OK;
+}
+
+// Lays the forward's device-mode buffers out inside [base, base + cap).
+int carve_noalloc(const gsvdec* h, int B, int T0, char* base, size_t cap, Workspace& w) {
+  const size_t act = max_act_elems(h, T0) * (size_t)B;
+  const size_t eb = act_bytes(h);
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  size_t off = 0;
+  const size_t o_zin = off; off += al((size_t)B * T0 * h->in_ch * eb);
+  const size_t o_buf = off; off += 12 * al(act * eb);
+  const size_t o_bbc = off; off += al((size_t)B * h->C0 * 4);
+  const size_t o_len = off; off += al((size_t)B * 16 * 4);
+  if (off > cap)
+    return set_err(GSV_E_INVALID_ARG,
+                   "gsvdec_forward_noalloc: B=%d x T0=%d needs %zu bytes of scratch, the static "
+                   "scratch holds %zu bytes",
+                   B, T0, off, cap);
+  w = Workspace{};
+  w.zin = base + o_zin;
+  for (int i = 0; i < 12; ++i) w.buf[i] = base + o_buf + i * al(act * eb);
+  w.bias_bc = reinterpret_cast<float*>(base + o_bbc);
+  w.lens = reinterpret_cast<int*>(base + o_len);
+  return GSV_OK;
+}
+
+}  // namespace
+}  // namespace gsv
+
+extern "C" int gsvdec_forward_noalloc(gsvdec_t* h, const float* z, const float* g,
+                                      const int32_t* lengths, int B, int T0, float* wav,
+                                      void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (!z || !wav) return gsv::set_err(GSV_E_INVALID_ARG, "z and wav must not be NULL");
+  if (B <= 0 || T0 <= 0) return gsv::set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
+  {
+    const cudaError_t e = cudaSetDevice(h->device);
+    if (e != cudaSuccess) return gsv::set_err(GSV_E_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
+  }
+  void* scratch = nullptr;
+  GSV_TRY(gsv::noalloc_scratch(h->device, &scratch));
+  gsv::Workspace w;
+  GSV_TRY(gsv::carve_noalloc(h, B, T0, static_cast<char*>(scratch), gsv::kNoAllocScratchBytes, w));
+  const float* gd = (h->has_cond && g) ? g : nullptr;
+  return gsv::forward_device(h, z, T0, 0, gd, lengths, B, T0, wav, w, nullptr,
+                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t gsvdec_noalloc_scratch_bytes(void) { return (int64_t)gsv::kNoAllocScratchBytes; }

@@ -164,6 +164,30 @@ typedef struct gsvdec_launch_stat {
 } gsvdec_launch_stat;
 int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* n);
 
+/* Allocation-free forward.  No counterpart in the reference crate.
+ *
+ * For callers that cannot allocate device memory when they decode -- a
+ * real-time audio callback, or a server whose device memory is owned by its
+ * own pool allocator, where a cudaMalloc would block, fragment the pool or
+ * fail.  Same result as gsvdec_forward with GSV_MEM_DEVICE pointers
+ * (z, g, lengths and wav are device pointers on the handle's device; the
+ * call is stream-async), but the per-call scratch between layers lives in a
+ * static device array of gsvdec_noalloc_scratch_bytes() bytes (32 MiB) that
+ * every GPU loading this library holds until process exit; this call never
+ * calls cudaMalloc / cudaFree.  Requests whose buffers do not fit (about
+ * 130 frames of B*T0 in BF16 mode, 65 in FP32 mode) are rejected with
+ * GSV_E_INVALID_ARG and a message giving the bytes needed.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device made current); make that first call before any
+ * stream capture.  Every call on a device shares the one array and leaves its
+ * contents behind; nothing in it needs clearing, since each layer overwrites
+ * all of its output, but calls that overlap on the GPU (two streams, two
+ * handles on one device, two threads) race on the array and must be
+ * serialised by the caller. */
+int gsvdec_forward_noalloc(gsvdec_t* h, const float* z, const float* g, const int32_t* lengths,
+                           int B, int T0, float* wav, void* stream);
+int64_t gsvdec_noalloc_scratch_bytes(void);
+
 /* Thread-local message describing the last error on this thread. */
 const char* gsvdec_last_error(void);
 
