@@ -18,7 +18,7 @@ from typing import Mapping, Optional, Sequence
 
 import numpy as np
 
-from . import synth  # noqa: F401  (seeded weights / inputs)
+from . import shard, synth  # noqa: F401  (multi-GPU plumbing, seeded weights / inputs)
 
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "_build" / "libgsvdec.so"

@@ -1,0 +1,141 @@
+"""Multi-GPU decode: one process per GPU, torch.distributed for the plumbing.
+
+The decoder has no exchange step: utterances are independent, and inside one
+utterance an output frame depends only on a finite window of input frames
+(the receptive field, ``Decoder.info["receptive_halo"]`` frames per side).
+So work is partitioned with no collective on the data path, and the single
+collective is the gather of finished waveform pieces to the output rank:
+
+* a batch (right-padded, per-utterance lengths) is split by utterance with a
+  longest-processing-time greedy balance of the frame counts
+  (:func:`plan_utterances`), each rank decoding its share as one masked batch;
+* one long utterance is split into contiguous frame ranges
+  (:func:`plan_chunks`), each rank decoding its range plus ``halo`` input
+  frames per side, clamped at the ends, and keeping only its own samples.
+
+The gather uses ``dist.gather`` of equal-size, zero-padded pieces (NCCL over
+NVLink on GPUs, gloo on CPU); rank 0 reassembles.  There is no reference
+counterpart: the reference runs one device (src/config/mod.rs:68-80).
+"""
+from __future__ import annotations
+
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+
+def plan_utterances(lengths: Sequence[int], nranks: int) -> List[List[int]]:
+    """Utterance indices per rank, balancing the summed frame counts (LPT).
+
+    Longest first onto the least-loaded rank; ties go to the lower rank, and
+    each rank's list is returned in ascending utterance order.
+    """
+    if nranks <= 0:
+        raise ValueError("nranks must be positive")
+    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
+    load = [0] * nranks
+    out: List[List[int]] = [[] for _ in range(nranks)]
+    for i in order:
+        r = min(range(nranks), key=lambda k: (load[k], k))
+        out[r].append(i)
+        load[r] += int(lengths[i])
+    return [sorted(x) for x in out]
+
+
+def plan_chunks(T0: int, nranks: int) -> List[Tuple[int, int]]:
+    """Contiguous frame ranges [begin, end) covering [0, T0), one per rank
+    (sizes differ by at most one frame; trailing ranks may be empty when
+    T0 < nranks)."""
+    if nranks <= 0 or T0 < 0:
+        raise ValueError("bad arguments")
+    base, extra = divmod(T0, nranks)
+    out, b = [], 0
+    for r in range(nranks):
+        n = base + (1 if r < extra else 0)
+        out.append((b, b + n))
+        b += n
+    return out
+
+
+def halo_window(begin: int, end: int, T0: int, halo: int) -> Tuple[int, int]:
+    """Input frames a chunk [begin, end) decodes with: the chunk plus `halo`
+    frames each side, clamped to the utterance."""
+    return max(0, begin - halo), min(T0, end + halo)
+
+
+def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device):
+    """Gather variable-length 1-D float32 pieces to rank 0 (zero-padded to
+    `maxlen`); returns the list of trimmed numpy pieces on rank 0, else None."""
+    import torch
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    buf = torch.zeros(maxlen, dtype=torch.float32, device=device)
+    if n_valid:
+        buf[:n_valid] = piece[:n_valid]
+    sizes = torch.tensor([n_valid], dtype=torch.int64, device=device)
+    all_sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
+    dist.all_gather(all_sizes, sizes, group=group)
+    gl = [torch.zeros(maxlen, dtype=torch.float32, device=device) for _ in range(world)] if rank == 0 else None
+    dist.gather(buf, gather_list=gl, dst=0, group=group)
+    if rank != 0:
+        return None
+    return [gl[r][: int(all_sizes[r].item())].cpu().numpy() for r in range(world)]
+
+
+def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray],
+                         lengths: Sequence[int], hop: int, dist, group=None, device="cpu"):
+    """Decode a right-padded batch across the ranks of `group`.
+
+    `decode(z_b, g_b, lengths_b)` runs this rank's share (a masked batch) and
+    returns its flattened waveform [n_b * hop * T_b].  Every rank passes the
+    same z / g / lengths.  Rank 0 returns the list of per-utterance waveforms
+    (each hop * lengths[i] samples), other ranks return None.
+    """
+    import torch
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    plan = plan_utterances(lengths, world)
+    mine = plan[rank]
+    lens = [int(lengths[i]) for i in mine]
+    if mine:
+        T = max(lens)
+        zb = np.ascontiguousarray(z[mine, :, :T])
+        gb = None if g is None else np.ascontiguousarray(g[mine])
+        wav = np.asarray(decode(zb, gb, lens), np.float32).reshape(len(mine), T * hop)
+        piece = np.concatenate([wav[k, : lens[k] * hop] for k in range(len(mine))])
+    else:
+        piece = np.zeros(0, np.float32)
+    maxlen = max(sum(int(lengths[i]) for i in p) for p in plan) * hop
+    maxlen = max(maxlen, 1)
+    got = _gather_to_root(torch.from_numpy(piece).to(device), piece.size, maxlen, dist, group, device)
+    if got is None:
+        return None
+    out: List[Optional[np.ndarray]] = [None] * len(lengths)
+    for r, idx in enumerate(plan):
+        off = 0
+        for i in idx:
+            n = int(lengths[i]) * hop
+            out[i] = got[r][off:off + n]
+            off += n
+    return out
+
+
+def decode_long_chunked(decode_chunk: Callable, T0: int, hop: int, dist, group=None,
+                        device="cpu"):
+    """Decode one long utterance split in time across the ranks of `group`.
+
+    `decode_chunk(begin, end)` returns the hop * (end - begin) samples of
+    frames [begin, end) (computed with its own halo).  Rank 0 returns the
+    whole waveform, other ranks None.
+    """
+    import torch
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    chunks = plan_chunks(T0, world)
+    b, e = chunks[rank]
+    piece = np.asarray(decode_chunk(b, e), np.float32) if e > b else np.zeros(0, np.float32)
+    maxlen = max(1, max(ee - bb for bb, ee in chunks) * hop)
+    got = _gather_to_root(torch.from_numpy(piece).to(device), piece.size, maxlen, dist, group, device)
+    if got is None:
+        return None
+    return np.concatenate(got)
