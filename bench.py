@@ -183,18 +183,21 @@ def load_pkg():
 
 
 def layer_roofline(stats, mode, pk):
-    """sum(t_roof) / sum(t_meas) over every launch; t_roof per launch is the
-    sum over its reference convs of max(F / P, bytes / BW) -- grouped launches
-    carry the summed work of same-shape convs, so the max is taken per launch
-    of uniform-shape convs."""
+    """sum(t_roof) / sum(t_meas) over every launch; t_roof of a launch is the
+    sum over the reference convs it computes of max(F / P, bytes / BW), each
+    conv's F and bytes counted as if it ran alone (unfused layer I/O)."""
     p_tensor = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) * 1e12
     p_comp = p_tensor if mode == "bf16" else FP32_CORE_TFLOPS * 1e12
     bw = pk["hbm_gbs"] * 1e9
     rows, roof, meas = [], 0.0, 0.0
     for s in stats:
         t_meas = s["ms"] / 1e3
-        comp = s["flops"] / p_comp if s["kind"] in (0, 2) else 0.0
-        t_roof = max(comp, s["bytes"] / bw)
+        if s["kind"] in (0, 2):
+            t_roof = sum(max(f / p_comp, b / bw) for f, b in zip(s["conv_flops"], s["conv_bytes"]))
+            comp = s["flops"] / p_comp
+        else:
+            comp = 0.0
+            t_roof = s["bytes"] / bw
         roof += t_roof
         meas += t_meas
         rows.append({"name": s["name"], "ms": round(s["ms"], 4),
@@ -215,6 +218,8 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
+    ap.add_argument("--once", action="store_true",
+                    help="one untimed forward, then exit (a short, fixed launch list for ncu)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     ws, rank, local = dist_setup()
@@ -253,6 +258,12 @@ def main():
     zt = torch.from_numpy(z).cuda()
     gt = torch.from_numpy(g).cuda()
     out = torch.empty(B * T0 * hop, device="cuda", dtype=torch.float32)
+    if args.once:
+        dec.forward_device(zt, gt, out=out)
+        torch.cuda.synchronize()
+        log(f"one forward: {dec.launch_count()} launches, finite={bool(torch.isfinite(out).all())}")
+        dec.close()
+        return
     for _ in range(args.warmup):
         dec.forward_device(zt, gt, out=out)
     torch.cuda.synchronize()

@@ -64,7 +64,9 @@ class _Info(ctypes.Structure):
 
 class _LaunchStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 48), ("kind", ctypes.c_int), ("n_convs", ctypes.c_int),
-                ("flops", ctypes.c_double), ("bytes", ctypes.c_double), ("ms", ctypes.c_float)]
+                ("flops", ctypes.c_double), ("bytes", ctypes.c_double),
+                ("conv_flops", ctypes.c_double * 3), ("conv_bytes", ctypes.c_double * 3),
+                ("ms", ctypes.c_float)]
 
 
 _lib = None
@@ -306,7 +308,9 @@ class Decoder:
         arr = (_LaunchStat * max(1, n.value))()
         _check(library().gsvdec_get_launch_stats(self._h, arr, n.value, ctypes.byref(n)))
         return [{"name": a.name.decode(), "kind": a.kind, "n_convs": a.n_convs, "flops": a.flops,
-                 "bytes": a.bytes, "ms": a.ms} for a in arr[:n.value]]
+                 "bytes": a.bytes, "conv_flops": list(a.conv_flops)[:max(1, a.n_convs)],
+                 "conv_bytes": list(a.conv_bytes)[:max(1, a.n_convs)], "ms": a.ms}
+                for a in arr[:n.value]]
 
     def stage_times(self) -> dict:
         ms = (ctypes.c_float * 5)()

@@ -30,7 +30,7 @@
 
 namespace gsv {
 
-constexpr int kMaxSeg = 3;
+constexpr int kMaxSeg = 6;  // up to 3 convs + 3 identity (residual) segments
 constexpr int kMaxRes = 3;
 constexpr int kMaxGroup = 3;
 

@@ -286,6 +286,15 @@ struct Packer {
     for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
     return g;
   }
+  // Identity [1][C][C]: a ResBlock residual fed through the MMA (bf16 mode).
+  size_t identity(int C) {
+    const size_t off = align(1024);
+    wbytes.resize(off + (size_t)C * C * esize());
+    for (int n = 0; n < C; ++n)
+      for (int c = 0; c < C; ++c) put(off, 1, C, C, 0, n, c, n == c ? 1.0f : 0.0f);
+    return off;
+  }
+
   // Polyphase ConvTranspose1d: tap m, column n = phi*Cout + o, channel c holds
   // w[c][o][phi + m*s] (zero past the kernel).
   GemmConv convT(const HostConv& c) {
@@ -338,6 +347,7 @@ struct gsvdec {
   float* d_cond_b = nullptr;
   float* d_post_w = nullptr;
   int* d_err = nullptr;  // error word of the bounded device waits
+  std::map<int, size_t> ident_off;  // bf16: identity weights per channel width
   size_t w_bytes = 0;
   // workspace
   void* ws = nullptr;
@@ -352,6 +362,7 @@ struct gsvdec {
     std::string name;
     int kind, nconv;
     double flops, bytes;
+    double cf[3], cb[3];
   };
   // Level 2 keeps one event list per forward until the stats are read, so a
   // timed loop of forwards needs no host sync: runs[k][0] starts forward k,
@@ -461,7 +472,8 @@ TapConv make_op(const gsvdec* h, const GemmConv& g, int B, const void* x, int Li
 
 // Records the end of one kernel launch (per-launch profile, timing level 2).
 int after_launch(gsvdec* h, cudaStream_t st, const std::string& name, int kind, int nconv,
-                 double flops, double bytes) {
+                 double flops, double bytes, const double* cf = nullptr,
+                 const double* cb = nullptr) {
   h->launches++;
   if (h->timing < 2 || h->runs.empty()) return GSV_OK;
   cudaEvent_t e;
@@ -473,19 +485,28 @@ int after_launch(gsvdec* h, cudaStream_t st, const std::string& name, int kind, 
   }
   CUDA_TRY(cudaEventRecord(e, st));
   h->runs.back().push_back(e);
-  h->run_recs.back().push_back({name, kind, nconv, flops, bytes});
+  gsvdec::Rec rec{name, kind, nconv, flops, bytes, {0, 0, 0}, {0, 0, 0}};
+  for (int i = 0; i < 3 && i < nconv; ++i) {
+    rec.cf[i] = cf ? cf[i] : (i == 0 ? flops : 0.0);
+    rec.cb[i] = cb ? cb[i] : (i == 0 ? bytes : 0.0);
+  }
+  h->run_recs.back().push_back(rec);
   return GSV_OK;
 }
 
 // Algorithmic work of one reference conv inside a tap GEMM (see gsvdec.h).
 struct Work {
   double flops = 0, bytes = 0;
+  double cf[3] = {0, 0, 0}, cb[3] = {0, 0, 0};
   int nconv = 0;
   void add(const GemmConv& g, int B, int Lin, int nres, double e) {
     const int Lout = g.Lout(Lin);
-    flops += 2.0 * g.Cin * g.Cout * g.K * (double)Lin * B;
-    bytes += e * B * ((double)g.Cin * Lin + (double)g.Cout * Lout) + e * (double)g.Cin * g.Cout * g.K;
-    bytes += e * B * (double)g.Cout * Lout * nres;
+    const double f = 2.0 * g.Cin * g.Cout * g.K * (double)Lin * B;
+    const double by = e * B * ((double)g.Cin * Lin + (double)g.Cout * Lout) +
+                      e * (double)g.Cin * g.Cout * g.K + e * B * (double)g.Cout * Lout * nres;
+    if (nconv < 3) { cf[nconv] = f; cb[nconv] = by; }
+    flops += f;
+    bytes += by;
     nconv++;
   }
 };
@@ -497,13 +518,33 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
   if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
   } else {
+    // Residuals enter the tensor-core GEMM as identity-weight segments.
+    for (int i = 0; i < grp.n; ++i) {
+      TapConv& op = grp.op[i];
+      if (op.nres == 0) continue;
+      auto it = h->ident_off.find(op.Cout);
+      if (it == h->ident_off.end() || op.N != op.Cout || op.crop != 0 || op.Q != op.Lout ||
+          op.nseg + op.nres > kMaxSeg)
+        return set_err(GSV_E_UNSUPPORTED, "residual of %s cannot be folded into the GEMM", name.c_str());
+      for (int r = 0; r < op.nres; ++r) {
+        TapSeg& sg = op.seg[op.nseg++];
+        sg.x = op.res[r];
+        sg.w = static_cast<const char*>(h->d_w) + it->second;
+        sg.Lin = op.Lout;
+        sg.Cin = op.Cout;
+        sg.ntaps = 1;
+        sg.off0 = 0;
+        sg.offstep = 1;
+      }
+      op.nres = 0;
+    }
     bool tc = true;
     for (int i = 0; i < grp.n; ++i) tc = tc && tapconv_tc_supported(grp.op[i]);
     e = tc ? launch_tapconv_tc(grp, st) : cudaErrorNotSupported;
     if (!tc) return set_err(GSV_E_UNSUPPORTED, "layer geometry not supported by the tcgen05 kernel");
   }
   if (e != cudaSuccess) return set_err(GSV_E_CUDA, "tap-conv launch failed: %s", cudaGetErrorString(e));
-  return after_launch(h, st, name, 0, wk.nconv, wk.flops, wk.bytes);
+  return after_launch(h, st, name, 0, wk.nconv, wk.flops, wk.bytes, wk.cf, wk.cb);
 }
 
 int run_one(gsvdec* h, const TapConv& op, cudaStream_t st, const std::string& name,
@@ -775,6 +816,8 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
       if (pk.biases.size() != expect) return set_err(GSV_E_SHAPE, "internal bias layout error");
       pk.biases.insert(pk.biases.end(), sum.begin(), sum.end());
     }
+    if (h->dt == Dt::BF16 && !s.c2.empty() && !h->ident_off.count(s.up.Cout))
+      h->ident_off[s.up.Cout] = pk.identity(s.up.Cout);
     h->stages.push_back(std::move(s));
   }
   if (h->dt == Dt::BF16) {
@@ -1051,6 +1094,10 @@ int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* 
       s.n_convs = ref[i].nconv;
       s.flops = ref[i].flops;
       s.bytes = ref[i].bytes;
+      for (int c = 0; c < 3; ++c) {
+        s.conv_flops[c] = ref[i].cf[c];
+        s.conv_bytes[c] = ref[i].cb[c];
+      }
       s.ms = used ? (float)(ms[i] / used) : 0.0f;
       h->stats.push_back(s);
     }

@@ -1,27 +1,35 @@
 // tapconv_tc.cu -- bf16 tap GEMM on the 5th-generation tensor cores (tcgen05).
 //
-// One CTA computes a 128-row x NT-column tile of a tap GEMM (gsv_internal.h)
-// for one utterance:
-//   warp 0      TMA producer: for every (segment, tap, channel chunk) it loads
-//               the tap-shifted activation tile [128 rows x CK channels] from
-//               the time-major activation (a 3-D tensor map over (C, L, B),
-//               whose out-of-range rows read as zero = the conv zero padding)
-//               and the weight tile [NT x CK] into a STAGES-deep ring;
-//   warp 1      allocates TMEM and issues tcgen05.mma (M=128, N=NT, K=16,
-//               bf16 x bf16 -> fp32 in TMEM), committing each stage back to
-//               the producer and the finished accumulator to the epilogue;
-//   warps 2-5   epilogue: tcgen05.ld of the accumulator rows, then the fused
-//               bias / cond / residual / branch-average / LeakyReLU of
-//               gsv_epilogue.cuh, stored as bf16 in 16-byte vectors.
-// Operands are K-major with the swizzle that matches the chunk width
-// (64 ch -> 128B, 32 ch -> 64B, 16 ch -> 32B).  Every mbarrier wait is
-// bounded; a wait that gives up sets the group's error word and the CTA
-// drains and frees its TMEM instead of hanging.
+// A persistent, warp-specialised kernel.  The GEMM (gsv_internal.h) is cut
+// into tiles of 128 rows (one utterance, rows q0..q0+127) x NT columns; each
+// CTA walks the tiles t = blockIdx.x, blockIdx.x + gridDim.x, ... with
+//   warp 0     TMA producer.  Per (segment, channel chunk) it loads ONE haloed
+//              activation window [128 + span rows x CK channels] from the
+//              time-major activation (3-D tensor map over (C, L, B): rows
+//              outside [0, L) read as zero = the conv zero padding), into a
+//              SA-deep ring; every tap of the conv is then the same window read
+//              from a row-shifted shared-memory descriptor (the swizzle is a
+//              function of the absolute shared address, so a K-major swizzled
+//              operand may start at any row).  Weights are either resident
+//              (loaded once per CTA: narrow layers) or streamed per
+//              (tap, chunk) through a SB-deep ring.
+//   warp 1     allocates 2 x NT TMEM columns (two accumulators) and issues
+//              tcgen05.mma (M = 128, N = NT, K = 16, bf16 x bf16 -> fp32),
+//              alternating accumulators between tiles so the epilogue of one
+//              tile overlaps the MMAs of the next.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator, bias / cond /
+//              branch-average / LeakyReLU (gsv_epilogue.cuh), 16-byte bf16
+//              stores; then hand the accumulator back.
+// A ResBlock residual enters the MMA as one more segment with identity
+// weights (exact: bf16 x 1.0 accumulated in fp32), so the epilogue issues no
+// global loads.  Every mbarrier wait is bounded; a wait that gives up sets
+// the group's error word, stops the CTA's loops and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -35,13 +43,25 @@ namespace {
 constexpr int kM = 128;
 constexpr int kThreads = 192;
 constexpr uint32_t kWaitLimit = 1u << 25;
+constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
 
 struct alignas(64) TcParams {
-  CUtensorMap mapA[kMaxSeg];  // activation maps, one per flattened segment
-  CUtensorMap mapB[kMaxSeg];  // weight maps
+  CUtensorMap mapA[kMaxFlat];  // activation windows, one per flattened segment
+  CUtensorMap mapB[kMaxFlat];  // weights [ntaps * N][Cin], one per flattened segment
   TapConvGroup grp;
-  int seg_base[kMaxGroup];    // first flattened segment of each op
+  int seg_base[kMaxGroup];     // first flattened segment of each op
+  int seg_minoff[kMaxFlat];    // row offset of the window start (min over taps)
+  int seg_wtap0[kMaxFlat];     // resident weights: first tap tile of the segment
+  int a_stage_bytes;           // bytes per A ring stage (multiple of 1024)
+  int row_tiles;               // 128-row tiles per utterance (same for all ops)
+  int n_tiles;                 // N / NT (same for all ops)
+  int total_tiles;             // B * row_tiles * n_tiles * grp.n
+  int w_tiles;                 // resident weight tiles
+  int bias_off[kMaxGroup];     // each op's offset in the shared bias table
+  int bias_floats;             // size of the shared bias table
 };
+
+static_assert(sizeof(TcParams) <= 4096, "kernel parameter space");
 
 // ---------------------------------------------------------------- PTX helpers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -57,6 +77,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -69,10 +93,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: false after kWaitLimit polls (each poll itself may suspend).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+// Bounded wait: false after kWaitLimit polls (each poll itself may suspend),
+// or as soon as another role of the CTA has given up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
     if (mbar_try(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && *abort) return false;
+  }
   return false;
 }
 
@@ -143,7 +170,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 }
 
 // K-major shared-memory matrix descriptor (tcgen05): start address, LBO = 16 B
-// (unused by swizzled K-major), SBO = 8 rows, version 1, swizzle = row width.
+// (unused by swizzled K-major), SBO = 8 rows, version 1, base offset 0,
+// swizzle = row width.  Valid for any row-aligned start (absolute-address swizzle).
 template <int CK>
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
   constexpr uint64_t layout = CK == 64 ? 2 : (CK == 32 ? 4 : 6);  // SW128 / SW64 / SW32
@@ -159,196 +187,391 @@ __host__ __device__ constexpr uint32_t idesc_bf16() {
          ((uint32_t)(kM >> 4) << 24);
 }
 
-__device__ __forceinline__ void raise_err(int* err, int code) {
+__device__ __forceinline__ void raise_err(int* err, volatile int* abort, int code) {
+  *abort = 1;
   if (err) atomicExch(err, code);
 }
 
-// Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q: their flat
-// output indices are consecutive (see gsv_internal.h), so the residuals and
-// outputs move as two 16-byte vectors when the run is fully in range.
-__device__ __forceinline__ void epi_run16(const TapConv& op, int b, int q, int n, const float* acc) {
-  const long long total = (long long)op.Lout * op.Cout;
-  const long long e0 = (long long)q * op.N + n - op.crop;
-  if (e0 < 0 || e0 + 16 > total) {
-#pragma unroll 1
-    for (int i = 0; i < 16; ++i) epi_element<__nv_bfloat16>(op, b, q, n + i, acc[i]);
-    return;
-  }
-  const size_t base = (size_t)b * (size_t)total + (size_t)e0;
-  int t = (int)(e0 / op.Cout);
-  int c = (int)(e0 - (long long)t * op.Cout);
-  const int lim = op.len ? op.len[b] : 0x7fffffff;
+// Per-op descriptor copied to shared memory at CTA start, so the roles' inner
+// loops never index the kernel-parameter block dynamically.
+struct SmSeg {
+  int ntaps, off0, offstep, Cin, minoff, wtap0, flat, rows;
+};
+struct SmOp {
+  int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
+  const int* len;
+  const float* bias;
+  const float* bias_bc;
+  __nv_bfloat16* out_raw;
+  __nv_bfloat16* out_act;
+  float slope, div;
+  SmSeg seg[kMaxSeg];
+};
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+  uint4 o;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-  for (int g = 0; g < 2; ++g) {
-    float v[8];
-    uint32_t dead = 0;  // masked rows (t >= len[b]) stay exactly zero
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float x = acc[g * 8 + i] + op.bias[c];
-      if (op.bias_bc != nullptr) x += op.bias_bc[(size_t)b * op.Cout + c];
-      v[i] = x;
-      if (t >= lim) dead |= 1u << i;
-      if (++c == op.Cout) { c = 0; ++t; }
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = o;
+}
+
+// Register copy of one op's epilogue parameters for the tile being stored
+// (read once per tile: loads through the shared table would be repeated after
+// every global store, which may alias it).
+struct EpiArgs {
+  int total, N, crop, Cout, shift, lim;
+  const float* bias;                  // shared-memory copy of the op's bias
+  const float* __restrict__ bias_bc;  // already offset to this utterance
+  __nv_bfloat16* __restrict__ raw;    // already offset to this utterance
+  __nv_bfloat16* __restrict__ act;
+  float slope, inv_div;
+  bool has_div;
+};
+
+__device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, int b) {
+  EpiArgs a;
+  a.total = o.Lout * o.Cout;
+  a.N = o.N;
+  a.crop = o.crop;
+  a.Cout = o.Cout;
+  a.shift = o.cout_shift;
+  a.lim = o.len ? o.len[b] : 0x7fffffff;
+  a.bias = sbias + o.bias_off;
+  a.bias_bc = o.bias_bc ? o.bias_bc + (size_t)b * o.Cout : nullptr;
+  a.raw = o.out_raw ? o.out_raw + (size_t)b * a.total : nullptr;
+  a.act = o.out_act ? o.out_act + (size_t)b * a.total : nullptr;
+  a.slope = o.slope;
+  a.has_div = o.div != 1.0f;
+  a.inv_div = o.div;
+  return a;
+}
+
+// Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q (see
+// gsv_internal.h: their flat output indices e are consecutive).  32-bit
+// index math; Cout is a power of two on every Generator layer (shift path).
+__device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const float* acc) {
+  const int e0 = q * a.N + n - a.crop;
+  if (e0 >= 0 && e0 + 16 <= a.total) {
+    int t, c;
+    if (a.shift >= 0) {
+      t = e0 >> a.shift;
+      c = e0 & (a.Cout - 1);
+    } else {
+      t = e0 / a.Cout;
+      c = e0 - t * a.Cout;
     }
-    for (int r = 0; r < op.nres; ++r) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(
-          static_cast<const __nv_bfloat16*>(op.res[r]) + base + g * 8);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h[i]);
-        v[2 * i] = f.x + v[2 * i];
-        v[2 * i + 1] = f.y + v[2 * i + 1];
+    for (int g = 0; g < 2; ++g) {
+      float v[8], w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float x = acc[g * 8 + i] + a.bias[c];
+        if (a.bias_bc != nullptr) x += __ldg(a.bias_bc + c);
+        if (t >= a.lim) x = 0.0f;
+        if (a.has_div) x = x / a.inv_div;
+        v[i] = x;
+        w[i] = lrelu(x, a.slope);
+        if (++c == a.Cout) { c = 0; ++t; }
       }
+      if (a.raw) store8(a.raw + e0 + g * 8, v);
+      if (a.act) store8(a.act + e0 + g * 8, w);
     }
+  } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (dead >> i & 1u) v[i] = 0.0f;
-    if (op.div != 1.0f) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = v[i] / op.div;
-    }
-    if (op.out_raw != nullptr) {
-      uint4 o;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(op.out_raw) + base + g * 8) = o;
-    }
-    if (op.out_act != nullptr) {
-      uint4 o;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        h[i] = __floats2bfloat162_rn(lrelu(v[2 * i], op.slope), lrelu(v[2 * i + 1], op.slope));
-      *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(op.out_act) + base + g * 8) = o;
+    for (int i = 0; i < 16; ++i) {  // fully unrolled: acc[] stays in registers
+      const int e = e0 + i;
+      if (e < 0 || e >= a.total) continue;
+      const int t = e / a.Cout, c = e - t * a.Cout;
+      float x = acc[i] + a.bias[c];
+      if (a.bias_bc != nullptr) x += a.bias_bc[c];
+      if (t >= a.lim) x = 0.0f;
+      if (a.has_div) x = x / a.inv_div;
+      if (a.raw) a.raw[e] = __float2bfloat16_rn(x);
+      if (a.act) a.act[e] = __float2bfloat16_rn(lrelu(x, a.slope));
     }
   }
 }
 
-template <int CK, int NT, int STAGES>
-struct TcCfg {
-  static constexpr uint32_t kABytes = kM * CK * 2;
+template <int CK, int NT>
+struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
-  static constexpr uint32_t kStage = kABytes + kBPitch;
-  static constexpr uint32_t kTmemCols = NT <= 32 ? 32 : (NT <= 64 ? 64 : (NT <= 128 ? 128 : 256));
-  static constexpr size_t kSmem = 1024 + (size_t)STAGES * kStage + 256;
+  static constexpr uint32_t kTmemCols = 2 * NT <= 32 ? 32 : (2 * NT <= 64 ? 64 : (2 * NT <= 128 ? 128 : (2 * NT <= 256 ? 256 : 512)));
 };
 
-template <int CK, int NT, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
-  using C = TcCfg<CK, NT, STAGES>;
-  const TapConv& op = P.grp.op[blockIdx.z];
-  const int b = blockIdx.x / op.row_tiles;
-  if (b >= op.B) return;
-  const int q0 = (blockIdx.x % op.row_tiles) * kM;
-  const int n0 = blockIdx.y * NT;
-  if (n0 >= op.N) return;
+__device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
+  if (o.len == nullptr) return false;
+  int e = q0 * o.N - o.crop;
+  if (e < 0) e = 0;
+  return e / o.Cout >= o.len[b];
+}
 
+// SA: activation-window ring depth; SB: streamed weight ring depth (RES = false).
+template <int CK, int NT, bool RES, int SA, int SB>
+__global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
+  using S = TcShape<CK, NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::kStage);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
-  const uint32_t full0 = smem_u32(bars);
-  const uint32_t empty0 = smem_u32(bars + STAGES);
-  const uint32_t accum = smem_u32(bars + 2 * STAGES);
+  const uint32_t a_stage = (uint32_t)P.a_stage_bytes;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + SA * a_stage;
+  const int nbt = RES ? P.w_tiles : SB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)nbt * S::kBPitch);
+  const uint32_t a_full = smem_u32(bars);
+  const uint32_t a_empty = a_full + 8 * SA;
+  const uint32_t b_full = a_empty + 8 * SA;
+  const uint32_t b_empty = b_full + 8 * SB;
+  const uint32_t acc_full = b_empty + 8 * SB;
+  const uint32_t acc_empty = acc_full + 16;
+  const uint32_t w_full = acc_empty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SA + 2 * SB + 5);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  SmOp* ops = reinterpret_cast<SmOp*>(tmem_slot + 4);
+  float* sbias = reinterpret_cast<float*>(ops + kMaxGroup);  // every op's bias, Cout floats each
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const bool masked = op.len != nullptr && first_out_row(op, q0) >= op.len[b];
-  int iters = 0;
-  if (!masked)
-    for (int s = 0; s < op.nseg; ++s) iters += op.seg[s].ntaps * (op.seg[s].Cin / CK);
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
+  const int nops = P.grp.n;
+  if (threadIdx.x < nops) {
+    const TapConv& g = P.grp.op[threadIdx.x];
+    SmOp& o = ops[threadIdx.x];
+    o.nseg = g.nseg;
+    o.Q = g.Q;
+    o.N = g.N;
+    o.Cout = g.Cout;
+    o.Lout = g.Lout;
+    o.crop = g.crop;
+    o.cout_shift = (g.Cout & (g.Cout - 1)) == 0 ? __ffs(g.Cout) - 1 : -1;
+    o.bias_off = P.bias_off[threadIdx.x];
+    o.len = g.len;
+    o.bias = g.bias;
+    o.bias_bc = g.bias_bc;
+    o.out_raw = static_cast<__nv_bfloat16*>(g.out_raw);
+    o.out_act = static_cast<__nv_bfloat16*>(g.out_act);
+    o.slope = g.slope;
+    o.div = g.div;
+    for (int s = 0; s < g.nseg; ++s) {
+      const int f = P.seg_base[threadIdx.x] + s;
+      SmSeg& d = o.seg[s];
+      d.ntaps = g.seg[s].ntaps;
+      d.off0 = g.seg[s].off0;
+      d.offstep = g.seg[s].offstep;
+      d.Cin = g.seg[s].Cin;
+      d.minoff = P.seg_minoff[f];
+      d.wtap0 = P.seg_wtap0[f];
+      d.flat = f;
+      d.rows = kM + (d.ntaps - 1) * abs(d.offstep);
     }
-    mbar_init(accum, 1);
+  }
+  for (int o = 0; o < nops; ++o)
+    for (int c = threadIdx.x; c < P.grp.op[o].Cout; c += kThreads)
+      sbias[P.bias_off[o] + c] = P.grp.op[o].bias[c];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SA; ++s) {
+      mbar_init(a_full + 8 * s, 1);
+      mbar_init(a_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < SB; ++s) {
+      mbar_init(b_full + 8 * s, 1);
+      mbar_init(b_empty + 8 * s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(acc_full + 8 * s, 1);
+      mbar_init(acc_empty + 8 * s, 4);
+    }
+    mbar_init(w_full, 1);
+    *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+  if (warp == 1) tmem_alloc(smem_u32(tmem_slot), S::kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  int* err = P.grp.err;
+  const int row_tiles = P.row_tiles, n_tiles = P.n_tiles, total = P.total_tiles;
+  const int per_m = nops * n_tiles;
 
   if (warp == 0) {
-    if (lane == 0 && iters > 0) {
-      int it = 0;
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
       bool ok = true;
-      for (int s = 0; s < op.nseg && ok; ++s) {
-        const TapSeg& sg = op.seg[s];
-        const CUtensorMap* ma = &P.mapA[P.seg_base[blockIdx.z] + s];
-        const CUtensorMap* mb = &P.mapB[P.seg_base[blockIdx.z] + s];
-        for (int j = 0; j < sg.ntaps && ok; ++j) {
-          const int row = q0 + sg.off0 + j * sg.offstep;
-          for (int c0 = 0; c0 < sg.Cin; c0 += CK, ++it) {
-            const int st = it % STAGES;
-            const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-            if (!mbar_wait(empty0 + 8 * st, ph ^ 1u)) {
-              raise_err(P.grp.err, 1);
+      if (RES) {
+        mbar_expect_tx(w_full, (uint32_t)P.w_tiles * S::kBBytes);
+        for (int o = 0; o < nops; ++o)
+          for (int s = 0; s < ops[o].nseg; ++s) {
+            const SmSeg& d = ops[o].seg[s];
+            for (int j = 0; j < d.ntaps; ++j)
+              tma_load_2d(smem_u32(sB + (size_t)(d.wtap0 + j) * S::kBPitch), &P.mapB[d.flat], w_full,
+                          0, j * ops[o].N);
+          }
+      }
+      for (int o = 0; o < nops; ++o)
+        for (int s = 0; s < ops[o].nseg; ++s) {
+          const int f = ops[o].seg[s].flat;
+          asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.mapA[f])) : "memory");
+          if (!RES)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.mapB[f])) : "memory");
+        }
+      uint32_t ia = 0, ib = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const int mt = t / per_m, rem = t - mt * per_m;
+        const int oi = rem / n_tiles;
+        const int n0 = (rem - oi * n_tiles) * NT;
+        const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+        if (tile_masked(ops[oi], b, q0)) continue;
+        const int nseg = ops[oi].nseg, N = ops[oi].N;
+        for (int s = 0; s < nseg && ok; ++s) {
+          const SmSeg d = ops[oi].seg[s];  // register copy (the asm below clobbers memory)
+          const uint32_t wbytes = (uint32_t)d.rows * CK * 2;
+          for (int c0 = 0; c0 < d.Cin && ok; c0 += CK) {
+            const uint32_t st = ia % SA;
+            if (!mbar_wait(a_empty + 8 * st, ((ia / SA) & 1u) ^ 1u, abort)) {
+              raise_err(err, abort, 1);
               ok = false;
               break;
             }
-            const uint32_t a = smem_u32(smem + st * C::kStage);
-            mbar_expect_tx(full0 + 8 * st, C::kABytes + C::kBBytes);
-            tma_load_3d(a, ma, full0 + 8 * st, c0, row, b);
-            tma_load_2d(a + C::kABytes, mb, full0 + 8 * st, c0, j * op.N + n0);
+            mbar_expect_tx(a_full + 8 * st, wbytes);
+            tma_load_3d(smem_u32(sA + st * a_stage), &P.mapA[d.flat], a_full + 8 * st, c0,
+                        q0 + d.minoff, b);
+            ++ia;
+            if (!RES) {
+              for (int j = 0; j < d.ntaps; ++j) {
+                const uint32_t sb = ib % SB;
+                if (!mbar_wait(b_empty + 8 * sb, ((ib / SB) & 1u) ^ 1u, abort)) {
+                  raise_err(err, abort, 2);
+                  ok = false;
+                  break;
+                }
+                mbar_expect_tx(b_full + 8 * sb, S::kBBytes);
+                tma_load_2d(smem_u32(sB + sb * S::kBPitch), &P.mapB[d.flat], b_full + 8 * sb, c0,
+                            j * N + n0);
+                ++ib;
+              }
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && iters > 0) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16<NT>();
-      for (int it = 0; it < iters; ++it) {
-        const int st = it % STAGES;
-        const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-        if (!mbar_wait(full0 + 8 * st, ph)) {
-          raise_err(P.grp.err, 2);
+      bool ok = true;
+      if (RES && !mbar_wait(w_full, 0, abort)) {
+        raise_err(err, abort, 3);
+        ok = false;
+      }
+      uint32_t ia = 0, ib = 0, i = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
+        const int mt = t / per_m, rem = t - mt * per_m;
+        const int oi = rem / n_tiles;
+        const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+        const bool masked = tile_masked(ops[oi], b, q0);
+        const int nseg = ops[oi].nseg;
+        const uint32_t buf = i & 1u;
+        if (!mbar_wait(acc_empty + 8 * buf, ((i >> 1) & 1u) ^ 1u, abort)) {
+          raise_err(err, abort, 4);
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_u32(smem + st * C::kStage);
-        const uint32_t bb = a + C::kABytes;
+        if (masked) {
+          mbar_arrive(acc_full + 8 * buf);
+          continue;
+        }
+        const uint32_t d = tmem + buf * NT;
+        uint32_t accumulate = 0;
+        for (int s = 0; s < nseg && ok; ++s) {
+          const SmSeg sg = ops[oi].seg[s];  // register copy
+          for (int c0 = 0; c0 < sg.Cin && ok; c0 += CK) {
+            const uint32_t st = ia % SA;
+            if (!mbar_wait(a_full + 8 * st, (ia / SA) & 1u, abort)) {
+              raise_err(err, abort, 5);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(sA + st * a_stage) +
+                                    (uint32_t)(sg.off0 - sg.minoff) * (CK * 2);
+            const int row_step = sg.offstep * (CK * 2);
+            for (int j = 0; j < sg.ntaps; ++j) {
+              uint32_t b_base;
+              uint32_t sb = 0;
+              if (RES) {
+                b_base = smem_u32(sB + (size_t)(sg.wtap0 + j) * S::kBPitch);
+              } else {
+                sb = ib % SB;
+                if (!mbar_wait(b_full + 8 * sb, (ib / SB) & 1u, abort)) {
+                  raise_err(err, abort, 6);
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                b_base = smem_u32(sB + sb * S::kBPitch);
+              }
+              const uint32_t a_tap = a_base + (uint32_t)(j * row_step);
 #pragma unroll
-        for (int kk = 0; kk < CK / 16; ++kk)
-          mma_bf16(tmem, sdesc<CK>(a + kk * 32), sdesc<CK>(bb + kk * 32), idesc,
-                   (it | kk) != 0 ? 1u : 0u);
-        mma_commit(empty0 + 8 * st);
+              for (int kk = 0; kk < CK / 16; ++kk) {
+                mma_bf16(d, sdesc<CK>(a_tap + kk * 32), sdesc<CK>(b_base + kk * 32), idesc,
+                         accumulate);
+                accumulate = 1;
+              }
+              if (!RES) {
+                mma_commit(b_empty + 8 * sb);
+                ++ib;
+              }
+            }
+            mma_commit(a_empty + 8 * st);
+            ++ia;
+          }
+        }
+        mma_commit(acc_full + 8 * buf);  // arrives once this tile's MMAs complete
       }
-      mma_commit(accum);  // also covers an early exit: arrives once issued MMAs finish
     }
   } else {
+    // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
-    const int q = q0 + row;
-    bool have = iters > 0;
-    if (have) {
-      const bool ok = mbar_wait(accum, 0);
-      if (!ok) raise_err(P.grp.err, 3);
-      have = __all_sync(0xffffffffu, ok);
-      tc_fence_after();
-    }
-#pragma unroll 1
-    for (int c0 = 0; c0 < NT; c0 += 16) {
-      float v[16];
-      if (have) {
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint32_t i = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
+      const int mt = t / per_m, rem = t - mt * per_m;
+      const int oi = rem / n_tiles;
+      const int n0 = (rem - oi * n_tiles) * NT;
+      const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+      const SmOp& o = ops[oi];
+      const uint32_t buf = i & 1u;
+      const bool ok = mbar_wait(acc_full + 8 * buf, (i >> 1) & 1u, abort);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) raise_err(err, abort, 7);
+        break;
       }
-      if (q < op.Q && (have || iters == 0)) epi_run16(op, b, q, n0 + c0, v);
+      tc_fence_after();
+      const bool masked = tile_masked(o, b, q0);
+      const int q = q0 + row;
+      const bool live = q < o.Q;
+      const EpiArgs ea = epi_args(o, sbias, b);
+#pragma unroll 1
+      for (int c0 = 0; c0 < NT; c0 += 16) {
+        float v[16];
+        if (!masked) {
+          tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, v);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] = 0.0f;
+        }
+        if (live) epi16(ea, q, n0 + c0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::kTmemCols);
+    tmem_dealloc(tmem, S::kTmemCols);
   }
 }
 
@@ -371,11 +594,11 @@ CUtensorMapSwizzle swizzle_for(int ck) {
                   : (ck == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
-// Activation [B][Lin][Cin] bf16 as a 3-D map (Cin, Lin, B); box CK x 128 x 1.
-bool encode_act(CUtensorMap* m, const void* x, int B, int Lin, int Cin, int ck) {
+// Activation [B][Lin][Cin] bf16 as a 3-D map (Cin, Lin, B); box CK x rows x 1.
+bool encode_act(CUtensorMap* m, const void* x, int B, int Lin, int Cin, int ck, int rows) {
   cuuint64_t dims[3] = {(cuuint64_t)Cin, (cuuint64_t)Lin, (cuuint64_t)B};
   cuuint64_t strides[2] = {(cuuint64_t)Cin * 2, (cuuint64_t)Lin * Cin * 2};
-  cuuint32_t box[3] = {(cuuint32_t)ck, (cuuint32_t)kM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)ck, (cuuint32_t)rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
   return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box,
                      es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(ck),
@@ -401,22 +624,54 @@ int nt_for(int n) {
   return n % 256 == 0 ? 256 : (n % 128 == 0 ? 128 : 0);
 }
 
-template <int CK, int NT, int STAGES>
-cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
-  using C = TcCfg<CK, NT, STAGES>;
-  static_assert(C::kSmem <= 227 * 1024, "shared memory budget");
-  cudaError_t e = cudaFuncSetAttribute(tapconv_tc_kernel<CK, NT, STAGES>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
-  if (e != cudaSuccess) return e;
-  int gx = 0, gy = 0;
-  for (int i = 0; i < P.grp.n; ++i) {
-    TapConv& op = P.grp.op[i];
-    op.row_tiles = cdiv(op.Q, kM);
-    gx = max(gx, op.B * op.row_tiles);
-    gy = max(gy, op.N / NT);
+int window_rows(const TapSeg& s) { return kM + (s.ntaps - 1) * abs(s.offstep); }
+
+struct DevInfo {
+  int sms = 0;
+};
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
   }
-  if (gx == 0 || gy == 0) return cudaSuccess;
-  tapconv_tc_kernel<CK, NT, STAGES><<<dim3(gx, gy, P.grp.n), kThreads, C::kSmem, st>>>(P);
+  return cached[dev];
+}
+
+template <int CK, int NT, bool RES, int SA, int SB>
+cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
+  using S = TcShape<CK, NT>;
+  const int nbt = RES ? P.w_tiles : SB;
+  const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch +
+                      8 * (2 * SA + 2 * SB + 5) + 16 + sizeof(SmOp) * kMaxGroup +
+                      sizeof(float) * (size_t)P.bias_floats;
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
+  // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
+  int dev = 0, smem_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  const int regs_cta = ((fa.numRegs * 32 + 255) / 256 * 256) * (kThreads / 32);
+  int per_sm = std::min({smem_sm / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
+                         2048 / kThreads, (int)(512 / S::kTmemCols)});
+  per_sm = std::max(1, per_sm);
+  const int grid = std::min(P.total_tiles, sm_count() * per_sm);
+  if (grid <= 0) return cudaSuccess;
+  kern<<<grid, kThreads, smem, st>>>(P);
   return cudaGetLastError();
 }
 
@@ -425,40 +680,65 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
 bool tapconv_tc_supported(const TapConv& op) {
   if (op.nseg < 1 || op.nseg > kMaxSeg) return false;
   const int cin = op.seg[0].Cin;
-  for (int s = 0; s < op.nseg; ++s)
+  for (int s = 0; s < op.nseg; ++s) {
     if (op.seg[s].Cin != cin || op.seg[s].ntaps < 1) return false;
+    if ((op.seg[s].ntaps - 1) * abs(op.seg[s].offstep) > 256 - kM) return false;  // TMA box rows
+  }
   const int ck = ck_for(cin), nt = nt_for(op.N);
   if (!ck || !nt || op.N % nt) return false;
-  if (op.Cout % 16) return false;  // 16-element epilogue runs stay row-aligned in bytes
-  // Instantiated (CK, NT) pairs.
+  if (op.Cout % 16) return false;  // 16-element epilogue runs stay 16-byte aligned
+  if (op.nres != 0) return false;  // residuals are folded into identity segments
+  if ((long long)op.Lout * op.Cout >= (1ll << 31) || (long long)op.Q * op.N >= (1ll << 31))
+    return false;  // 32-bit per-utterance index math
   return (ck == 64 && (nt == 256 || nt == 128 || nt == 64)) || (ck == 32 && nt == 32) ||
          (ck == 16 && nt == 16);
 }
 
 cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   if (!encode_fn()) return cudaErrorNotSupported;
+  if (g.n < 1 || g.n > kMaxGroup) return cudaErrorInvalidValue;
   TcParams P;
   memset(&P, 0, sizeof P);
   P.grp = g;
-  int nseg = 0;
   const int ck = ck_for(g.op[0].seg[0].Cin), nt = nt_for(g.op[0].N);
+  int nflat = 0, wtiles = 0, max_rows = 0;
   for (int i = 0; i < g.n; ++i) {
-    const TapConv& op = g.op[i];
-    if (!tapconv_tc_supported(op) || ck_for(op.seg[0].Cin) != ck || nt_for(op.N) != nt)
+    TapConv& op = P.grp.op[i];
+    if (!tapconv_tc_supported(op) || ck_for(op.seg[0].Cin) != ck || nt_for(op.N) != nt ||
+        op.N != g.op[0].N || op.Q != g.op[0].Q || op.B != g.op[0].B)
       return cudaErrorInvalidValue;
-    P.seg_base[i] = nseg;
-    for (int s = 0; s < op.nseg; ++s, ++nseg) {
-      if (nseg >= kMaxSeg) return cudaErrorInvalidValue;
+    op.row_tiles = cdiv(op.Q, kM);
+    P.seg_base[i] = nflat;
+    for (int s = 0; s < op.nseg; ++s, ++nflat) {
+      if (nflat >= kMaxFlat) return cudaErrorInvalidValue;
       const TapSeg& sg = op.seg[s];
-      if (!encode_act(&P.mapA[nseg], sg.x, op.B, sg.Lin, sg.Cin, ck)) return cudaErrorInvalidValue;
-      if (!encode_w(&P.mapB[nseg], sg.w, sg.ntaps * op.N, sg.Cin, ck, nt)) return cudaErrorInvalidValue;
+      const int rows = window_rows(sg);
+      max_rows = std::max(max_rows, rows);
+      P.seg_minoff[nflat] = sg.offstep >= 0 ? sg.off0 : sg.off0 + (sg.ntaps - 1) * sg.offstep;
+      P.seg_wtap0[nflat] = wtiles;
+      wtiles += sg.ntaps;
+      if (!encode_act(&P.mapA[nflat], sg.x, op.B, sg.Lin, sg.Cin, ck, rows)) return cudaErrorInvalidValue;
+      if (!encode_w(&P.mapB[nflat], sg.w, sg.ntaps * op.N, sg.Cin, ck, nt)) return cudaErrorInvalidValue;
     }
   }
-  if (ck == 64 && nt == 256) return launch_cfg<64, 256, 4>(P, st);
-  if (ck == 64 && nt == 128) return launch_cfg<64, 128, 4>(P, st);
-  if (ck == 64 && nt == 64) return launch_cfg<64, 64, 4>(P, st);
-  if (ck == 32 && nt == 32) return launch_cfg<32, 32, 4>(P, st);
-  if (ck == 16 && nt == 16) return launch_cfg<16, 16, 4>(P, st);
+  int boff = 0;
+  for (int i = 0; i < g.n; ++i) {
+    P.bias_off[i] = boff;
+    boff += g.op[i].Cout;
+  }
+  P.bias_floats = boff;
+  P.row_tiles = P.grp.op[0].row_tiles;
+  P.n_tiles = g.op[0].N / nt;
+  P.total_tiles = g.op[0].B * P.row_tiles * P.n_tiles * g.n;
+  P.a_stage_bytes = (max_rows * ck * 2 + 1023) / 1024 * 1024;
+  P.w_tiles = wtiles;
+  if (P.total_tiles <= 0) return cudaSuccess;
+  // Narrow layers keep every weight tile of the launch resident in shared memory.
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, true, 4, 1>(P, st);
+  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 2, 4>(P, st);
+  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 4>(P, st);
+  if (ck == 64 && nt == 64) return launch_cfg<64, 64, false, 3, 4>(P, st);
   return cudaErrorInvalidValue;
 }
 

@@ -158,8 +158,10 @@ typedef struct gsvdec_launch_stat {
   char name[48];   /* e.g. "conv_pre", "ups2", "rb3.step1.conv1", "rb3.final" */
   int kind;        /* 0 tap-GEMM conv, 1 relayout / cond / lengths, 2 conv_post */
   int n_convs;     /* reference conv layers inside this launch */
-  double flops;
+  double flops;    /* sums over the launch's convs */
   double bytes;
+  double conv_flops[3]; /* per conv (first n_convs entries; layer rooflines are per conv) */
+  double conv_bytes[3];
   float ms;
 } gsvdec_launch_stat;
 int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* n);
