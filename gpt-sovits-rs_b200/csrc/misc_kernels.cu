@@ -65,36 +65,72 @@ __global__ void lengths_kernel(const int* __restrict__ len_in, int B, int T0, St
   }
 }
 
-// conv_post: Cout 1, so one thread per output sample; the CTA stages its
-// haloed window of x (time-major, C channels) in shared memory.
-template <typename T, int C>
-__global__ void post_kernel(const T* __restrict__ x, int L, const float* __restrict__ w, int K,
-                            int pad, float bias, const int* __restrict__ len,
-                            float* __restrict__ wav, float* __restrict__ pre) {
-  constexpr int TT = 256;
-  extern __shared__ float sx[];  // [(TT + K - 1)][C]
-  __shared__ float sw[64 * C];
-  const int b = blockIdx.y;
-  const int t0 = blockIdx.x * TT;
-  const int rows = TT + K - 1;
-  for (int i = threadIdx.x; i < K * C; i += blockDim.x) sw[i] = w[i];
-  const T* xb = x + (size_t)b * L * C;
-  for (int i = threadIdx.x; i < rows * C; i += blockDim.x) {
-    const int r = i / C, c = i % C;
-    const int t = t0 - pad + r;
-    sx[i] = (t >= 0 && t < L) ? ld_act<T>(xb, (size_t)t * C + c) : 0.0f;
-  }
-  __syncthreads();
-  const int t = t0 + threadIdx.x;
-  if (t >= L) return;
-  float s = 0.0f;
-  for (int j = 0; j < K; ++j)
+// conv_post: Cout 1, K taps over C = 16 channels.  Each thread produces 4
+// consecutive samples from the K + 3 input rows they span (rows shared with
+// neighbouring threads come from L1); weights live in shared memory.
+template <int C>
+__device__ __forceinline__ void load_row(const float* p, float* v) {
 #pragma unroll
-    for (int c = 0; c < C; ++c) s = fmaf(sx[(threadIdx.x + j) * C + c], sw[j * C + c], s);
-  s += bias;
-  const bool dead = len && t >= len[b];
-  if (pre) pre[(size_t)b * L + t] = dead ? 0.0f : s;
-  wav[(size_t)b * L + t] = dead ? 0.0f : tanhf(s);
+  for (int k = 0; k < C / 4; ++k) {
+    const float4 f = __ldg(reinterpret_cast<const float4*>(p) + k);
+    v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+  }
+}
+template <int C>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float* v) {
+#pragma unroll
+  for (int k = 0; k < C / 8; ++k) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + k);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      v[8 * k + 2 * i] = f.x;
+      v[8 * k + 2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <typename T, int C>
+__global__ void __launch_bounds__(256) post_kernel(const T* __restrict__ x, int L,
+                                                   const float* __restrict__ w, int K, int pad,
+                                                   float bias, const int* __restrict__ len,
+                                                   float* __restrict__ wav, float* __restrict__ pre) {
+  constexpr int kPer = 4;
+  __shared__ float sw[64 * C];  // [K][C]
+  for (int i = threadIdx.x; i < K * C; i += blockDim.x) sw[i] = w[i];
+  __syncthreads();
+  const int b = blockIdx.y;
+  const int t0 = (blockIdx.x * blockDim.x + threadIdx.x) * kPer;
+  if (t0 >= L) return;
+  const T* xb = x + (size_t)b * L * C;
+  float acc[kPer];
+#pragma unroll
+  for (int o = 0; o < kPer; ++o) acc[o] = bias;
+  for (int r = 0; r < K + kPer - 1; ++r) {
+    const int row = t0 - pad + r;
+    if (row < 0 || row >= L) continue;
+    float v[C];
+    load_row<C>(xb + (size_t)row * C, v);
+#pragma unroll
+    for (int o = 0; o < kPer; ++o) {
+      const int j = r - o;  // tap of output t0 + o that reads this row
+      if (j < 0 || j >= K) continue;
+      float s = 0.0f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) s = fmaf(v[c], sw[j * C + c], s);
+      acc[o] += s;
+    }
+  }
+  const int lim = len ? len[b] : L;
+#pragma unroll
+  for (int o = 0; o < kPer; ++o) {
+    const int t = t0 + o;
+    if (t >= L) break;
+    const bool dead = t >= lim;
+    if (pre) pre[(size_t)b * L + t] = dead ? 0.0f : acc[o];
+    wav[(size_t)b * L + t] = dead ? 0.0f : tanhf(acc[o]);
+  }
 }
 
 template <typename T>
@@ -146,14 +182,13 @@ cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, con
 cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, int K, int pad,
                         float bias, const int* len, float* wav, float* pre, cudaStream_t st) {
   if (K > 64 || C != 16) return cudaErrorInvalidValue;
-  const size_t smem = sizeof(float) * (size_t)(256 + K - 1) * C;
-  dim3 grid(cdiv(L, 256), B);
+  dim3 grid(cdiv(L, 256 * 4), B);
   if (dt == Dt::F32)
-    post_kernel<float, 16><<<grid, 256, smem, st>>>(static_cast<const float*>(x), L, w, K, pad,
-                                                    bias, len, wav, pre);
+    post_kernel<float, 16><<<grid, 256, 0, st>>>(static_cast<const float*>(x), L, w, K, pad, bias,
+                                                 len, wav, pre);
   else
-    post_kernel<__nv_bfloat16, 16><<<grid, 256, smem, st>>>(
-        static_cast<const __nv_bfloat16*>(x), L, w, K, pad, bias, len, wav, pre);
+    post_kernel<__nv_bfloat16, 16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), L,
+                                                         w, K, pad, bias, len, wav, pre);
   return cudaGetLastError();
 }
 

@@ -42,7 +42,11 @@ namespace {
 
 constexpr int kM = 128;
 constexpr int kThreads = 192;
-constexpr uint32_t kWaitLimit = 1u << 25;
+// Bounded waits: each poll may suspend the warp for up to kSuspendNs until the
+// barrier phase completes (so idle roles stop consuming issue slots); after
+// kWaitPolls polls (about 1.3 s) the wait gives up and reports an error.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint32_t kWaitPolls = 1u << 16;
 constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
 
 struct alignas(64) TcParams {
@@ -85,20 +89,20 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: false after kWaitLimit polls (each poll itself may suspend),
-// or as soon as another role of the CTA has given up.
+// Bounded wait: false after kWaitPolls polls, or as soon as another role of
+// the CTA has given up.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+  for (uint32_t i = 0; i < kWaitPolls; ++i) {
     if (mbar_try(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort) return false;
+    if (*abort) return false;
   }
   return false;
 }
@@ -208,6 +212,8 @@ struct SmOp {
   SmSeg seg[kMaxSeg];
 };
 
+static_assert(sizeof(SmOp) % 16 == 0, "16-byte aligned bias table after the op table");
+
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   uint4 o;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -247,49 +253,56 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   return a;
 }
 
-// Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q (see
-// gsv_internal.h: their flat output indices e are consecutive).  32-bit
-// index math; Cout is a power of two on every Generator layer (shift path).
+// Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q.  Their flat
+// output indices e0..e0+15 are consecutive (gsv_internal.h) and, since Cout
+// and e0 are multiples of 16, lie in ONE output row t at channels c..c+15:
+// one mask test, 16-byte vector bias reads from shared memory, two packed
+// bf16 stores per output.
 __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const float* acc) {
   const int e0 = q * a.N + n - a.crop;
-  if (e0 >= 0 && e0 + 16 <= a.total) {
-    int t, c;
-    if (a.shift >= 0) {
-      t = e0 >> a.shift;
-      c = e0 & (a.Cout - 1);
-    } else {
-      t = e0 / a.Cout;
-      c = e0 - t * a.Cout;
-    }
+  if (e0 < 0 || e0 >= a.total) return;  // cropped ConvTranspose rows
+  const int t = a.shift >= 0 ? e0 >> a.shift : e0 / a.Cout;
+  const int c = e0 - t * a.Cout;
+  float v[16];
+  if (t >= a.lim) {
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      float v[8], w[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float x = acc[g * 8 + i] + a.bias[c];
-        if (a.bias_bc != nullptr) x += __ldg(a.bias_bc + c);
-        if (t >= a.lim) x = 0.0f;
-        if (a.has_div) x = x / a.inv_div;
-        v[i] = x;
-        w[i] = lrelu(x, a.slope);
-        if (++c == a.Cout) { c = 0; ++t; }
-      }
-      if (a.raw) store8(a.raw + e0 + g * 8, v);
-      if (a.act) store8(a.act + e0 + g * 8, w);
-    }
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
   } else {
+    const float4* bb = reinterpret_cast<const float4*>(a.bias + c);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {  // fully unrolled: acc[] stays in registers
-      const int e = e0 + i;
-      if (e < 0 || e >= a.total) continue;
-      const int t = e / a.Cout, c = e - t * a.Cout;
-      float x = acc[i] + a.bias[c];
-      if (a.bias_bc != nullptr) x += a.bias_bc[c];
-      if (t >= a.lim) x = 0.0f;
-      if (a.has_div) x = x / a.inv_div;
-      if (a.raw) a.raw[e] = __float2bfloat16_rn(x);
-      if (a.act) a.act[e] = __float2bfloat16_rn(lrelu(x, a.slope));
+    for (int k = 0; k < 4; ++k) {
+      const float4 bv = bb[k];
+      v[4 * k + 0] = acc[4 * k + 0] + bv.x;
+      v[4 * k + 1] = acc[4 * k + 1] + bv.y;
+      v[4 * k + 2] = acc[4 * k + 2] + bv.z;
+      v[4 * k + 3] = acc[4 * k + 3] + bv.w;
     }
+    if (a.bias_bc != nullptr) {
+      const float4* gb = reinterpret_cast<const float4*>(a.bias_bc + c);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 bv = __ldg(gb + k);
+        v[4 * k + 0] += bv.x;
+        v[4 * k + 1] += bv.y;
+        v[4 * k + 2] += bv.z;
+        v[4 * k + 3] += bv.w;
+      }
+    }
+    if (a.has_div) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
+    }
+  }
+  if (a.raw) {
+    store8(a.raw + e0, v);
+    store8(a.raw + e0 + 8, v + 8);
+  }
+  if (a.act) {
+    float w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) w[i] = lrelu(v[i], a.slope);
+    store8(a.act + e0, w);
+    store8(a.act + e0 + 8, w + 8);
   }
 }
 
@@ -327,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   const uint32_t w_full = acc_empty + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SA + 2 * SB + 5);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  SmOp* ops = reinterpret_cast<SmOp*>(tmem_slot + 4);
+  SmOp* ops = reinterpret_cast<SmOp*>((reinterpret_cast<uintptr_t>(tmem_slot + 2) + 15) & ~uintptr_t(15));
   float* sbias = reinterpret_cast<float*>(ops + kMaxGroup);  // every op's bias, Cout floats each
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -648,7 +661,7 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   using S = TcShape<CK, NT>;
   const int nbt = RES ? P.w_tiles : SB;
   const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch +
-                      8 * (2 * SA + 2 * SB + 5) + 16 + sizeof(SmOp) * kMaxGroup +
+                      8 * (2 * SA + 2 * SB + 5) + 32 + sizeof(SmOp) * kMaxGroup +
                       sizeof(float) * (size_t)P.bias_floats;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB>;
@@ -737,7 +750,7 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1>(P, st);
   if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, true, 4, 1>(P, st);
   if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 2, 4>(P, st);
-  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 4>(P, st);
+  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3>(P, st);
   if (ck == 64 && nt == 64) return launch_cfg<64, 64, false, 3, 4>(P, st);
   return cudaErrorInvalidValue;
 }
