@@ -207,6 +207,66 @@ def layer_roofline(stats, mode, pk):
     return roof, meas, rows
 
 
+def run_sweep(args):
+    """Every distinct conv shape of the Generator (conv_pre, the 5 ConvTranspose,
+    the 9 (k, d) ResBlock shapes of each of the 5 widths, conv_post), fed
+    N(0,1) activations, timed on the device (CUDA events around the conv launch
+    only), reported against its own roofline."""
+    import torch
+    gsv = load_pkg()
+    pk, pk_kind = peaks()
+    B = 64 if args.batch == 16 else args.batch
+    T0 = args.frames
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    dec = gsv.Decoder.load(sd, device=0, mode=args.mode)
+    Ls = [T0]
+    for s in (10, 8, 2, 2, 2):
+        Ls.append(Ls[-1] * s)
+    shapes = [("dec.conv_pre", 192, T0)]
+    for i in range(5):
+        shapes.append((f"dec.ups.{i}", (512, 256, 128, 64, 32)[i], Ls[i]))
+        for r in range(3):
+            for j in range(3):
+                shapes.append((f"dec.resblocks.{3 * i + r}.convs1.{j}", (256, 128, 64, 32, 16)[i], Ls[i + 1]))
+    shapes.append(("dec.conv_post", 16, Ls[5]))
+    p_comp = (pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) if args.mode == "bf16"
+              else FP32_CORE_TFLOPS) * 1e12
+    bw = pk["hbm_gbs"] * 1e9
+    rows = []
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for name, cin, L in shapes:
+        x = torch.randn((B, cin, L), device="cuda", generator=gen)
+        if name == "dec.conv_post":
+            cout, lout = 1, L
+        else:
+            cout, lout = dec._layer_out(name, L)
+        y = torch.empty((B, cout, lout), device="cuda")
+        for _ in range(2):
+            dec.layer_forward_device(name, x, y)
+        dec.set_stage_timing(2)
+        for _ in range(3):
+            dec.layer_forward_device(name, x, y)
+        st = [s for s in dec.launch_stats() if s["name"] == name][0]
+        dec.set_stage_timing(0)
+        t = st["ms"] / 1e3
+        f, by = st["flops"], st["bytes"]
+        t_roof = max(f / p_comp, by / bw)
+        bound = "hbm" if by / bw >= f / p_comp else ("tensor" if args.mode == "bf16" else "fp32-core")
+        rows.append({"layer": name, "cin": cin, "cout": cout, "L_in": L, "ms": round(1e3 * t, 4),
+                     "tflops": round(f / t / 1e12, 2), "gbs": round(by / t / 1e9, 1), "bound": bound,
+                     "roof_ms": round(1e3 * t_roof, 4), "frac": round(t_roof / t, 3)})
+        log(f"{name:<28s} {cin:4d}->{cout:<4d} L={L:<7d} {1e3 * t:8.3f} ms  {f / t / 1e12:7.1f} TF/s "
+            f"{by / t / 1e9:7.0f} GB/s  {bound:<9s} frac {t_roof / t:.3f}")
+        del x, y
+        torch.cuda.empty_cache()
+    tot_roof = sum(r["roof_ms"] for r in rows)
+    tot = sum(r["ms"] for r in rows)
+    print(json.dumps({"workload": f"per-layer sweep, B={B} x {T0 / 50:g} s, {args.mode}",
+                      "peaks": pk_kind, "layers": rows, "sum_ms": tot, "sum_roof_ms": tot_roof,
+                      "frac": tot_roof / tot}), flush=True)
+    dec.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -218,6 +278,9 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
+    ap.add_argument("--sweep", action="store_true",
+                    help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
+                         "x --frames, in --mode; prints one JSON line per mode")
     ap.add_argument("--once", action="store_true",
                     help="one untimed forward, then exit (a short, fixed launch list for ncu)")
     args = ap.parse_args()
@@ -226,6 +289,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, ws, rank)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
 
     import torch

@@ -37,7 +37,8 @@ EXPORTS = (
     "gsvdec_create", "gsvdec_create_from_file", "gsvdec_destroy", "gsvdec_get_info",
     "gsvdec_forward", "gsvdec_forward_chunk", "gsvdec_forward_taps", "gsvdec_set_stage_timing",
     "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
-    "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_last_error",
+    "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_layer_forward",
+    "gsvdec_layer_names", "gsvdec_last_error",
 )
 
 
@@ -97,6 +98,9 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
     lib.gsvdec_get_launch_stats.argtypes = [vp, ctypes.POINTER(_LaunchStat), i, ctypes.POINTER(i)]
     lib.gsvdec_forward_noalloc.argtypes = [vp, vp, vp, vp, i, i, vp, vp]
     lib.gsvdec_noalloc_scratch_bytes.restype = ctypes.c_int64
+    lib.gsvdec_layer_forward.argtypes = [vp, ctypes.c_char_p, vp, i, i, vp, i, vp]
+    lib.gsvdec_layer_names.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t,
+                                       ctypes.POINTER(ctypes.c_size_t)]
     _lib = lib
     return lib
 
@@ -284,6 +288,49 @@ class Decoder:
         _check(library().gsvdec_forward_taps(self._h, _ptr(z), _ptr(gg), B, T0, _ptr(wav), ptrs,
                                              len(taps)))
         return wav, taps
+
+    def layer_names(self) -> list:
+        """dec.* prefixes of the Generator's conv layers, in forward order."""
+        n = ctypes.c_size_t()
+        _check(library().gsvdec_layer_names(self._h, None, 0, ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(n.value)
+        _check(library().gsvdec_layer_names(self._h, buf, n.value, ctypes.byref(n)))
+        return [x for x in buf.value.decode().split("\n") if x]
+
+    def layer_forward(self, name: str, x, out_len: Optional[int] = None) -> np.ndarray:
+        """One conv layer on host x [B, Cin, L] -> [B, Cout, Lout] (bias, no activation)."""
+        xx = _host_f32(x)
+        B, _, L = xx.shape
+        if name == "dec.conv_post":
+            cout, lout = 1, L
+        else:
+            cout, lout = self._layer_out(name, L)
+        y = np.empty((B, cout, lout), np.float32)
+        _check(library().gsvdec_layer_forward(self._h, name.encode(), _ptr(xx), B, L, _ptr(y),
+                                              MEM_HOST, None))
+        return y
+
+    def layer_forward_device(self, name: str, x, y, stream=None):
+        """Device-pointer variant (torch CUDA tensors, fp32, reference layout)."""
+        import torch
+        B, _, L = x.shape
+        st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+        _check(library().gsvdec_layer_forward(self._h, name.encode(), ctypes.c_void_p(x.data_ptr()),
+                                              B, L, ctypes.c_void_p(y.data_ptr()), MEM_DEVICE,
+                                              ctypes.c_void_p(st)))
+        return y
+
+    def _layer_out(self, name: str, L: int):
+        # Output width / length by the load rules (src/models/sovits_decoder.rs:146-194, 551-576).
+        if name == "dec.conv_pre":
+            return 512, L
+        if name.startswith("dec.ups."):
+            i = int(name.split(".")[2])
+            rates, kernels, chans = (10, 8, 2, 2, 2), (16, 16, 8, 2, 2), (256, 128, 64, 32, 16)
+            s, k = rates[i], kernels[i]
+            return chans[i], (L - 1) * s + k - 2 * ((k - s) // 2)
+        r = int(name.split(".")[2])
+        return (256, 128, 64, 32, 16)[r // 3], L
 
     def tap_shapes(self, B: int, T0: int):
         chans = [512, 256, 128, 64, 32, 16]

@@ -53,6 +53,7 @@ int set_err(int code, const char* fmt, ...) {
 // Host-side model, following Decoder::load (src/models/sovits_decoder.rs:231-293).
 
 struct HostConv {
+  std::string name;      // dec.* prefix of the layer
   std::vector<float> w;  // folded weight, the tensor's own layout [d0, d1, K]
   std::vector<float> b;  // bias or empty
   int d0 = 0, d1 = 0, K = 0;
@@ -117,6 +118,7 @@ int to_f32(const gsvdec_tensor* t, std::vector<float>& out) {
 // Plain conv: "<pfx>.weight" [O, I, K], optional "<pfx>.bias"; pad (K-1)/2
 // (src/models/sovits_decoder.rs:295-321, 356-383).
 int load_plain(const TensorMap& tm, const std::string& pfx, HostConv& c) {
+  c.name = pfx;
   const gsvdec_tensor* w = tm.get(pfx + ".weight");
   if (!w) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight' not found in state dict", pfx.c_str());
   if (w->ndim != 3) return set_err(GSV_E_SHAPE, "%s.weight must be 3-d", pfx.c_str());
@@ -135,6 +137,7 @@ int load_plain(const TensorMap& tm, const std::string& pfx, HostConv& c) {
 // Weight-norm conv: w = g * v / ||v||, norm over dims (1, 2) of each dim-0
 // slice, folded once at load (src/utils/weights.rs:589-614).
 int load_wn(const TensorMap& tm, const std::string& pfx, HostConv& c) {
+  c.name = pfx;
   const gsvdec_tensor* v = tm.get(pfx + ".weight_v");
   const gsvdec_tensor* g = tm.get(pfx + ".weight_g");
   if (!v) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight_v' not found in state dict", pfx.c_str());
@@ -348,6 +351,10 @@ struct gsvdec {
   float* d_post_w = nullptr;
   int* d_err = nullptr;  // error word of the bounded device waits
   std::map<int, size_t> ident_off;  // bf16: identity weights per channel width
+  std::map<std::string, GemmConv> layers;  // every tap-GEMM conv by its dec.* prefix
+  std::string layer_names;                 // newline-separated, in forward order
+  void* lws = nullptr;                     // single-layer workspace
+  size_t lws_bytes = 0;
   size_t w_bytes = 0;
   // workspace
   void* ws = nullptr;
@@ -511,6 +518,8 @@ struct Work {
   }
 };
 
+constexpr int kIdentityResidualMinC = 32;
+
 int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& name,
               const Work& wk) {
   grp.err = h->d_err;
@@ -518,10 +527,12 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
   if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
   } else {
-    // Residuals enter the tensor-core GEMM as identity-weight segments.
+    // Residuals of wide layers enter the tensor-core GEMM as identity-weight
+    // segments (no global loads in the epilogue); narrow layers read them in
+    // the epilogue instead (an extra TMA window costs more there than the MMA saves).
     for (int i = 0; i < grp.n; ++i) {
       TapConv& op = grp.op[i];
-      if (op.nres == 0) continue;
+      if (op.nres == 0 || op.Cout < kIdentityResidualMinC) continue;
       auto it = h->ident_off.find(op.Cout);
       if (it == h->ident_off.end() || op.N != op.Cout || op.crop != 0 || op.Q != op.Lout ||
           op.nseg + op.nres > kMaxSeg)
@@ -793,15 +804,27 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   h->gin = m.has_cond ? m.cond.d1 : 0;
   Packer pk{h->dt};
   h->pre = pk.conv(m.pre);
+  auto reg = [&](const std::string& n, const GemmConv& g) {
+    h->layers[n] = g;
+    h->layer_names += n + "\n";
+  };
+  reg(m.pre.name, h->pre);
   h->hop = 1;
   for (size_t i = 0; i < m.ups.size(); ++i) {
     Stage s;
     s.up = pk.convT(m.ups[i]);
+    reg(m.ups[i].name, s.up);
     h->hop *= m.ups[i].stride;
     for (size_t r = 3 * i; r < std::min(3 * i + 3, m.rbs.size()); ++r) {
       std::vector<GemmConv> a, b;
-      for (auto& c : m.rbs[r].c1) a.push_back(pk.conv(c));
-      for (auto& c : m.rbs[r].c2) b.push_back(pk.conv(c));
+      for (auto& c : m.rbs[r].c1) {
+        a.push_back(pk.conv(c));
+        reg(c.name, a.back());
+      }
+      for (auto& c : m.rbs[r].c2) {
+        b.push_back(pk.conv(c));
+        reg(c.name, b.back());
+      }
       s.c1.push_back(std::move(a));
       s.c2.push_back(std::move(b));
     }
@@ -836,6 +859,7 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     }
     if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the bf16 tcgen05 kernel");
   }
+  h->layer_names += m.post.name + "\n";
   h->post_K = m.post.K;
   h->post_pad = m.post.pad;
   h->post_C = m.post.d1;
@@ -879,6 +903,7 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->d_post_w);
   cudaFree(h->d_err);
   cudaFree(h->ws);
+  cudaFree(h->lws);
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
   for (auto& run : h->runs)
@@ -933,6 +958,84 @@ int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengt
     GSV_TRY(check_device_error(h));
   }
   GSV_TRY(collect_timing(h, st));
+  return GSV_OK;
+}
+
+// One reference conv layer on [B][Cin][L] fp32 (reference layout) -> [B][Cout][Lout]
+// fp32, through the same kernel and packed weights the forward uses: bias
+// added, no activation (conv_post: before tanh).
+int layer_impl(gsvdec* h, const char* name, const float* x, int B, int L, float* y, int mem_kind,
+               cudaStream_t st) {
+  if (!name || !x || !y) return set_err(GSV_E_INVALID_ARG, "NULL argument");
+  if (B <= 0 || L <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and L=%d must be positive", B, L);
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+    return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
+  const bool post = h->layer_names.find(std::string(name) + "\n") != std::string::npos &&
+                    !h->layers.count(name);
+  auto it = h->layers.find(name);
+  if (!post && it == h->layers.end()) return set_err(GSV_E_INVALID_ARG, "no layer named %s", name);
+  const int Cin = post ? h->post_C : it->second.Cin;
+  const int Cout = post ? 1 : it->second.Cout;
+  const int Lout = post ? L : it->second.Lout(L);
+  if (Lout <= 0) return set_err(GSV_E_INVALID_ARG, "output length %d <= 0", Lout);
+  CUDA_TRY(cudaSetDevice(h->device));
+  const size_t eb = act_bytes(h);
+  auto al = [](size_t v) { return (v + 255) / 256 * 256; };
+  const size_t nx = (size_t)B * Cin * L, ny = (size_t)B * Cout * Lout;
+  const size_t need = al(nx * 4) + al(nx * eb) + al(ny * eb) + al(ny * 4);
+  if (need > h->lws_bytes) {
+    if (h->lws) CUDA_TRY(cudaFree(h->lws));
+    h->lws = nullptr;
+    h->lws_bytes = 0;
+    CUDA_TRY(cudaMalloc(&h->lws, need));
+    h->lws_bytes = need;
+  }
+  char* p = static_cast<char*>(h->lws);
+  float* xs = reinterpret_cast<float*>(p);
+  void* xt = p + al(nx * 4);
+  void* yt = p + al(nx * 4) + al(nx * eb);
+  float* ys = reinterpret_cast<float*>(p + al(nx * 4) + al(nx * eb) + al(ny * eb));
+  const float* xd = x;
+  if (mem_kind == GSV_MEM_HOST) {
+    CUDA_TRY(cudaMemcpyAsync(xs, x, nx * 4, cudaMemcpyHostToDevice, st));
+    xd = xs;
+  }
+  h->launches = 0;
+  h->n_ev = 0;
+  if (h->timing >= 2) {
+    cudaEvent_t e;
+    if (!h->pool.empty()) {
+      e = h->pool.back();
+      h->pool.pop_back();
+    } else {
+      CUDA_TRY(cudaEventCreate(&e));
+    }
+    CUDA_TRY(cudaEventRecord(e, st));
+    h->runs.push_back({e});
+    h->run_recs.push_back({});
+  }
+  CUDA_TRY(launch_transpose_in(xd, B, Cin, L, 0, L, nullptr, xt, h->dt, st));
+  GSV_TRY(after_launch(h, st, "input_relayout", 1, 0, 0.0, (4.0 + eb) * nx));
+  float* yd = mem_kind == GSV_MEM_DEVICE ? y : ys;
+  if (post) {
+    CUDA_TRY(launch_post(xt, h->dt, B, L, Cin, h->d_post_w, h->post_K, h->post_pad, h->post_bias,
+                         nullptr, xs /* tanh output, unused */, yd, st));
+    GSV_TRY(after_launch(h, st, name, 2, 1, 2.0 * Cin * h->post_K * (double)L * B,
+                         eb * B * (double)Cin * L + 4.0 * B * (double)L + 4.0 * Cin * h->post_K));
+  } else {
+    TapConv op = make_op(h, it->second, B, xt, L);
+    op.out_raw = yt;
+    Work wk;
+    wk.add(it->second, B, L, 0, eb);
+    GSV_TRY(run_one(h, op, st, name, wk));
+    CUDA_TRY(launch_to_ncl(yt, h->dt, B, Lout, Cout, yd, st));
+    GSV_TRY(after_launch(h, st, "output_relayout", 1, 0, 0.0, (4.0 + eb) * ny));
+  }
+  if (mem_kind == GSV_MEM_HOST) {
+    CUDA_TRY(cudaMemcpyAsync(y, yd, ny * 4, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    GSV_TRY(check_device_error(h));
+  }
   return GSV_OK;
 }
 
@@ -1053,6 +1156,23 @@ int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int 
   const int64_t L = gsv::out_len(h, T0 > 0 ? T0 : 1);
   return gsv::forward_impl(h, z, g, nullptr, B, T0, 0, T0, wav, GSV_MEM_HOST, nullptr, taps, 0,
                            (int64_t)B * L);
+}
+
+int gsvdec_layer_forward(gsvdec_t* h, const char* layer, const float* x, int B, int L, float* y,
+                         int mem_kind, void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  return gsv::layer_impl(h, layer, x, B, L, y, mem_kind, static_cast<cudaStream_t>(stream));
+}
+
+int gsvdec_layer_names(const gsvdec_t* h, char* buf, size_t cap, size_t* needed) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (needed) *needed = h->layer_names.size() + 1;
+  if (buf && cap) {
+    const size_t n = std::min(cap - 1, h->layer_names.size());
+    memcpy(buf, h->layer_names.data(), n);
+    buf[n] = 0;
+  }
+  return GSV_OK;
 }
 
 int gsvdec_set_stage_timing(gsvdec_t* h, int enable) {

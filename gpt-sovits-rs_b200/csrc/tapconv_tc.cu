@@ -47,6 +47,7 @@ constexpr int kThreads = 192;
 // kWaitPolls polls (about 1.3 s) the wait gives up and reports an error.
 constexpr uint32_t kSuspendNs = 20000;
 constexpr uint32_t kWaitPolls = 1u << 16;
+constexpr uint32_t kHandoffNs = 1000;  // suspension bound on accumulator hand-offs
 constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
 
 struct alignas(64) TcParams {
@@ -85,23 +86,27 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
 
-// Bounded wait: false after kWaitPolls polls, or as soon as another role of
-// the CTA has given up.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-  for (uint32_t i = 0; i < kWaitPolls; ++i) {
-    if (mbar_try(bar, parity)) return true;
+// Bounded wait: false after about kWaitPolls * kSuspendNs, or as soon as
+// another role of the CTA has given up.  `hint_ns` bounds each poll's
+// suspension: short on the accumulator hand-offs (latency-critical), long on
+// the producer's ring waits.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint32_t hint_ns = kSuspendNs) {
+  const uint32_t polls = hint_ns >= kSuspendNs ? kWaitPolls : kWaitPolls * (kSuspendNs / (hint_ns | 1));
+  for (uint32_t i = 0; i < polls; ++i) {
+    if (mbar_try(bar, parity, hint_ns)) return true;
     if (*abort) return false;
   }
   return false;
@@ -203,6 +208,8 @@ struct SmSeg {
 };
 struct SmOp {
   int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
+  int nres, pad_[3];
+  const __nv_bfloat16* res[4];
   const int* len;
   const float* bias;
   const float* bias_bc;
@@ -226,7 +233,8 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
 // (read once per tile: loads through the shared table would be repeated after
 // every global store, which may alias it).
 struct EpiArgs {
-  int total, N, crop, Cout, shift, lim;
+  int total, N, crop, Cout, shift, lim, nres;
+  const __nv_bfloat16* res[kMaxRes];  // residuals, already offset to this utterance
   const float* bias;                  // shared-memory copy of the op's bias
   const float* __restrict__ bias_bc;  // already offset to this utterance
   __nv_bfloat16* __restrict__ raw;    // already offset to this utterance
@@ -238,6 +246,9 @@ struct EpiArgs {
 __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, int b) {
   EpiArgs a;
   a.total = o.Lout * o.Cout;
+  a.nres = o.nres;
+  for (int r = 0; r < kMaxRes; ++r)
+    a.res[r] = r < o.nres ? o.res[r] + (size_t)b * a.total : nullptr;
   a.N = o.N;
   a.crop = o.crop;
   a.Cout = o.Cout;
@@ -288,6 +299,20 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
         v[4 * k + 3] += bv.w;
       }
     }
+    for (int r = 0; r < a.nres; ++r) {  // residual runs: 16 contiguous bf16
+      const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const uint4 u = __ldg(rp + k);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = __bfloat1622float2(h2[i]);
+          v[8 * k + 2 * i] = f.x + v[8 * k + 2 * i];
+          v[8 * k + 2 * i + 1] = f.y + v[8 * k + 2 * i + 1];
+        }
+      }
+    }
     if (a.has_div) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
@@ -306,11 +331,14 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
   }
 }
 
-template <int CK, int NT>
+template <int CK, int NT, int NBUF>
 struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
-  static constexpr uint32_t kTmemCols = 2 * NT <= 32 ? 32 : (2 * NT <= 64 ? 64 : (2 * NT <= 128 ? 128 : (2 * NT <= 256 ? 256 : 512)));
+  static constexpr int kCols = NBUF * NT;  // NBUF accumulators of NT fp32 columns
+  static constexpr uint32_t kTmemCols =
+      kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
+  static_assert(kCols <= 512, "TMEM holds 512 columns");
 };
 
 __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
@@ -320,10 +348,11 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
   return e / o.Cout >= o.len[b];
 }
 
-// SA: activation-window ring depth; SB: streamed weight ring depth (RES = false).
-template <int CK, int NT, bool RES, int SA, int SB>
+// SA: activation-window ring depth; SB: streamed weight ring depth (RES = false);
+// NBUF: TMEM accumulators in flight between the MMA warp and the epilogue.
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
-  using S = TcShape<CK, NT>;
+  using S = TcShape<CK, NT, NBUF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t a_stage = (uint32_t)P.a_stage_bytes;
@@ -336,9 +365,9 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   const uint32_t b_full = a_empty + 8 * SA;
   const uint32_t b_empty = b_full + 8 * SB;
   const uint32_t acc_full = b_empty + 8 * SB;
-  const uint32_t acc_empty = acc_full + 16;
-  const uint32_t w_full = acc_empty + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SA + 2 * SB + 5);
+  const uint32_t acc_empty = acc_full + 8 * NBUF;
+  const uint32_t w_full = acc_empty + 8 * NBUF;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SA + 2 * SB + 2 * NBUF + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   SmOp* ops = reinterpret_cast<SmOp*>((reinterpret_cast<uintptr_t>(tmem_slot + 2) + 15) & ~uintptr_t(15));
   float* sbias = reinterpret_cast<float*>(ops + kMaxGroup);  // every op's bias, Cout floats each
@@ -355,6 +384,9 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     o.Lout = g.Lout;
     o.crop = g.crop;
     o.cout_shift = (g.Cout & (g.Cout - 1)) == 0 ? __ffs(g.Cout) - 1 : -1;
+    o.nres = g.nres;
+    for (int r = 0; r < kMaxRes; ++r)
+      o.res[r] = r < g.nres ? static_cast<const __nv_bfloat16*>(g.res[r]) : nullptr;
     o.bias_off = P.bias_off[threadIdx.x];
     o.len = g.len;
     o.bias = g.bias;
@@ -388,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       mbar_init(b_full + 8 * s, 1);
       mbar_init(b_empty + 8 * s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NBUF; ++s) {
       mbar_init(acc_full + 8 * s, 1);
       mbar_init(acc_empty + 8 * s, 4);
     }
@@ -482,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
         const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
         const bool masked = tile_masked(ops[oi], b, q0);
         const int nseg = ops[oi].nseg;
-        const uint32_t buf = i & 1u;
-        if (!mbar_wait(acc_empty + 8 * buf, ((i >> 1) & 1u) ^ 1u, abort)) {
+        const uint32_t buf = i % NBUF;
+        if (!mbar_wait(acc_empty + 8 * buf, ((i / NBUF) & 1u) ^ 1u, abort, kHandoffNs)) {
           raise_err(err, abort, 4);
           break;
         }
@@ -498,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           const SmSeg sg = ops[oi].seg[s];  // register copy
           for (int c0 = 0; c0 < sg.Cin && ok; c0 += CK) {
             const uint32_t st = ia % SA;
-            if (!mbar_wait(a_full + 8 * st, (ia / SA) & 1u, abort)) {
+            if (!mbar_wait(a_full + 8 * st, (ia / SA) & 1u, abort, kHandoffNs)) {
               raise_err(err, abort, 5);
               ok = false;
               break;
@@ -553,8 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const int n0 = (rem - oi * n_tiles) * NT;
       const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
       const SmOp& o = ops[oi];
-      const uint32_t buf = i & 1u;
-      const bool ok = mbar_wait(acc_full + 8 * buf, (i >> 1) & 1u, abort);
+      const uint32_t buf = i % NBUF;
+      const bool ok = mbar_wait(acc_full + 8 * buf, (i / NBUF) & 1u, abort, kHandoffNs);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) raise_err(err, abort, 7);
         break;
@@ -656,15 +688,15 @@ int sm_count() {
   return cached[dev];
 }
 
-template <int CK, int NT, bool RES, int SA, int SB>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
-  using S = TcShape<CK, NT>;
+  using S = TcShape<CK, NT, NBUF>;
   const int nbt = RES ? P.w_tiles : SB;
   const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch +
-                      8 * (2 * SA + 2 * SB + 5) + 32 + sizeof(SmOp) * kMaxGroup +
+                      8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
                       sizeof(float) * (size_t)P.bias_floats;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -700,7 +732,6 @@ bool tapconv_tc_supported(const TapConv& op) {
   const int ck = ck_for(cin), nt = nt_for(op.N);
   if (!ck || !nt || op.N % nt) return false;
   if (op.Cout % 16) return false;  // 16-element epilogue runs stay 16-byte aligned
-  if (op.nres != 0) return false;  // residuals are folded into identity segments
   if ((long long)op.Lout * op.Cout >= (1ll << 31) || (long long)op.Q * op.N >= (1ll << 31))
     return false;  // 32-bit per-utterance index math
   return (ck == 64 && (nt == 256 || nt == 128 || nt == 64)) || (ck == 32 && nt == 32) ||
@@ -747,11 +778,11 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   P.w_tiles = wtiles;
   if (P.total_tiles <= 0) return cudaSuccess;
   // Narrow layers keep every weight tile of the launch resident in shared memory.
-  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1>(P, st);
-  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, true, 4, 1>(P, st);
-  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 2, 4>(P, st);
-  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3>(P, st);
-  if (ck == 64 && nt == 64) return launch_cfg<64, 64, false, 3, 4>(P, st);
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, true, 4, 1, 4>(P, st);
+  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 2, 4, 2>(P, st);
+  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2>(P, st);
+  if (ck == 64 && nt == 64) return launch_cfg<64, 64, false, 3, 4, 4>(P, st);
   return cudaErrorInvalidValue;
 }
 

@@ -127,6 +127,25 @@ int gsvdec_forward_chunk(gsvdec_t* h, const float* z, const float* g, int T0, in
 int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int T0,
                         float* wav, float* const* taps, int n_taps);
 
+/* One conv layer of the Generator, named by its dec.* prefix ("dec.conv_pre",
+ * "dec.ups.3", "dec.resblocks.7.convs1.2", "dec.conv_post", ...; see
+ * gsvdec_layer_names), on x [B, Cin, L] -> y [B, Cout, Lout] in the
+ * reference's layout (fp32; host or device per mem_kind), through the same
+ * kernel and packed weights the forward uses: the bias is added, no
+ * activation is applied (conv_post: the value before tanh).  In BF16 mode x
+ * is rounded to bf16 first, as activations are inside the forward.  This is
+ * the per-layer tap of the reference's Conv1d/Conv1dWeightNorm::forward
+ * (src/utils/weights.rs:533-550, 646-658) and ConvTranspose upsample
+ * (src/models/sovits_decoder.rs:551-576), for per-layer parity and sweeps. */
+int gsvdec_layer_forward(gsvdec_t* h, const char* layer, const float* x, int B, int L, float* y,
+                         int mem_kind, void* stream);
+
+/* Newline-separated layer names of the handle, in forward order (conv_pre,
+ * then per stage the upsample and its resblock convs, then conv_post).
+ * Writes at most cap bytes including the terminating NUL; *needed gets the
+ * full size. */
+int gsvdec_layer_names(const gsvdec_t* h, char* buf, size_t cap, size_t* needed);
+
 /* Stage timers, the counterpart of the reference's "profile decoder
  * pre/upsample/resblocks/post" line (src/models/sovits_decoder.rs:459-468):
  * with enable = 1 the following forwards record CUDA events between stages,

@@ -245,3 +245,58 @@ def test_bf16_chunked_equals_whole(gsv, dec_bf16):
     cuts = [0, 20, 51, 90]
     parts = [dec_bf16.forward_chunk(z, g, a, b, halo=16) for a, b in zip(cuts[:-1], cuts[1:])]
     assert np.array_equal(np.concatenate(parts), whole)
+
+
+# ---------------------------------------------- isolated layers (per-layer bars)
+
+
+def _layer_ref(sd, name, x):
+    """The reference computation of one layer on x (oracle conv restatements)."""
+    if name in ("dec.conv_pre", "dec.conv_post"):
+        w = sd[name + ".weight"]
+        return oracle.conv1d(x, w, sd.get(name + ".bias"), padding=(w.shape[2] - 1) // 2)
+    w = oracle.weight_norm(sd[name + ".weight_v"], sd[name + ".weight_g"])
+    b = sd.get(name + ".bias")
+    if name.startswith("dec.ups."):
+        i = int(name.split(".")[2])
+        s = (10, 8, 2, 2, 2)[i]
+        return oracle.conv_transpose1d(x, w, b, stride=s, padding=(w.shape[2] - s) // 2)
+    parts = name.split(".")
+    r, which, j = int(parts[2]), parts[3], int(parts[4])
+    k = (3, 7, 11)[r % 3]
+    d = (1, 3, 5)[j] if which == "convs1" else 1
+    return oracle.conv1d(x, w, b, padding=d * (k - 1) // 2, dilation=d)
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+def test_every_layer_in_isolation(gsv, sd_unit, mode):
+    """Each of the 97 tap-GEMM convs and conv_post, fed the same fp32 input as
+    the oracle: FP32 within 1e-4 relative max error, BF16 within the per-layer
+    relative-L2 bar of 1e-2."""
+    dec = gsv.Decoder.load(sd_unit, device=0, mode=mode)
+    names = dec.layer_names()
+    assert len(names) == 1 + 5 + 90 + 1
+    rng = np.random.default_rng(123)
+    worst = 0.0
+    for name in names:
+        if name == "dec.conv_pre":
+            cin, L = 192, 23
+        elif name == "dec.conv_post":
+            cin, L = 16, 700
+        elif name.startswith("dec.ups."):
+            i = int(name.split(".")[2])
+            cin, L = (512, 256, 128, 64, 32)[i], (9, 41, 150, 210, 333)[i]
+        else:
+            r = int(name.split(".")[2])
+            cin, L = (256, 128, 64, 32, 16)[r // 3], (97, 130, 211, 260, 317)[r // 3]
+        x = rng.standard_normal((2, cin, L), dtype=np.float32)
+        y = dec.layer_forward(name, x)
+        ref = _layer_ref(sd_unit, name, x)
+        assert y.shape == ref.shape, name
+        if mode == "fp32":
+            assert rel_max(y, ref) <= FP32_REL, name
+        else:
+            err = rel_l2(y, ref)
+            worst = max(worst, err)
+            assert err <= BF16_LAYER_REL_L2, (name, err)
+    dec.close()
