@@ -267,6 +267,100 @@ def run_sweep(args):
     dec.close()
 
 
+def run_sharded(args, ws, rank, local):
+    """Strong-scaling workloads over torch.distributed (NCCL): every rank gets the
+    same inputs, decodes its share and the finished waveform pieces are gathered
+    to rank 0 inside the timed region; rank 0 then checks the result against a
+    single-GPU decode of the same inputs."""
+    import torch
+    import torch.distributed as dist
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    gsv = load_pkg()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    dec = gsv.Decoder.load(sd, device=local, mode=args.mode)
+    hop = dec.hop
+    group = dist.group.WORLD if ws > 1 else None
+
+    class _Solo:  # the same calls on a single process
+        @staticmethod
+        def get_rank(group=None): return 0
+        @staticmethod
+        def get_world_size(group=None): return 1
+        @staticmethod
+        def all_gather(out, t, group=None): out[0].copy_(t)
+        @staticmethod
+        def gather(t, gather_list=None, dst=0, group=None): gather_list[0].copy_(t)
+    dd = dist if ws > 1 else _Solo
+    if args.workload == "varlen256":
+        Bn, lo, hi = 256, 100, 1000
+        lens = gsv.synth.make_lengths(Bn, lo, hi)
+        z, g = gsv.synth.make_inputs(Bn, hi)
+        total_s = float(lens.sum()) * hop / SAMPLE_RATE
+
+        def step():
+            def decode(zb, gb, lb):
+                return dec.forward(zb, gb, lengths=lb)
+            return gsv.shard.decode_batch_sharded(decode, z, g, lens, hop, dd, group, device="cuda")
+        workload = f"{Bn} utterances, frames ~ U[{lo},{hi}] (2-20 s), sharded by utterance (LPT)"
+    else:
+        T0, halo = 3000, 16
+        z, g = gsv.synth.make_inputs(1, T0)
+        total_s = T0 * hop / SAMPLE_RATE
+
+        def step():
+            return gsv.shard.decode_long_chunked(
+                lambda b, e: dec.forward_chunk(z, g, b, e, halo=halo), T0, hop, dd, group, device="cuda")
+        workload = f"one 60 s utterance (z [1,192,{T0}]) in {ws} time chunks, halo {halo} frames"
+    for _ in range(args.warmup):
+        step()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        res = step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    parity = None
+    if rank == 0:
+        if args.workload == "varlen256":
+            idx = [0, int(np.argmax(lens)), int(np.argmin(lens))]
+            errs = []
+            for i in idx:
+                alone = dec.forward(z[i:i + 1, :, :lens[i]], g[i:i + 1])
+                errs.append(float(np.abs(res[i] - alone).max() / max(np.abs(alone).max(), 1e-30)))
+            parity = {"checked_utterances": idx, "max_rel_err": max(errs)}
+        else:
+            whole = dec.forward(z, g)
+            parity = {"max_rel_err": float(np.abs(res - whole).max() / max(np.abs(whole).max(), 1e-30)),
+                      "bit_exact": bool(np.array_equal(res, whole))}
+        print(json.dumps({
+            "metric": METRIC, "value": total_s * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if args.mode == "bf16" else "f32",
+            "data": "synthetic: seeded N(0,1) z/g, N(0,0.01) random-init weights, zero bias",
+            "config": {"workload": workload, "audio_seconds_per_step": total_s, "mode": args.mode,
+                       "gather": "waveform pieces to rank 0 inside the timed region (dist.gather)"},
+            "e2e": {"value": total_s * args.steps / (ms / 1e3), "unit": UNIT,
+                    "note": "host-memory API end to end (z/g from host, waveform back to host)"},
+            "parity": parity,
+        }), flush=True)
+    dec.close()
+    if ws > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -278,6 +372,10 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
+    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60"), default="batch16",
+                    help="batch16: 16 x 10 s per GPU (weak scaling, the headline); varlen256: "
+                         "256 utterances of 2-20 s sharded by utterance (strong scaling); long60: "
+                         "one 60 s utterance split in halo time chunks (strong scaling)")
     ap.add_argument("--sweep", action="store_true",
                     help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
                          "x --frames, in --mode; prints one JSON line per mode")
@@ -292,6 +390,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.workload != "batch16":
+        run_sharded(args, ws, rank, local)
         return
 
     import torch

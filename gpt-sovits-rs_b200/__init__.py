@@ -66,7 +66,7 @@ class _Info(ctypes.Structure):
 class _LaunchStat(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 48), ("kind", ctypes.c_int), ("n_convs", ctypes.c_int),
                 ("flops", ctypes.c_double), ("bytes", ctypes.c_double),
-                ("conv_flops", ctypes.c_double * 3), ("conv_bytes", ctypes.c_double * 3),
+                ("conv_flops", ctypes.c_double * 6), ("conv_bytes", ctypes.c_double * 6),
                 ("ms", ctypes.c_float)]
 
 

@@ -16,6 +16,31 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st);
 // True when the tcgen05 kernel supports this op's geometry.
 bool tapconv_tc_supported(const TapConv& op);
 
+// One fused ResBlock1 step (conv1 -> lrelu -> conv2 -> +x) per op, bf16
+// tcgen05, for C in {16, 32} (rbstep_tc.cu).  Weights packed like the tap
+// GEMM ([tap][C][C] bf16), identity [C][C] bf16.
+struct RbStepOp {
+  const void* x;      // [B][L][C] raw input
+  const void* w1;     // conv1 (dilation d)
+  const void* w2;     // conv2 (dilation 1)
+  const float* b1;
+  const float* b2;
+  void* out_raw;      // [B][L][C]
+  void* out_act;      // [B][L][C] lrelu(out), or null
+  int k, d;
+};
+struct RbStepGroup {
+  RbStepOp op[kMaxGroup];
+  int n;
+  int C, B, L;
+  const int* len;     // [B] valid rows, or null
+  float slope;        // LeakyReLU slope inside the step (0.1)
+  const void* identity;
+  int* err;
+};
+bool rbstep_supported(int C, int k, int d);
+cudaError_t launch_rbstep(const RbStepGroup& g, cudaStream_t st);
+
 // z [B][Cin][Tsrc] fp32 (NCL, the reference layout) -> zt [B][T][Cin] (time-major)
 // reading frames [t_off, t_off + T); frames t >= len[b] are written as 0.
 cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_off, int T,

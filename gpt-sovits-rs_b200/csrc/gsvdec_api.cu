@@ -369,7 +369,7 @@ struct gsvdec {
     std::string name;
     int kind, nconv;
     double flops, bytes;
-    double cf[3], cb[3];
+    double cf[6], cb[6];
   };
   // Level 2 keeps one event list per forward until the stats are read, so a
   // timed loop of forwards needs no host sync: runs[k][0] starts forward k,
@@ -492,8 +492,8 @@ int after_launch(gsvdec* h, cudaStream_t st, const std::string& name, int kind, 
   }
   CUDA_TRY(cudaEventRecord(e, st));
   h->runs.back().push_back(e);
-  gsvdec::Rec rec{name, kind, nconv, flops, bytes, {0, 0, 0}, {0, 0, 0}};
-  for (int i = 0; i < 3 && i < nconv; ++i) {
+  gsvdec::Rec rec{name, kind, nconv, flops, bytes, {0, 0, 0, 0, 0, 0}, {0, 0, 0, 0, 0, 0}};
+  for (int i = 0; i < 6 && i < nconv; ++i) {
     rec.cf[i] = cf ? cf[i] : (i == 0 ? flops : 0.0);
     rec.cb[i] = cb ? cb[i] : (i == 0 ? bytes : 0.0);
   }
@@ -504,14 +504,14 @@ int after_launch(gsvdec* h, cudaStream_t st, const std::string& name, int kind, 
 // Algorithmic work of one reference conv inside a tap GEMM (see gsvdec.h).
 struct Work {
   double flops = 0, bytes = 0;
-  double cf[3] = {0, 0, 0}, cb[3] = {0, 0, 0};
+  double cf[6] = {0, 0, 0, 0, 0, 0}, cb[6] = {0, 0, 0, 0, 0, 0};
   int nconv = 0;
   void add(const GemmConv& g, int B, int Lin, int nres, double e) {
     const int Lout = g.Lout(Lin);
     const double f = 2.0 * g.Cin * g.Cout * g.K * (double)Lin * B;
     const double by = e * B * ((double)g.Cin * Lin + (double)g.Cout * Lout) +
                       e * (double)g.Cin * g.Cout * g.K + e * B * (double)g.Cout * Lout * nres;
-    if (nconv < 3) { cf[nconv] = f; cb[nconv] = by; }
+    if (nconv < 6) { cf[nconv] = f; cb[nconv] = by; }
     flops += f;
     bytes += by;
     nconv++;
@@ -672,9 +672,56 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
       mark(h, st);
       continue;
     }
+    // Narrow stages in BF16 mode: ResBlock steps 0 and 1 run as fused
+    // conv1 -> conv2 kernels (rbstep_tc.cu); the intermediate stays on chip.
+    bool fuse = h->dt == Dt::BF16 && nb == 3 && rbstep_supported(C, 1, 1) && h->ident_off.count(C);
+    for (int r = 0; r < nb && fuse; ++r) {
+      fuse = sg.c1[r].size() == 3;
+      for (int j = 0; j < 2 && fuse; ++j)
+        fuse = rbstep_supported(C, sg.c1[r][j].ntaps, sg.c1[r][j].offstep) && sg.c1[r][j].off0 == -sg.c1[r][j].pad;
+    }
+    int first_step = 0;
+    if (fuse) {
+      for (int j = 0; j < 2; ++j) {
+        RbStepGroup rg{};
+        rg.n = nb;
+        rg.C = C;
+        rg.B = B;
+        rg.L = L;
+        rg.len = len;
+        rg.slope = 0.1f;
+        rg.identity = static_cast<const char*>(h->d_w) + h->ident_off[C];
+        rg.err = h->d_err;
+        Work wk;
+        for (int r = 0; r < nb; ++r) {
+          const GemmConv& a = sg.c1[r][j];
+          const GemmConv& c = sg.c2[r][j];
+          RbStepOp& o = rg.op[r];
+          o.x = j == 0 ? X : XR[r];
+          o.w1 = static_cast<const char*>(h->d_w) + a.w_off;
+          o.w2 = static_cast<const char*>(h->d_w) + c.w_off;
+          o.b1 = h->d_bias + a.b_off;
+          o.b2 = h->d_bias + c.b_off;
+          o.out_raw = j == 0 ? XR[r] : TT[r];
+          o.out_act = j == 0 ? nullptr : AXR[r];
+          o.k = a.ntaps;
+          o.d = a.offstep;
+          wk.add(a, B, L, 0, eb);
+          wk.add(c, B, L, 1, eb);
+        }
+        const cudaError_t e = launch_rbstep(rg, st);
+        if (e != cudaSuccess) return set_err(GSV_E_CUDA, "fused resblock step launch failed: %s", cudaGetErrorString(e));
+        GSV_TRY(after_launch(h, st, "rb" + std::to_string(i) + ".step" + std::to_string(j) + ".fused", 0,
+                             wk.nconv, wk.flops, wk.bytes, wk.cf, wk.cb));
+      }
+      // Step 2: conv1 into XR (free now) from AXR, then the fused final op reads
+      // t = XR and the raw step-1 output TT.
+      std::swap(XR, TT);  // XR[r] now names the step-1 raw output; TT[r] the free buffers
+      first_step = 2;
+    }
     int max_steps = 0;
     for (int r = 0; r < nb; ++r) max_steps = std::max(max_steps, (int)sg.c1[r].size());
-    for (int j = 0; j < max_steps; ++j) {
+    for (int j = first_step; j < max_steps; ++j) {
       TapConvGroup g1{}, g2{};
       Work w1, w2;
       for (int r = 0; r < nb; ++r) {
@@ -1214,7 +1261,7 @@ int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* 
       s.n_convs = ref[i].nconv;
       s.flops = ref[i].flops;
       s.bytes = ref[i].bytes;
-      for (int c = 0; c < 3; ++c) {
+      for (int c = 0; c < 6; ++c) {
         s.conv_flops[c] = ref[i].cf[c];
         s.conv_bytes[c] = ref[i].cb[c];
       }

@@ -1,0 +1,259 @@
+// tc_common.cuh -- PTX helpers, descriptors and tensor-map encoding shared by
+// the tcgen05 kernels (tapconv_tc.cu, rbstep_tc.cu).  Everything lives in an
+// anonymous namespace: each translation unit gets its own copy.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+namespace gsv {
+namespace {
+
+constexpr int kM = 128;  // MMA rows per tile (TMEM lanes)
+// Bounded waits: each poll may suspend the warp for up to kSuspendNs until the
+// barrier phase completes (so idle roles stop consuming issue slots); after
+// kWaitPolls polls (about 1.3 s) the wait gives up and reports an error.
+constexpr uint32_t kSuspendNs = 20000;
+constexpr uint32_t kWaitPolls = 1u << 16;
+constexpr uint32_t kHandoffNs = 1000;  // suspension bound on accumulator hand-offs
+constexpr uint32_t kSpinPolls = 1u << 26;  // bound of a spinning wait (about a second)
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false after about kWaitPolls * kSuspendNs, or as soon as
+// another role of the CTA has given up.  `hint_ns` bounds each poll's
+// suspension: short on the accumulator hand-offs (latency-critical), long on
+// the producer's ring waits.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint32_t hint_ns = kSuspendNs) {
+  const uint32_t polls = hint_ns >= kSuspendNs ? kWaitPolls : kWaitPolls * (kSuspendNs / (hint_ns | 1));
+  for (uint32_t i = 0; i < polls; ++i) {
+    if (mbar_try(bar, parity, hint_ns)) return true;
+    if (*abort) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Spinning wait for the latency-critical hand-offs between the roles of a
+// CTA (a suspended waiter wakes up to a microsecond late): non-blocking
+// polls, bounded by kSpinPolls, abandoned as soon as another role gave up.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, volatile int* abort) {
+  for (uint32_t i = 0; i < kSpinPolls; ++i) {
+    if (mbar_test(bar, parity)) return true;
+    if ((i & 4095u) == 4095u && *abort) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// K-major shared-memory matrix descriptor (tcgen05): start address, LBO = 16 B
+// (unused by swizzled K-major), SBO = 8 rows, version 1, base offset 0,
+// swizzle = row width.  Valid for any row-aligned start (absolute-address swizzle).
+template <int CK>
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+  constexpr uint64_t layout = CK == 64 ? 2 : (CK == 32 ? 4 : 6);  // SW128 / SW64 / SW32
+  constexpr uint64_t sbo = (8 * CK * 2) >> 4;
+  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (sbo << 32) | (1ull << 46) |
+         (layout << 61);
+}
+
+// Instruction descriptor: D fp32, A/B bf16, both K-major, M = 128, N = NT.
+template <int NT>
+__host__ __device__ constexpr uint32_t idesc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(NT >> 3) << 17) |
+         ((uint32_t)(kM >> 4) << 24);
+}
+
+__device__ __forceinline__ void raise_err(int* err, volatile int* abort, int code) {
+  *abort = 1;
+  if (err) atomicExch(err, code);
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+  uint4 o;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = o;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+CUtensorMapSwizzle swizzle_for(int ck) {
+  return ck == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                  : (ck == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
+// Activation [B][Lin][Cin] bf16 as a 3-D map (Cin, Lin, B); box CK x rows x 1.
+bool encode_act(CUtensorMap* m, const void* x, int B, int Lin, int Cin, int ck, int rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)Cin, (cuuint64_t)Lin, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)Cin * 2, (cuuint64_t)Lin * Cin * 2};
+  cuuint32_t box[3] = {(cuuint32_t)ck, (cuuint32_t)rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box,
+                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(ck),
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// Weights [ntaps * N][Cin] bf16 as a 2-D map; box CK x NT.
+bool encode_w(CUtensorMap* m, const void* w, int rows, int Cin, int ck, int nt) {
+  cuuint64_t dims[2] = {(cuuint64_t)Cin, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)Cin * 2};
+  cuuint32_t box[2] = {(cuuint32_t)ck, (cuuint32_t)nt};
+  cuuint32_t es[2] = {1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(w), dims, strides, box,
+                     es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_for(ck),
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+int ck_for(int cin) { return cin % 64 == 0 ? 64 : (cin == 32 ? 32 : (cin == 16 ? 16 : 0)); }
+int nt_for(int n) {
+  if (n <= 256) return (n % 16 == 0 && n >= 16) ? n : 0;
+  return n % 256 == 0 ? 256 : (n % 128 == 0 ? 128 : 0);
+}
+
+int window_rows(const TapSeg& s) { return kM + (s.ntaps - 1) * abs(s.offstep); }
+
+struct DevInfo {
+  int sms = 0;
+};
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+}  // namespace
+}  // namespace gsv

@@ -179,8 +179,8 @@ typedef struct gsvdec_launch_stat {
   int n_convs;     /* reference conv layers inside this launch */
   double flops;    /* sums over the launch's convs */
   double bytes;
-  double conv_flops[3]; /* per conv (first n_convs entries; layer rooflines are per conv) */
-  double conv_bytes[3];
+  double conv_flops[6]; /* per conv (first n_convs entries; layer rooflines are per conv) */
+  double conv_bytes[6];
   float ms;
 } gsvdec_launch_stat;
 int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* n);
