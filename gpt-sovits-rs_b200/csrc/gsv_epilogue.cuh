@@ -28,10 +28,12 @@ __device__ __forceinline__ void st_act<__nv_bfloat16>(void* p, size_t i, float v
   static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
 }
 
-// LeakyReLU with the reference's sign-bit test (src/models/sovits_decoder.rs:46-53):
-// -0.0 takes the slope branch.
+// LeakyReLU of the reference (src/models/sovits_decoder.rs:46-53: sign-bit
+// test, -0.0 takes the slope branch).  For a slope in [0, 1], max(v, v * slope)
+// is the same function bit for bit (v * slope keeps v's sign, so -0.0 maps to
+// -0.0 and a NaN stays a NaN) in two instructions instead of three.
 __device__ __forceinline__ float lrelu(float v, float slope) {
-  return signbit(v) ? v * slope : v;
+  return fmaxf(v, v * slope);
 }
 
 // Epilogue value of one output element at flat index e (already in range):

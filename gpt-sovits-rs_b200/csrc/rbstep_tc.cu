@@ -29,7 +29,7 @@ namespace gsv {
 namespace {
 
 constexpr int kRbThreads = 192;
-constexpr int kRbWindowStages = 2;
+constexpr int kRbWindowStages = 3;  // windows in flight: hides the HBM latency of the next loads
 
 struct RbOpDev {
   const __nv_bfloat16* x;
@@ -73,10 +73,6 @@ template <int C>
 __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int h) {
   const uint32_t a = base + (uint32_t)r * RbShape<C>::kRow + (uint32_t)h * 16;
   return a ^ (((a >> 7) & RbShape<C>::kSwMask) << 4);
-}
-
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
@@ -198,8 +194,8 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
       uint32_t i = 0;
       for (int t = lc; t < ntiles && ok; t += ncta, ++i) {
         const uint32_t par = i & 1u;
-        if (!mbar_wait_spin(ax_full, par, abort) ||
-            !mbar_wait_spin(acc1_empty, par ^ 1u, abort)) {
+        if (!mbar_wait_fast(ax_full, par, abort) ||
+            !mbar_wait_fast(acc1_empty, par ^ 1u, abort)) {
           raise_err(err, abort, 13);
           break;
         }
@@ -214,8 +210,8 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
           }
         }
         mma_commit(acc1_full);
-        if (!mbar_wait_spin(t_full, par, abort) ||
-            !mbar_wait_spin(acc2_empty, par ^ 1u, abort)) {
+        if (!mbar_wait_fast(t_full, par, abort) ||
+            !mbar_wait_fast(acc2_empty, par ^ 1u, abort)) {
           raise_err(err, abort, 14);
           break;
         }
@@ -251,7 +247,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
     // a(i): lrelu of window i into the conv1 operand buffer (same swizzle).
     auto transform = [&](uint32_t i) -> bool {
       const uint32_t s = i % kRbWindowStages;
-      if (!mbar_wait_spin(x_full + 8 * s, (i / kRbWindowStages) & 1u, abort)) return false;
+      if (!mbar_wait_fast(x_full + 8 * s, (i / kRbWindowStages) & 1u, abort)) return false;
       const uint32_t src = smem_u32(sX + s * P.a_stage);
       const int n16 = win_rows * S::kRow / 16;
       for (int c = tid; c < n16; c += 128)
@@ -268,7 +264,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
       const int lim = min(L, P.len ? P.len[b] : L);
       const uint32_t par = i & 1u;
       // b(i): t = lrelu(conv1 + b1) into shared memory, zero outside the utterance.
-      if (!mbar_wait_spin(acc1_full, par, abort)) {
+      if (!mbar_wait_fast(acc1_full, par, abort)) {
         ok = false;
         break;
       }
@@ -308,7 +304,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
         break;
       }
       // c(i): x + conv2 + b2 for the P output rows.
-      if (!mbar_wait_spin(acc2_full, par, abort)) {
+      if (!mbar_wait_fast(acc2_full, par, abort)) {
         ok = false;
         break;
       }

@@ -33,6 +33,10 @@ namespace gsv {
 namespace {
 
 constexpr int kThreads = 192;
+// Epilogue output paths: plain 16-byte stores, or chunks staged in shared
+// memory and written by TMA tensor stores through a 3-D (Conv1d) or 4-D
+// (ConvTranspose: output row t = s * u + v) view of the output.
+constexpr int kOutPlain = 0, kOutConv = 1, kOutConvT = 2;
 constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
 
 struct alignas(64) TcParams {
@@ -49,6 +53,12 @@ struct alignas(64) TcParams {
   int w_tiles;                 // resident weight tiles
   int bias_off[kMaxGroup];     // each op's offset in the shared bias table
   int bias_floats;             // size of the shared bias table
+  // Output tensor maps for the TMA-store epilogue: [2 * op] raw, [2 * op + 1] act.
+  CUtensorMap mapOut[2 * kMaxGroup];
+  int out_mode[kMaxGroup];     // kOutPlain / kOutConv (C, L, B) / kOutConvT (C, s, L/s, B)
+  int out_scw[kMaxGroup];      // channels per staged chunk (16 or 32)
+  int out_s[kMaxGroup];        // ConvTranspose stride (phases per GEMM row)
+  int out_pad[kMaxGroup];      // ConvTranspose crop in output rows
 };
 
 static_assert(sizeof(TcParams) <= 4096, "kernel parameter space");
@@ -60,7 +70,8 @@ struct SmSeg {
 };
 struct SmOp {
   int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
-  int nres, pad_[3];
+  int nres, out_mode, scw, stride;
+  int pad, pad_[3];
   const __nv_bfloat16* res[4];
   const int* len;
   const float* bias;
@@ -175,10 +186,106 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
   }
 }
 
-template <int CK, int NT, int NBUF>
+// Values of the 16 consecutive GEMM columns [n, n + 16) of row q (bias, cond,
+// residuals, division, row mask) computed in place in `v`; false when the run
+// falls outside the output (cropped ConvTranspose rows), which the TMA path
+// leaves to the tensor map's bounds.
+__device__ __forceinline__ bool epi16_values(const EpiArgs& a, int q, int n, float* v) {
+  const int e0 = q * a.N + n - a.crop;
+  if (e0 < 0 || e0 >= a.total) return false;
+  const int t = a.shift >= 0 ? e0 >> a.shift : e0 / a.Cout;
+  const int c = e0 - t * a.Cout;
+  if (t >= a.lim) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    return true;
+  }
+  const float4* bb = reinterpret_cast<const float4*>(a.bias + c);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float4 bv = bb[k];
+    v[4 * k + 0] += bv.x;
+    v[4 * k + 1] += bv.y;
+    v[4 * k + 2] += bv.z;
+    v[4 * k + 3] += bv.w;
+  }
+  if (a.bias_bc != nullptr) {
+    const float4* gb = reinterpret_cast<const float4*>(a.bias_bc + c);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 bv = __ldg(gb + k);
+      v[4 * k + 0] += bv.x;
+      v[4 * k + 1] += bv.y;
+      v[4 * k + 2] += bv.z;
+      v[4 * k + 3] += bv.w;
+    }
+  }
+  for (int r = 0; r < a.nres; ++r) {
+    const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const uint4 u = __ldg(rp + k);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h2[i]);
+        v[8 * k + 2 * i] = f.x + v[8 * k + 2 * i];
+        v[8 * k + 2 * i + 1] = f.y + v[8 * k + 2 * i + 1];
+      }
+    }
+  }
+  if (a.has_div) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 o;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return o;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+// Byte address of 16-byte chunk h of staging row r (rows of 2 * scw bytes,
+// swizzled like the output map: SW64 for 32-channel rows, SW32 for 16).
+__device__ __forceinline__ uint32_t stage_addr(uint32_t base, int r, int h, int scw) {
+  const uint32_t a = base + (uint32_t)(r * scw * 2 + h * 16);
+  return a ^ (((a >> 7) & (scw == 32 ? 3u : 1u)) << 4);
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+template <int CK, int NT, int NBUF, bool STG>
 struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
+  // TMA-store staging: per epilogue warp, 32 rows x 32 channels bf16 for each
+  // of the two outputs (raw, act).
+  static constexpr uint32_t kStageOut = 32 * 32 * 2;
+  static constexpr uint32_t kStageWarp = 2 * kStageOut;
+  static constexpr uint32_t kStageBytes = STG ? 4 * kStageWarp : 0;
   static constexpr int kCols = NBUF * NT;  // NBUF accumulators of NT fp32 columns
   static constexpr uint32_t kTmemCols =
       kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
@@ -193,17 +300,19 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 }
 
 // SA: activation-window ring depth; SB: streamed weight ring depth (RES = false);
-// NBUF: TMEM accumulators in flight between the MMA warp and the epilogue.
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF>
+// NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
+// STG: outputs leave through shared-memory staging and TMA tensor stores.
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
-  using S = TcShape<CK, NT, NBUF>;
+  using S = TcShape<CK, NT, NBUF, STG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t a_stage = (uint32_t)P.a_stage_bytes;
   uint8_t* sA = smem;
   uint8_t* sB = smem + SA * a_stage;
   const int nbt = RES ? P.w_tiles : SB;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)nbt * S::kBPitch);
+  uint8_t* sStage = sB + (size_t)nbt * S::kBPitch;  // 1024-byte aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + S::kStageBytes);
   const uint32_t a_full = smem_u32(bars);
   const uint32_t a_empty = a_full + 8 * SA;
   const uint32_t b_full = a_empty + 8 * SA;
@@ -229,6 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     o.crop = g.crop;
     o.cout_shift = (g.Cout & (g.Cout - 1)) == 0 ? __ffs(g.Cout) - 1 : -1;
     o.nres = g.nres;
+    o.out_mode = P.out_mode[threadIdx.x];
+    o.scw = P.out_scw[threadIdx.x];
+    o.stride = P.out_s[threadIdx.x];
+    o.pad = P.out_pad[threadIdx.x];
     for (int r = 0; r < kMaxRes; ++r)
       o.res[r] = r < g.nres ? static_cast<const __nv_bfloat16*>(g.res[r]) : nullptr;
     o.bias_off = P.bias_off[threadIdx.x];
@@ -359,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
         const bool masked = tile_masked(ops[oi], b, q0);
         const int nseg = ops[oi].nseg;
         const uint32_t buf = i % NBUF;
-        if (!mbar_wait_spin(acc_empty + 8 * buf, ((i / NBUF) & 1u) ^ 1u, abort)) {
+        if (!mbar_wait_fast(acc_empty + 8 * buf, ((i / NBUF) & 1u) ^ 1u, abort)) {
           raise_err(err, abort, 4);
           break;
         }
@@ -374,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           const SmSeg sg = ops[oi].seg[s];  // register copy
           for (int c0 = 0; c0 < sg.Cin && ok; c0 += CK) {
             const uint32_t st = ia % SA;
-            if (!mbar_wait_spin(a_full + 8 * st, (ia / SA) & 1u, abort)) {
+            if (!mbar_wait_fast(a_full + 8 * st, (ia / SA) & 1u, abort)) {
               raise_err(err, abort, 5);
               ok = false;
               break;
@@ -390,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
                 b_base = smem_u32(sB + (size_t)(sg.wtap0 + j) * S::kBPitch);
               } else {
                 sb = ib % SB;
-                if (!mbar_wait_spin(b_full + 8 * sb, (ib / SB) & 1u, abort)) {
+                if (!mbar_wait_fast(b_full + 8 * sb, (ib / SB) & 1u, abort)) {
                   raise_err(err, abort, 6);
                   ok = false;
                   break;
@@ -422,6 +535,9 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t stg_raw = smem_u32(sStage) + (uint32_t)quarter * S::kStageWarp;
+    const uint32_t stg_act = stg_raw + S::kStageOut;
+    bool pending = false;  // a TMA store of this warp may still be reading its staging
     uint32_t i = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
       const int mt = t / per_m, rem = t - mt * per_m;
@@ -430,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
       const SmOp& o = ops[oi];
       const uint32_t buf = i % NBUF;
-      const bool ok = mbar_wait_spin(acc_full + 8 * buf, (i / NBUF) & 1u, abort);
+      const bool ok = mbar_wait_fast(acc_full + 8 * buf, (i / NBUF) & 1u, abort);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) raise_err(err, abort, 7);
         break;
@@ -440,21 +556,77 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const int q = q0 + row;
       const bool live = q < o.Q;
       const EpiArgs ea = epi_args(o, sbias, b);
+      const int mode = STG ? o.out_mode : kOutPlain, scw = STG ? o.scw : 16;
 #pragma unroll 1
-      for (int c0 = 0; c0 < NT; c0 += 16) {
-        float v[16];
-        if (!masked) {
-          tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, v);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] = 0.0f;
+      for (int cc = 0; cc < NT; cc += scw) {
+        // Destination of this warp's chunk: rows q0 + 32 * quarter .. + 31,
+        // GEMM columns n0 + cc .. + scw - 1.
+        bool tma = mode != kOutPlain;
+        int oc = n0 + cc, ov = 0, ou = q0 + quarter * 32;
+        if (mode == kOutConvT) {
+          const int p = oc / o.Cout;  // phase: output row t = s * q - pad + p
+          oc -= p * o.Cout;
+          const int vv = p - o.pad;
+          const int du = vv >= 0 ? vv / o.stride : -((o.stride - 1 - vv) / o.stride);
+          ov = vv - du * o.stride;
+          ou += du;
+          tma = ou >= 0;  // a store never starts at a negative row: plain stores there
         }
-        if (live) epi16(ea, q, n0 + c0, v);
+        if (tma && pending) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+          pending = false;
+        }
+#pragma unroll 1
+        for (int c0 = cc; c0 < cc + scw; c0 += 16) {
+          float v[16];
+          if (!masked) {
+            tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, v);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) v[k] = 0.0f;
+          }
+          if (!tma) {
+            if (live) epi16(ea, q, n0 + c0, v);
+            continue;
+          }
+          // Rows outside the output are clipped by the tensor map.
+          epi16_values(ea, q, n0 + c0, v);
+          const int h = (c0 - cc) / 8;
+          if (ea.raw) {
+            sts128(stage_addr(stg_raw, lane, h, scw), pack8(v));
+            sts128(stage_addr(stg_raw, lane, h + 1, scw), pack8(v + 8));
+          }
+          if (ea.act) {
+            float w[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) w[k] = lrelu(v[k], ea.slope);
+            sts128(stage_addr(stg_act, lane, h, scw), pack8(w));
+            sts128(stage_addr(stg_act, lane, h + 1, scw), pack8(w + 8));
+          }
+        }
+        if (tma) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (mode == kOutConv) {
+              if (ea.raw) tma_store_3d(&P.mapOut[2 * oi], stg_raw, oc, ou, b);
+              if (ea.act) tma_store_3d(&P.mapOut[2 * oi + 1], stg_act, oc, ou, b);
+            } else {
+              if (ea.raw) tma_store_4d(&P.mapOut[2 * oi], stg_raw, oc, ov, ou, b);
+              if (ea.act) tma_store_4d(&P.mapOut[2 * oi + 1], stg_act, oc, ov, ou, b);
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          pending = true;
+        }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
     }
+    // Every TMA store of this warp has finished before the CTA exits.
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   tc_fence_before();
   __syncthreads();
@@ -465,15 +637,38 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------------- host side
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF>
+// Output map of the TMA-store epilogue: box of scw channels x 32 rows, swizzled
+// like the staging rows.  Conv1d: (C, L, B).  ConvTranspose with stride s:
+// (C, s, L / s, B), so the rows of one phase of a GEMM row block are a box.
+bool encode_out(CUtensorMap* m, void* y, int mode, int B, int Lout, int Cout, int s, int scw) {
+  const CUtensorMapSwizzle sw = scw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
+  if (mode == kOutConv) {
+    cuuint64_t dims[3] = {(cuuint64_t)Cout, (cuuint64_t)Lout, (cuuint64_t)B};
+    cuuint64_t strides[2] = {(cuuint64_t)Cout * 2, (cuuint64_t)Lout * Cout * 2};
+    cuuint32_t box[3] = {(cuuint32_t)scw, 32, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, y, dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  cuuint64_t dims[4] = {(cuuint64_t)Cout, (cuuint64_t)s, (cuuint64_t)(Lout / s), (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)Cout * 2, (cuuint64_t)s * Cout * 2, (cuuint64_t)Lout * Cout * 2};
+  cuuint32_t box[4] = {(cuuint32_t)scw, 1, 32, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
-  using S = TcShape<CK, NT, NBUF>;
+  using S = TcShape<CK, NT, NBUF, STG>;
   const int nbt = RES ? P.w_tiles : SB;
-  const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch +
+  const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
                       8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
                       sizeof(float) * (size_t)P.bias_floats;
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
@@ -548,6 +743,33 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     boff += g.op[i].Cout;
   }
   P.bias_floats = boff;
+  for (int i = 0; i < g.n; ++i) {
+    const TapConv& op = P.grp.op[i];
+    P.out_mode[i] = kOutPlain;
+    P.out_scw[i] = op.Cout >= 32 ? 32 : 16;
+    P.out_s[i] = 1;
+    if (op.crop == 0 && op.N == op.Cout) {
+      P.out_mode[i] = kOutConv;
+    } else if (op.N % op.Cout == 0 && op.crop % op.Cout == 0 && op.Lout % (op.N / op.Cout) == 0) {
+      P.out_mode[i] = kOutConvT;
+      P.out_s[i] = op.N / op.Cout;
+      P.out_pad[i] = op.crop / op.Cout;
+    }
+    // Staged TMA stores pay off where a tile writes two outputs (raw and act)
+    // in rows of at least 64 bytes that a TMA box covers densely: Conv1d, and
+    // ConvTranspose of stride 2.  Elsewhere the plain 16-byte stores win.
+    const bool dense = op.out_raw && op.out_act && op.Cout >= 32 &&
+                       (P.out_mode[i] == kOutConv || (P.out_mode[i] == kOutConvT && P.out_s[i] == 2));
+    if (!dense) P.out_mode[i] = kOutPlain;
+    if (P.out_mode[i] != kOutPlain) {
+      for (int k = 0; k < 2; ++k) {
+        void* out = k == 0 ? op.out_raw : op.out_act;
+        if (out && !encode_out(&P.mapOut[2 * i + k], out, P.out_mode[i], op.B, op.Lout, op.Cout, P.out_s[i],
+                               P.out_scw[i]))
+          P.out_mode[i] = kOutPlain;
+      }
+    }
+  }
   P.row_tiles = P.grp.op[0].row_tiles;
   P.n_tiles = g.op[0].N / nt;
   P.total_tiles = g.op[0].B * P.row_tiles * P.n_tiles * g.n;
@@ -555,11 +777,19 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   P.w_tiles = wtiles;
   if (P.total_tiles <= 0) return cudaSuccess;
   // Narrow layers keep every weight tile of the launch resident in shared memory.
-  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
-  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, true, 4, 1, 4>(P, st);
-  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 2, 4, 2>(P, st);
-  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2>(P, st);
-  if (ck == 64 && nt == 64) return launch_cfg<64, 64, false, 3, 4, 4>(P, st);
+  bool stg = false;
+  for (int i = 0; i < g.n; ++i) stg = stg || P.out_mode[i] != kOutPlain;
+  // With staging, ring depths shrink to keep two CTAs per SM (one for NT = 256)
+  // next to the 16 KB of staging.
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4, false>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1)
+    return stg ? launch_cfg<32, 32, true, 3, 1, 4, true>(P, st) : launch_cfg<32, 32, true, 4, 1, 4, false>(P, st);
+  if (ck == 64 && nt == 256)
+    return stg ? launch_cfg<64, 256, false, 2, 4, 2, true>(P, st) : launch_cfg<64, 256, false, 2, 4, 2, false>(P, st);
+  if (ck == 64 && nt == 128)
+    return stg ? launch_cfg<64, 128, false, 2, 2, 2, true>(P, st) : launch_cfg<64, 128, false, 2, 3, 2, false>(P, st);
+  if (ck == 64 && nt == 64)
+    return stg ? launch_cfg<64, 64, false, 2, 4, 4, true>(P, st) : launch_cfg<64, 64, false, 3, 4, 4, false>(P, st);
   return cudaErrorInvalidValue;
 }
 
