@@ -53,6 +53,7 @@ struct alignas(64) RbParams {
   int a_stage;  // bytes per window buffer (multiple of 1024)
   int t_bytes;  // bytes of the t buffer (multiple of 1024)
   int* err;
+  int len_smem;  // lengths copied to shared memory (B ints) rather than read per tile
 };
 
 static_assert(sizeof(RbParams) <= 4096, "kernel parameter space");
@@ -134,9 +135,12 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8 + 2 * kRbWindowStages);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* sb = reinterpret_cast<float*>(tmem_slot + 4);  // b1[C], b2[C]
+  int* slen = reinterpret_cast<int*>(sb + 2 * C);        // valid rows per utterance
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int c = threadIdx.x; c < 2 * C; c += kRbThreads) sb[c] = c < C ? op.b1[c] : op.b2[c - C];
+  if (P.len_smem)
+    for (int b = threadIdx.x; b < P.B; b += kRbThreads) slen[b] = P.len ? P.len[b] : P.L;
   if (threadIdx.x == 0) {
     mbar_init(w_full, 1);
     for (int s = 0; s < kRbWindowStages; ++s) {
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
     if (lc < ntiles) ok = transform(0);
     for (int t = lc; t < ntiles && ok; t += ncta, ++i) {
       const int b = t / op.row_tiles, q0 = (t - b * op.row_tiles) * Pr;
-      const int lim = min(L, P.len ? P.len[b] : L);
+      const int lim = min(L, P.len_smem ? slen[b] : (P.len ? __ldg(P.len + b) : L));
       const uint32_t par = i & 1u;
       // b(i): t = lrelu(conv1 + b1) into shared memory, zero outside the utterance.
       if (!mbar_wait_fast(acc1_full, par, abort)) {
@@ -357,7 +361,8 @@ cudaError_t launch_c(RbParams& P, cudaStream_t st) {
   for (int i = 0; i < P.nops; ++i) kmax = std::max(kmax, P.op[i].k);
   const size_t smem = 1024 + (size_t)(2 * kmax + 1) * S::kWPitch +
                       (size_t)(kRbWindowStages + 1) * P.a_stage + P.t_bytes +
-                      8 * (8 + 2 * kRbWindowStages) + 16 + 2 * C * sizeof(float);
+                      8 * (8 + 2 * kRbWindowStages) + 16 + 2 * C * sizeof(float) +
+                      (P.len_smem ? sizeof(int) * (size_t)P.B : 0);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = rbstep_kernel<C>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -405,6 +410,7 @@ cudaError_t launch_rbstep(const RbStepGroup& g, cudaStream_t st) {
   P.len = g.len;
   P.slope = g.slope;
   P.err = g.err;
+  P.len_smem = g.B <= 1024;
   int max_win = kM;
   for (int i = 0; i < g.n; ++i) {
     const RbStepOp& o = g.op[i];

@@ -59,6 +59,7 @@ struct alignas(64) TcParams {
   int out_scw[kMaxGroup];      // channels per staged chunk (16 or 32)
   int out_s[kMaxGroup];        // ConvTranspose stride (phases per GEMM row)
   int out_pad[kMaxGroup];      // ConvTranspose crop in output rows
+  int len_smem;                // per-op valid lengths copied to shared memory (B ints each)
 };
 
 static_assert(sizeof(TcParams) <= 4096, "kernel parameter space");
@@ -102,6 +103,7 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   EpiArgs a;
   a.total = o.Lout * o.Cout;
   a.nres = o.nres;
+#pragma unroll
   for (int r = 0; r < kMaxRes; ++r)
     a.res[r] = r < o.nres ? o.res[r] + (size_t)b * a.total : nullptr;
   a.N = o.N;
@@ -154,7 +156,9 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
         v[4 * k + 3] += bv.w;
       }
     }
-    for (int r = 0; r < a.nres; ++r) {  // residual runs: 16 contiguous bf16
+#pragma unroll
+    for (int r = 0; r < kMaxRes; ++r) {  // residual runs: 16 contiguous bf16
+      if (r >= a.nres) break;
       const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -220,7 +224,9 @@ __device__ __forceinline__ bool epi16_values(const EpiArgs& a, int q, int n, flo
       v[4 * k + 3] += bv.w;
     }
   }
-  for (int r = 0; r < a.nres; ++r) {
+#pragma unroll
+  for (int r = 0; r < kMaxRes; ++r) {
+    if (r >= a.nres) break;
     const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -292,6 +298,42 @@ struct TcShape {
   static_assert(kCols <= 512, "TMEM holds 512 columns");
 };
 
+// A CTA's walk over tiles t = start, start + stride, ...: tile t is the
+// mixed-radix number (b, row tile, op, column tile) with the column tile
+// fastest.  The stride is decomposed once; each step is digit additions with
+// carries instead of three integer divisions per tile in every role.
+struct TileWalker {
+  int t, step, nt, oi, qt, b;
+  int g_nt, g_oi, g_qt, g_b;
+  int n_tiles, nops, row_tiles;
+  __device__ __forceinline__ TileWalker(int start, int stride, int n_tiles_, int nops_, int row_tiles_)
+      : t(start), step(stride), n_tiles(n_tiles_), nops(nops_), row_tiles(row_tiles_) {
+    split(start, nt, oi, qt, b);
+    split(stride, g_nt, g_oi, g_qt, g_b);
+  }
+  __device__ __forceinline__ void split(int x, int& a0, int& a1, int& a2, int& a3) const {
+    a0 = x % n_tiles;
+    x /= n_tiles;
+    a1 = x % nops;
+    x /= nops;
+    a2 = x % row_tiles;
+    a3 = x / row_tiles;
+  }
+  __device__ __forceinline__ void next() {
+    t += step;
+    nt += g_nt;
+    int c = nt >= n_tiles;
+    if (c) nt -= n_tiles;
+    oi += g_oi + c;
+    c = oi >= nops;
+    if (c) oi -= nops;
+    qt += g_qt + c;
+    c = qt >= row_tiles;
+    if (c) qt -= row_tiles;
+    b += g_b + c;
+  }
+};
+
 __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
   if (o.len == nullptr) return false;
   int e = q0 * o.N - o.crop;
@@ -324,6 +366,9 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   SmOp* ops = reinterpret_cast<SmOp*>((reinterpret_cast<uintptr_t>(tmem_slot + 2) + 15) & ~uintptr_t(15));
   float* sbias = reinterpret_cast<float*>(ops + kMaxGroup);  // every op's bias, Cout floats each
+  // Valid lengths of every op's utterances: every role tests them once per tile,
+  // a dependent global load each time otherwise.
+  int* slen = reinterpret_cast<int*>(sbias + P.bias_floats);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nops = P.grp.n;
@@ -345,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     for (int r = 0; r < kMaxRes; ++r)
       o.res[r] = r < g.nres ? static_cast<const __nv_bfloat16*>(g.res[r]) : nullptr;
     o.bias_off = P.bias_off[threadIdx.x];
-    o.len = g.len;
+    o.len = (g.len && P.len_smem) ? slen + threadIdx.x * g.B : g.len;
     o.bias = g.bias;
     o.bias_bc = g.bias_bc;
     o.out_raw = static_cast<__nv_bfloat16*>(g.out_raw);
@@ -368,6 +413,10 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   for (int o = 0; o < nops; ++o)
     for (int c = threadIdx.x; c < P.grp.op[o].Cout; c += kThreads)
       sbias[P.bias_off[o] + c] = P.grp.op[o].bias[c];
+  if (P.len_smem)
+    for (int o = 0; o < nops; ++o)
+      if (P.grp.op[o].len)
+        for (int b = threadIdx.x; b < P.grp.op[o].B; b += kThreads) slen[o * P.grp.op[o].B + b] = P.grp.op[o].len[b];
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
       mbar_init(a_full + 8 * s, 1);
@@ -392,7 +441,6 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
   int* err = P.grp.err;
   const int row_tiles = P.row_tiles, n_tiles = P.n_tiles, total = P.total_tiles;
-  const int per_m = nops * n_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -416,11 +464,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&P.mapB[f])) : "memory");
         }
       uint32_t ia = 0, ib = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int mt = t / per_m, rem = t - mt * per_m;
-        const int oi = rem / n_tiles;
-        const int n0 = (rem - oi * n_tiles) * NT;
-        const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+      for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total && ok; w.next()) {
+        const int oi = w.oi, n0 = w.nt * NT, b = w.b, q0 = w.qt * kM;
         if (tile_masked(ops[oi], b, q0)) continue;
         const int nseg = ops[oi].nseg, N = ops[oi].N;
         for (int s = 0; s < nseg && ok; ++s) {
@@ -465,10 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
         ok = false;
       }
       uint32_t ia = 0, ib = 0, i = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
-        const int mt = t / per_m, rem = t - mt * per_m;
-        const int oi = rem / n_tiles;
-        const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+      for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total && ok; w.next(), ++i) {
+        const int oi = w.oi, b = w.b, q0 = w.qt * kM;
         const bool masked = tile_masked(ops[oi], b, q0);
         const int nseg = ops[oi].nseg;
         const uint32_t buf = i % NBUF;
@@ -539,11 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     const uint32_t stg_act = stg_raw + S::kStageOut;
     bool pending = false;  // a TMA store of this warp may still be reading its staging
     uint32_t i = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-      const int mt = t / per_m, rem = t - mt * per_m;
-      const int oi = rem / n_tiles;
-      const int n0 = (rem - oi * n_tiles) * NT;
-      const int b = mt / row_tiles, q0 = (mt - b * row_tiles) * kM;
+    for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total; w.next(), ++i) {
+      const int oi = w.oi, n0 = w.nt * NT, b = w.b, q0 = w.qt * kM;
       const SmOp& o = ops[oi];
       const uint32_t buf = i % NBUF;
       const bool ok = mbar_wait_fast(acc_full + 8 * buf, (i / NBUF) & 1u, abort);
@@ -666,7 +706,8 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   const int nbt = RES ? P.w_tiles : SB;
   const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
                       8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
-                      sizeof(float) * (size_t)P.bias_floats;
+                      sizeof(float) * (size_t)P.bias_floats +
+                      (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -743,6 +784,7 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     boff += g.op[i].Cout;
   }
   P.bias_floats = boff;
+  P.len_smem = g.op[0].B <= 1024;
   for (int i = 0; i < g.n; ++i) {
     const TapConv& op = P.grp.op[i];
     P.out_mode[i] = kOutPlain;
