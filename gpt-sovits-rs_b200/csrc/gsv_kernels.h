@@ -51,11 +51,17 @@ cudaError_t launch_cond(const float* g, const float* wc, const float* bc, int B,
 // Per-stage valid lengths: lens[s*B + b] for s in [0, nstage], stage 0 = frames.
 cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, const int* add,
                            int nstage, int* lens, cudaStream_t st);
+// conv_post weights [K][16] by value (K <= 16), for the kernel-parameter path.
+struct PostWeights {
+  float w[16 * 16];
+};
 // conv_post (Cout 1, K taps, pad) + optional bias + tanh over x [B][L][C]:
 // wav[b][t] = tanh(sum_{j,c} w[j][c] x[b][t + j - pad][c] + bias); rows t >= len[b]
-// give 0.  With pre_tanh != null the pre-tanh value is stored there too.
-cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, int K, int pad,
-                        float bias, const int* len, float* wav, float* pre_tanh, cudaStream_t st);
+// give 0.  With pre_tanh != null the pre-tanh value is stored there too.  `w` is
+// the device copy; `wh` (or null) the same weights by value for the fast path.
+cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, const PostWeights* wh,
+                        int K, int pad, float bias, const int* len, float* wav, float* pre_tanh,
+                        cudaStream_t st);
 // Time-major [B][L][C] (mode dtype) -> [B][C][L] fp32, the reference's layout (taps).
 cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st);
 

@@ -349,6 +349,8 @@ struct gsvdec {
   float* d_cond_w = nullptr;  // [C0][gin]
   float* d_cond_b = nullptr;
   float* d_post_w = nullptr;
+  PostWeights post_wh{};  // the same [K][C] weights by value (K <= 16)
+  bool post_wh_ok = false;
   int* d_err = nullptr;  // error word of the bounded device waits
   std::map<int, size_t> ident_off;  // bf16: identity weights per channel width
   std::map<std::string, GemmConv> layers;  // every tap-GEMM conv by its dec.* prefix
@@ -779,7 +781,8 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
     mark(h, st);
   }
   // LeakyReLU(0.01) was applied by the producer; conv_post + tanh (:449-455).
-  CUDA_TRY(launch_post(OUT, h->dt, B, L, h->post_C, h->d_post_w, h->post_K, h->post_pad,
+  CUDA_TRY(launch_post(OUT, h->dt, B, L, h->post_C, h->d_post_w, h->post_wh_ok ? &h->post_wh : nullptr,
+                       h->post_K, h->post_pad,
                        h->post_bias, stage_len(nst), wav_dev, taps && taps[1 + 2 * nst] ? w.tap : nullptr, st));
   GSV_TRY(after_launch(h, st, "conv_post", 2, 1, 2.0 * h->post_C * h->post_K * (double)L * B,
                        eb * B * (double)h->post_C * L + 4.0 * B * (double)L + 4.0 * h->post_C * h->post_K));
@@ -922,6 +925,10 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   CUDA_TRY(cudaMemcpy(h->d_w, pk.wbytes.data(), h->w_bytes, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMalloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
   CUDA_TRY(cudaMemcpy(h->d_bias, pk.biases.data(), sizeof(float) * pk.biases.size(), cudaMemcpyHostToDevice));
+  if (post_w.size() <= sizeof(h->post_wh.w) / sizeof(float)) {
+    std::copy(post_w.begin(), post_w.end(), h->post_wh.w);
+    h->post_wh_ok = true;
+  }
   CUDA_TRY(cudaMalloc(&h->d_post_w, sizeof(float) * post_w.size()));
   CUDA_TRY(cudaMemcpy(h->d_post_w, post_w.data(), sizeof(float) * post_w.size(), cudaMemcpyHostToDevice));
   if (h->has_cond) {
@@ -1065,7 +1072,8 @@ int layer_impl(gsvdec* h, const char* name, const float* x, int B, int L, float*
   GSV_TRY(after_launch(h, st, "input_relayout", 1, 0, 0.0, (4.0 + eb) * nx));
   float* yd = mem_kind == GSV_MEM_DEVICE ? y : ys;
   if (post) {
-    CUDA_TRY(launch_post(xt, h->dt, B, L, Cin, h->d_post_w, h->post_K, h->post_pad, h->post_bias,
+    CUDA_TRY(launch_post(xt, h->dt, B, L, Cin, h->d_post_w, h->post_wh_ok ? &h->post_wh : nullptr, h->post_K,
+                         h->post_pad, h->post_bias,
                          nullptr, xs /* tanh output, unused */, yd, st));
     GSV_TRY(after_launch(h, st, name, 2, 1, 2.0 * Cin * h->post_K * (double)L * B,
                          eb * B * (double)Cin * L + 4.0 * B * (double)L + 4.0 * Cin * h->post_K));

@@ -133,6 +133,81 @@ __global__ void __launch_bounds__(256) post_kernel(const T* __restrict__ x, int 
   }
 }
 
+// conv_post for a kernel size known at compile time: the K x 16 weights are a
+// kernel parameter (the FMAs read them from the constant bank), a block stages
+// its input rows in shared memory with coalesced 16-byte loads, and thread i
+// computes samples t_base + i + 256 o (o < kPostPer), so a warp's row reads
+// are contiguous (no bank conflicts) and its stores coalesce.  The staged rows
+// take 33 KB of shared memory in either precision.
+constexpr int kPostThreads = 256;
+template <typename T>
+constexpr int post_per() { return sizeof(T) == 2 ? 4 : 2; }
+
+template <typename T, int K>
+__global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __restrict__ x, int L,
+                                                                 const __grid_constant__ PostWeights P,
+                                                                 int pad, float bias,
+                                                                 const int* __restrict__ len,
+                                                                 float* __restrict__ wav,
+                                                                 float* __restrict__ pre) {
+  constexpr int C = 16;
+  constexpr int U = C * (int)sizeof(T) / 16;  // 16-byte units per input row
+  constexpr int kPostPer = post_per<T>(), kPostOut = kPostThreads * kPostPer;
+  constexpr int kRows = kPostOut + K - 1;
+  __shared__ uint4 srow[kRows * U];
+  const int b = blockIdx.y;
+  const int t_base = blockIdx.x * kPostOut;
+  const int r0 = t_base - pad;
+  const uint4* xb = reinterpret_cast<const uint4*>(x + (size_t)b * L * C);
+  for (int i = threadIdx.x; i < kRows * U; i += kPostThreads) {
+    const int row = r0 + i / U;
+    srow[i] = (row >= 0 && row < L) ? __ldg(xb + (size_t)row * U + i % U) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  const int lim = len ? min(len[b], L) : L;
+#pragma unroll
+  for (int o = 0; o < kPostPer; ++o) {
+    const int tl = threadIdx.x + o * kPostThreads;  // sample within the block
+    const int t = t_base + tl;
+    if (t >= L) break;
+    float acc = bias;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float v[C];
+      const uint4* rp = srow + (tl + j) * U;
+      if constexpr (sizeof(T) == 2) {
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const uint4 u = rp[k];
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            v[8 * k + 2 * e] = f.x;
+            v[8 * k + 2 * e + 1] = f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const uint4 u = rp[k];
+          v[4 * k] = __uint_as_float(u.x);
+          v[4 * k + 1] = __uint_as_float(u.y);
+          v[4 * k + 2] = __uint_as_float(u.z);
+          v[4 * k + 3] = __uint_as_float(u.w);
+        }
+      }
+      float s = 0.0f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) s = fmaf(v[c], P.w[j * C + c], s);
+      acc += s;
+    }
+    const bool dead = t >= lim;
+    if (pre) pre[(size_t)b * L + t] = dead ? 0.0f : acc;
+    wav[(size_t)b * L + t] = dead ? 0.0f : tanhf(acc);
+  }
+}
+
 template <typename T>
 __global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __restrict__ y) {
   __shared__ float tile[32][33];
@@ -179,9 +254,19 @@ cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, con
   return cudaGetLastError();
 }
 
-cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, int K, int pad,
-                        float bias, const int* len, float* wav, float* pre, cudaStream_t st) {
+cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, const PostWeights* wh,
+                        int K, int pad, float bias, const int* len, float* wav, float* pre, cudaStream_t st) {
   if (K > 64 || C != 16) return cudaErrorInvalidValue;
+  if (wh != nullptr && K == 7) {
+    if (dt == Dt::F32)
+      post_fast_kernel<float, 7><<<dim3(cdiv(L, kPostThreads * post_per<float>()), B), kPostThreads, 0, st>>>(
+          static_cast<const float*>(x), L, *wh, pad, bias, len, wav, pre);
+    else
+      post_fast_kernel<__nv_bfloat16, 7>
+          <<<dim3(cdiv(L, kPostThreads * post_per<__nv_bfloat16>()), B), kPostThreads, 0, st>>>(
+              static_cast<const __nv_bfloat16*>(x), L, *wh, pad, bias, len, wav, pre);
+    return cudaGetLastError();
+  }
   dim3 grid(cdiv(L, 256 * 4), B);
   if (dt == Dt::F32)
     post_kernel<float, 16><<<grid, 256, 0, st>>>(static_cast<const float*>(x), L, w, K, pad, bias,
