@@ -14,10 +14,11 @@ data path).
 value     audio-seconds per second, whole job, inputs resident in HBM.
 e2e       the same metric through the public C-ABI call with host buffers
           (H2D of z/g and D2H of the waveform inside every timed step).
-roofline  the tap-GEMM conv kernel: achieved = algorithmic FLOPs / average
+roofline  the tap-GEMM conv launches: achieved = algorithmic FLOPs / average
           launch time (CUDA events around every launch on the forward's
-          stream, over the timed region); layer_roofline adds the survey's
-          layer-weighted fraction sum(t_roof) / sum(t_measured).
+          stream, over the timed region); layer_roofline adds the
+          layer-weighted fraction sum(t_roof) / sum(t_measured), t_roof =
+          max(FLOPs / tensor peak, bytes / HBM peak) per conv.
 """
 from __future__ import annotations
 
@@ -489,7 +490,7 @@ def main():
         bound = "fp32-core"
     achieved = f_conv / t_conv / 1e12 if t_conv > 0 else None
     traffic = None
-    prof = ROOT / "profiles" / f"tapconv_{args.mode}_traffic.json"
+    prof = ROOT / "profiles" / f"tapgemm_{args.mode}_B16x10s_traffic.json"
     if prof.exists():
         try:
             traffic = json.loads(prof.read_text()).get("dram_bytes_per_step")
@@ -498,7 +499,8 @@ def main():
     roof_s, meas_s, rows = layer_roofline(stats, args.mode, pk)
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if achieved else None, "traffic": traffic,
-                "kernel": "tapconv (all 97 tap-GEMM convs of one forward)",
+                "kernel": "tap-GEMM conv launches of one forward (tapconv_tc + fused rbstep_tc: "
+                          "all 97 convs except conv_post)",
                 "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
                                                  else "nominal fp32 CUDA-core")}
     layer = {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
