@@ -79,6 +79,58 @@ def make_state_dict(seed: int = 0, gin: int = 512, init: str = "n001", bias: str
     return sd
 
 
+FLOW_HALF = 96      # inter_channels / 2
+FLOW_HIDDEN = 192
+FLOW_KERNEL = 5
+FLOW_WN_LAYERS = 4
+FLOW_COUPLINGS = 4  # at indices 0, 2, 4, 6 (the flips between them hold no weights)
+
+
+def make_flow_state_dict(seed: int = 10, gin: int = 512, init: str = "unit", bias: str = "rand",
+                         with_cond: bool = True, n_couplings: int = FLOW_COUPLINGS) -> dict:
+    """The ``flow.flows.*`` tensors (float32) of a seeded random SoVITS v2 flow,
+    under the keys ResidualCouplingBlock::load reads (reference
+    src/models/sovits_flow.rs:346-368, 186-335, 10-108): per coupling layer
+    ``pre.{weight [192,96,1], bias}`` and ``post.{weight [96,192,1], bias}``
+    (plain weights), ``enc.in_layers.{j}`` [384,192,5], ``enc.res_skip_layers.{j}``
+    [384 or 192 (last),192,1] and ``enc.cond_layer`` [1536,gin,1] as weight-norm
+    pairs (v, g) with biases."""
+    rng = np.random.default_rng(seed)
+    sd = {}
+    h, half, k, nl = FLOW_HIDDEN, FLOW_HALF, FLOW_KERNEL, FLOW_WN_LAYERS
+
+    def w(shape, fan_in):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(_std(init, fan_in)))
+
+    def b(n):
+        if bias == "zero":
+            return np.zeros(n, np.float32)
+        return (rng.standard_normal(n, dtype=np.float32) * np.float32(0.05))
+
+    def wn(prefix, weight):
+        r = rng.uniform(0.5, 2.0, size=(weight.shape[0], 1, 1)).astype(np.float32)
+        norm = np.sqrt((weight.astype(np.float64) ** 2).sum(axis=(1, 2))).astype(np.float32)
+        sd[prefix + ".weight_v"] = (weight * r).astype(np.float32)
+        sd[prefix + ".weight_g"] = norm.reshape(-1, 1, 1)
+
+    for li in range(n_couplings):
+        p = f"flow.flows.{2 * li}"
+        sd[p + ".pre.weight"] = w((h, half, 1), half)
+        sd[p + ".pre.bias"] = b(h)
+        for j in range(nl):
+            wn(f"{p}.enc.in_layers.{j}", w((2 * h, h, k), h * k))
+            sd[f"{p}.enc.in_layers.{j}.bias"] = b(2 * h)
+            ro = 2 * h if j < nl - 1 else h
+            wn(f"{p}.enc.res_skip_layers.{j}", w((ro, h, 1), h))
+            sd[f"{p}.enc.res_skip_layers.{j}.bias"] = b(ro)
+        if with_cond:
+            wn(f"{p}.enc.cond_layer", w((2 * h * nl, gin, 1), gin))
+            sd[f"{p}.enc.cond_layer.bias"] = b(2 * h * nl)
+        sd[p + ".post.weight"] = w((half, h, 1), h)
+        sd[p + ".post.bias"] = b(half)
+    return sd
+
+
 def make_inputs(B: int, T0: int, gin: int = 512, seed_z: int = 1, seed_g: int = 2):
     """z [B,192,T0] ~ N(0,1) and g [B,gin,1] ~ N(0,1), seeded."""
     z = np.random.default_rng(seed_z).standard_normal((B, IN_CHANNELS, T0), dtype=np.float32)

@@ -58,6 +58,9 @@ def _load():
         lib.gsvo_decoder_forward.argtypes = [ctypes.POINTER(_Tensor), ctypes.c_int, fp, fp,
                                              ctypes.c_int, ctypes.c_int, fp,
                                              ctypes.POINTER(fp), ctypes.c_int, ctypes.c_int]
+        lib.gsvo_flow_inverse.argtypes = [ctypes.POINTER(_Tensor), ctypes.c_int, ctypes.c_char_p, fp,
+                                          fp, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                          ctypes.c_int, fp, ctypes.c_int, ctypes.c_int]
         _lib = lib
     return _lib
 
@@ -172,6 +175,44 @@ def decoder_forward(state_dict, z, g=None, acc64=True, taps=False, nthreads=0):
     if taps:
         return wav, tap_bufs
     return wav
+
+
+def _tensor_array(state_dict, prefix=None):
+    items = [(k, v) for k, v in state_dict.items() if prefix is None or k.startswith(prefix)]
+    keep = []
+    arr = (_Tensor * max(1, len(items)))()
+    for i, (k, v) in enumerate(items):
+        a = _f32(np.asarray(v, dtype=np.float32))
+        keep.append(a)
+        arr[i].name = k.encode()
+        arr[i].data = _fp(a)
+        arr[i].ndim = a.ndim
+        for d in range(a.ndim):
+            arr[i].shape[d] = a.shape[d]
+    return arr, len(items), keep
+
+
+def flow_inverse(state_dict, z_p, g=None, lengths=None, prefix="flow.flows", acc64=True,
+                 nthreads=0):
+    """z = flow^-1(z_p) * y_mask: ResidualCouplingBlock::forward(reverse = true)
+    (reference src/models/sovits_flow.rs:341-415) then src/models/sovits.rs:394.
+
+    z_p [B, 192, T0]; g [B, gin, 1] or None; lengths [B] (valid frames) or None.
+    """
+    lib = _load()
+    arr, n, keep = _tensor_array(state_dict, prefix + ".")
+    z_p = _f32(z_p)
+    B, C, T0 = z_p.shape
+    gg = _f32(g) if g is not None else None
+    ln = None
+    if lengths is not None:
+        la = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
+        keep.append(la)
+        ln = la.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    z = np.empty((B, C, T0), np.float32)
+    _check(lib.gsvo_flow_inverse(arr, n, prefix.encode(), _fp(z_p), _fp(gg), ln, B, T0, _fp(z),
+                                 int(acc64), int(nthreads)))
+    return z
 
 
 def num_threads() -> int:

@@ -202,7 +202,7 @@ typedef struct {
 } conv_t;
 
 static int load_plain(const gsvo_tensor* ts, int n, const char* pfx, int required, conv_t* c) {
-  char key[160];
+  char key[256];
   snprintf(key, sizeof key, "%s.weight", pfx);
   const gsvo_tensor* w = find(ts, n, key);
   if (!w) return required ? fail("key not found in state dict", key) : 1;
@@ -219,7 +219,7 @@ static int load_plain(const gsvo_tensor* ts, int n, const char* pfx, int require
 }
 
 static int load_wn(const gsvo_tensor* ts, int n, const char* pfx, conv_t* c) {
-  char key[160];
+  char key[256];
   snprintf(key, sizeof key, "%s.weight_v", pfx);
   const gsvo_tensor* v = find(ts, n, key);
   if (!v) return fail("key not found in state dict", key);
@@ -268,7 +268,7 @@ static int load_dec(const gsvo_tensor* ts, int n, dec_t* d) {
   /* Upsample strides are training config, hard-coded [10,8,2,2,2] with a
    * fallback of 2 (src/models/sovits_decoder.rs:252-270). */
   static const int rates[5] = {10, 8, 2, 2, 2};
-  char key[160];
+  char key[256];
   for (int i = 0; i < MAX_UPS; ++i) {
     snprintf(key, sizeof key, "dec.ups.%d.weight_v", i);
     if (!find(ts, n, key)) continue;
@@ -413,5 +413,210 @@ int gsvo_decoder_forward(const gsvo_tensor* ts, int n_tensors, const float* z, c
 out:
   free(x); free(y); free(acc); free(t1); free(t2); free(rbo);
   free_dec(&d);
+  return rc;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Flow inverse: ResidualCouplingBlock::forward(reverse = true)             */
+/* (src/models/sovits_flow.rs:341-415) over ResidualCouplingLayer           */
+/* (:186-335) and WN (:10-168), then z * y_mask (src/models/sovits.rs:394). */
+
+#define MAX_FLOWS 8
+#define MAX_WN 16
+
+typedef struct {
+  conv_t pre, post, cond;
+  conv_t in[MAX_WN], rs[MAX_WN];
+  int n_wn, has_cond, half;
+} couple_t;
+
+typedef struct {
+  couple_t L[MAX_FLOWS];
+  int n;
+} flow_t;
+
+static void free_flow(flow_t* f) {
+  for (int l = 0; l < f->n; ++l) {
+    couple_t* c = &f->L[l];
+    free(c->pre.w); free(c->post.w); free(c->cond.w);
+    for (int i = 0; i < c->n_wn; ++i) { free(c->in[i].w); free(c->rs[i].w); }
+  }
+}
+
+/* ResidualCouplingLayer::load_conv (:225-279): weight-norm pair if present,
+ * else the plain weight (whose g = ||w|| makes the fold the identity up to
+ * rounding; the plain weight is used as is). */
+static int load_pre_post(const gsvo_tensor* ts, int n, const char* pfx, conv_t* c) {
+  char key[256];
+  snprintf(key, sizeof key, "%s.weight_v", pfx);
+  if (find(ts, n, key)) return load_wn(ts, n, pfx, c);
+  return load_plain(ts, n, pfx, 1, c);
+}
+
+/* ResidualCouplingBlock::load (:346-368): layers at indices 0..7 that carry a
+ * pre.weight (the flips between them hold no weights). */
+static int load_flow(const gsvo_tensor* ts, int n, const char* prefix, flow_t* f) {
+  memset(f, 0, sizeof *f);
+  char key[200], pfx[200];
+  for (int i = 0; i < MAX_FLOWS; ++i) {
+    snprintf(key, sizeof key, "%s.%d.pre.weight", prefix, i);
+    if (!find(ts, n, key)) continue;
+    couple_t* c = &f->L[f->n];
+    memset(c, 0, sizeof *c);
+    f->n++;
+    snprintf(pfx, sizeof pfx, "%s.%d.pre", prefix, i);
+    if (load_pre_post(ts, n, pfx, &c->pre)) return -1;
+    snprintf(pfx, sizeof pfx, "%s.%d.post", prefix, i);
+    if (load_pre_post(ts, n, pfx, &c->post)) return -1;
+    c->half = c->pre.I; /* half_channels = pre.weight_v.dims()[1] (:211-213) */
+    for (int j = 0; j < MAX_WN; ++j) {
+      snprintf(key, sizeof key, "%s.%d.enc.in_layers.%d.weight_v", prefix, i, j);
+      if (!find(ts, n, key)) break;
+      snprintf(pfx, sizeof pfx, "%s.%d.enc.in_layers.%d", prefix, i, j);
+      if (load_wn(ts, n, pfx, &c->in[j])) return -1;
+      c->n_wn++;
+    }
+    for (int j = 0; j < c->n_wn; ++j) {
+      snprintf(pfx, sizeof pfx, "%s.%d.enc.res_skip_layers.%d", prefix, i, j);
+      if (load_wn(ts, n, pfx, &c->rs[j])) return -1;
+    }
+    snprintf(key, sizeof key, "%s.%d.enc.cond_layer.weight_v", prefix, i);
+    if (find(ts, n, key)) {
+      snprintf(pfx, sizeof pfx, "%s.%d.enc.cond_layer", prefix, i);
+      if (load_wn(ts, n, pfx, &c->cond)) return -1;
+      c->has_cond = 1;
+    }
+    if (c->n_wn == 0) return fail("coupling layer without WN in_layers", pfx);
+  }
+  if (f->n == 0) return fail("no flow coupling layers under the prefix", prefix);
+  return 0;
+}
+
+static double sigm(double v) { return 1.0 / (1.0 + exp(-v)); }
+
+/* WN::forward (:119-168) on h [B, hid, T] (already masked), mask [B, T]. */
+static int wn_forward(const couple_t* c, const float* h_in, const float* mask, const float* gproj,
+                      int B, int T, float* out, float* xw, float* xin, float* acts, float* rsb,
+                      int acc64) {
+  const int hid = c->in[0].I;
+  const int64_t nh = (int64_t)B * hid * T;
+  memcpy(xw, h_in, sizeof(float) * (size_t)nh);
+  memset(out, 0, sizeof(float) * (size_t)nh);
+  for (int i = 0; i < c->n_wn; ++i) {
+    const conv_t* in = &c->in[i];
+    const conv_t* rs = &c->rs[i];
+    /* x_masked = x * mask; x_in = in_layer(x_masked) */
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < nh; ++e) acts[e] = xw[e] * mask[(e / ((int64_t)hid * T)) * T + e % T];
+    if (gsvo_conv1d(acts, B, hid, T, in->w, in->O, in->K, in->pad, 1, in->b, xin, acc64)) return -1;
+    /* fused_add_tanh_sigmoid_multiply (:171-184): tanh(a + g_a) * sigmoid(b + g_b) */
+#pragma omp parallel for schedule(static)
+    for (int64_t e = 0; e < nh; ++e) {
+      const int64_t b = e / ((int64_t)hid * T), ch = (e / T) % hid, t = e % T;
+      const float* xi = xin + (int64_t)b * 2 * hid * T;
+      double a = xi[ch * T + t], s = xi[(hid + ch) * T + t];
+      if (gproj) {
+        const float* gl = gproj + (int64_t)b * c->cond.O + (int64_t)i * 2 * hid;
+        a = (double)(float)(a + gl[ch]);
+        s = (double)(float)(s + gl[hid + ch]);
+      }
+      acts[e] = acc64 ? (float)(tanh(a) * sigm(s)) : tanhf((float)a) * (1.0f / (1.0f + expf(-(float)s)));
+    }
+    if (gsvo_conv1d(acts, B, hid, T, rs->w, rs->O, rs->K, rs->pad, 1, rs->b, rsb, acc64)) return -1;
+    if (i < c->n_wn - 1) {
+      /* x = (x + res) * mask; output += skip */
+#pragma omp parallel for schedule(static)
+      for (int64_t e = 0; e < nh; ++e) {
+        const int64_t b = e / ((int64_t)hid * T), ch = (e / T) % hid, t = e % T;
+        const float* r = rsb + (int64_t)b * rs->O * T;
+        xw[e] = (xw[e] + r[ch * T + t]) * mask[b * T + t];
+        out[e] = out[e] + r[(hid + ch) * T + t];
+      }
+    } else {
+#pragma omp parallel for schedule(static)
+      for (int64_t e = 0; e < nh; ++e) {
+        const int64_t b = e / ((int64_t)hid * T), ch = (e / T) % hid, t = e % T;
+        out[e] = out[e] + rsb[(int64_t)b * rs->O * T + ch * T + t];
+      }
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (int64_t e = 0; e < nh; ++e) out[e] = out[e] * mask[(e / ((int64_t)hid * T)) * T + e % T];
+  return 0;
+}
+
+/* z = flow^-1(z_p) * y_mask.  z_p and z are [B, C, T0] (C = 2 * half);
+ * g [B, gin, 1] or NULL; lengths [B] or NULL (all T0). */
+int gsvo_flow_inverse(const gsvo_tensor* ts, int n_tensors, const char* prefix, const float* z_p,
+                      const float* g, const int* lengths, int B, int T0, float* z, int acc64,
+                      int nthreads) {
+  if (nthreads > 0) omp_set_num_threads(nthreads);
+  if (B <= 0 || T0 <= 0) return fail("batch and frame count must be positive", NULL);
+  flow_t f;
+  if (load_flow(ts, n_tensors, prefix, &f)) { free_flow(&f); return -1; }
+  int rc = -1;
+  const int half = f.L[0].half, C = 2 * half, T = T0;
+  int hid = f.L[0].in[0].I, maxo = 0;
+  for (int l = 0; l < f.n; ++l) {
+    if (f.L[l].half != half || f.L[l].in[0].I != hid) { fail("flow layer shapes differ", NULL); free_flow(&f); return -1; }
+    for (int i = 0; i < f.L[l].n_wn; ++i) {
+      if (f.L[l].in[i].O > maxo) maxo = f.L[l].in[i].O;
+      if (f.L[l].rs[i].O > maxo) maxo = f.L[l].rs[i].O;
+    }
+    if (f.L[l].post.O > maxo) maxo = f.L[l].post.O;
+  }
+  const int64_t nx = (int64_t)B * C * T, nh = (int64_t)B * hid * T, nw = (int64_t)B * maxo * T;
+  float *x = alloc_f(nx), *xf = alloc_f(nx), *mask = alloc_f((int64_t)B * T), *h = alloc_f(nh),
+        *out = alloc_f(nh), *xw = alloc_f(nh), *xin = alloc_f(nw), *acts = alloc_f(nh),
+        *rsb = alloc_f(nw), *x0 = alloc_f((int64_t)B * half * T), *gp = NULL;
+  for (int b = 0; b < B; ++b) {
+    const int len = lengths ? lengths[b] : T;
+    for (int t = 0; t < T; ++t) mask[(int64_t)b * T + t] = t < len ? 1.0f : 0.0f;
+  }
+  memcpy(x, z_p, sizeof(float) * (size_t)nx);
+  for (int l = f.n - 1; l >= 0; --l) {
+    const couple_t* c = &f.L[l];
+    /* flip along channels (:408-414) */
+    for (int b = 0; b < B; ++b)
+      for (int ch = 0; ch < C; ++ch)
+        memcpy(xf + ((int64_t)b * C + ch) * T, x + ((int64_t)b * C + (C - 1 - ch)) * T, sizeof(float) * (size_t)T);
+    { float* s = x; x = xf; xf = s; }
+    /* h = pre(x0) * mask */
+    for (int b = 0; b < B; ++b)
+      memcpy(x0 + (int64_t)b * half * T, x + (int64_t)b * C * T, sizeof(float) * (size_t)half * T);
+    if (gsvo_conv1d(x0, B, half, T, c->pre.w, c->pre.O, c->pre.K, c->pre.pad, 1, c->pre.b, h, acc64)) goto out;
+    for (int64_t e = 0; e < nh; ++e) h[e] *= mask[(e / ((int64_t)hid * T)) * T + e % T];
+    free(gp); gp = NULL;
+    if (c->has_cond && g) {
+      gp = alloc_f((int64_t)B * c->cond.O);
+      if (gsvo_conv1d(g, B, c->cond.I, 1, c->cond.w, c->cond.O, c->cond.K, c->cond.pad, 1, c->cond.b, gp, acc64)) goto out;
+    }
+    if (wn_forward(c, h, mask, gp, B, T, out, xw, xin, acts, rsb, acc64)) goto out;
+    /* stats = post(h) * mask; mean-only when post has half_channels outputs (:298-318) */
+    if (gsvo_conv1d(out, B, hid, T, c->post.w, c->post.O, c->post.K, c->post.pad, 1, c->post.b, rsb, acc64)) goto out;
+    {
+      const int so = c->post.O;
+      const int has_logs = so >= 2 * half;
+      for (int b = 0; b < B; ++b)
+        for (int ch = 0; ch < half; ++ch)
+          for (int t = 0; t < T; ++t) {
+            const float mk = mask[(int64_t)b * T + t];
+            const float m = rsb[((int64_t)b * so + ch) * T + t] * mk;
+            const float lg = has_logs ? rsb[((int64_t)b * so + half + ch) * T + t] * mk : 0.0f;
+            float* x1 = x + ((int64_t)b * C + half + ch) * T + t;
+            /* inverse: x1 = (x1 - m) * exp(-logs) (:327-333) */
+            *x1 = (*x1 - m) * expf(-lg);
+          }
+    }
+  }
+  for (int b = 0; b < B; ++b)
+    for (int ch = 0; ch < C; ++ch)
+      for (int t = 0; t < T; ++t)
+        z[((int64_t)b * C + ch) * T + t] = x[((int64_t)b * C + ch) * T + t] * mask[(int64_t)b * T + t];
+  rc = 0;
+out:
+  free(x); free(xf); free(mask); free(h); free(out); free(xw); free(xin); free(acts); free(rsb);
+  free(x0); free(gp);
+  free_flow(&f);
   return rc;
 }

@@ -24,6 +24,12 @@ int gsvo_conv_transpose1d(const float* x, int B, int Cin, int L, const float* w,
                           int stride, int pad, const float* bias, float* y, int acc64);
 int gsvo_decoder_forward(const gsvo_tensor* ts, int n_tensors, const float* z, const float* g,
                          int B, int T0, float* wav, float** taps, int acc64, int nthreads);
+/* Flow inverse (src/models/sovits_flow.rs:341-415, reverse = true) followed by
+ * z * y_mask (src/models/sovits.rs:394): z_p, z [B, C, T0]; g [B, gin, 1] or
+ * NULL; lengths [B] or NULL.  prefix is the state-dict prefix ("flow.flows"). */
+int gsvo_flow_inverse(const gsvo_tensor* ts, int n_tensors, const char* prefix, const float* z_p,
+                      const float* g, const int* lengths, int B, int T0, float* z, int acc64,
+                      int nthreads);
 
 #ifdef __cplusplus
 }

@@ -36,6 +36,11 @@ def tiny():
     return dict(np.load(GOLDEN / "decoder_tiny.npz"))
 
 
+@pytest.fixture(scope="session")
+def flow_golden():
+    return dict(np.load(GOLDEN / "flow_tiny.npz"))
+
+
 def rel_max(a, b):
     """max |a - b| / max |b|."""
     a = np.asarray(a, np.float64)

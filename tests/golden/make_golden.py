@@ -17,6 +17,10 @@ independent of both the C oracle and the CUDA library.  Inputs:
 * ``decoder_tiny.npz`` -- whole-Generator outputs for seeded weights
   (synth.make_state_dict) at T0 in {1, 2, 3, 7}, B = 2, two inits; the
   state-dict checksum is stored to detect generator drift.
+* ``flow_tiny.npz`` -- flow inverse (ResidualCouplingBlock reverse, then
+  z * y_mask) for seeded flow weights (synth.make_flow_state_dict), B = 2,
+  T0 in {1, 5, 24} with lengths (T0, ceil(T0/2)), with and without g; the
+  state-dict checksum again guards the generator.
 """
 from __future__ import annotations
 
@@ -76,7 +80,28 @@ def decoders():
     return out
 
 
+def flows():
+    gsv = load_pkg()
+    import torch_ref
+    out = {}
+    for init in ("unit", "n001"):
+        sd = gsv.synth.make_flow_state_dict(init=init)
+        out[f"{init}_checksum"] = np.array(gsv.synth.checksum(sd))
+        for T0 in (1, 5, 24):
+            rng = np.random.default_rng(100 + T0)
+            zp = rng.standard_normal((2, 192, T0)).astype(np.float32)
+            g = rng.standard_normal((2, 512, 1)).astype(np.float32)
+            lengths = np.array([T0, (T0 + 1) // 2], np.int32)
+            out[f"T{T0}_zp"] = zp
+            out[f"T{T0}_g"] = g
+            out[f"T{T0}_len"] = lengths
+            out[f"{init}_T{T0}_z"] = torch_ref.flow_inverse(sd, zp, g, lengths).astype(np.float32)
+            out[f"{init}_T{T0}_z_nog"] = torch_ref.flow_inverse(sd, zp, None, None).astype(np.float32)
+    return out
+
+
 if __name__ == "__main__":
     np.savez_compressed(HERE / "kat_ref.npz", **kats())
     np.savez_compressed(HERE / "decoder_tiny.npz", **decoders())
+    np.savez_compressed(HERE / "flow_tiny.npz", **flows())
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

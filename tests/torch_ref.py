@@ -74,3 +74,49 @@ def decoder_forward(sd, z, g=None, taps=False):
     if taps:
         return wav, [t.numpy() for t in out_taps]
     return wav
+
+
+def flow_inverse(sd, z_p, g=None, lengths=None, prefix="flow.flows"):
+    """z = flow^-1(z_p) * y_mask in float64: ResidualCouplingBlock::forward with
+    reverse = true (src/models/sovits_flow.rs:341-415; coupling layer :286-335,
+    WN :119-168) and src/models/sovits.rs:394, with torch conv semantics."""
+    x = torch.as_tensor(np.asarray(z_p), dtype=torch.float64)
+    B, C, T = x.shape
+    ln = torch.full((B,), T) if lengths is None else torch.as_tensor(np.asarray(lengths))
+    mask = (torch.arange(T)[None, :] < ln[:, None]).to(torch.float64)[:, None, :]
+    gg = torch.as_tensor(np.asarray(g), dtype=torch.float64) if g is not None else None
+    idx = [i for i in range(8) if f"{prefix}.{i}.pre.weight" in sd]
+
+    def conv(p, inp):
+        w = fold(sd, p) if p + ".weight_v" in sd else t64(sd, p + ".weight")
+        return F.conv1d(inp, w, t64(sd, p + ".bias"), padding=(w.shape[2] - 1) // 2)
+
+    for i in reversed(idx):
+        p = f"{prefix}.{i}"
+        x = torch.flip(x, dims=[1])
+        half = sd[p + ".pre.weight"].shape[1]
+        x0, x1 = x[:, :half], x[:, half:]
+        h = conv(p + ".pre", x0) * mask
+        nl = len([j for j in range(16) if f"{p}.enc.in_layers.{j}.weight_v" in sd])
+        hid = h.shape[1]
+        gp = conv(p + ".enc.cond_layer", gg) if gg is not None and p + ".enc.cond_layer.weight_v" in sd else None
+        out = torch.zeros_like(h)
+        xw = h
+        for j in range(nl):
+            xin = conv(f"{p}.enc.in_layers.{j}", xw * mask)
+            if gp is not None:
+                xin = xin + gp[:, j * 2 * hid:(j + 1) * 2 * hid]
+            acts = torch.tanh(xin[:, :hid]) * torch.sigmoid(xin[:, hid:])
+            rs = conv(f"{p}.enc.res_skip_layers.{j}", acts)
+            if j < nl - 1:
+                xw = (xw + rs[:, :hid]) * mask
+                out = out + rs[:, hid:]
+            else:
+                out = out + rs
+        stats = conv(p + ".post", out * mask) * mask
+        if stats.shape[1] >= 2 * half:
+            m, logs = stats[:, :half], stats[:, half:]
+        else:
+            m, logs = stats, torch.zeros_like(stats)
+        x = torch.cat([x0, (x1 - m) * torch.exp(-logs)], dim=1)
+    return (x * mask).numpy()
