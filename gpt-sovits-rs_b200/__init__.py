@@ -38,7 +38,8 @@ EXPORTS = (
     "gsvdec_forward", "gsvdec_forward_chunk", "gsvdec_forward_taps", "gsvdec_set_stage_timing",
     "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
     "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_layer_forward",
-    "gsvdec_layer_names", "gsvdec_last_error",
+    "gsvdec_layer_names", "gsvdec_last_error", "gsvdec_flow_info", "gsvdec_flow_inverse",
+    "gsvdec_flow_decode",
 )
 
 
@@ -101,6 +102,9 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
     lib.gsvdec_layer_forward.argtypes = [vp, ctypes.c_char_p, vp, i, i, vp, i, vp]
     lib.gsvdec_layer_names.argtypes = [vp, ctypes.c_char_p, ctypes.c_size_t,
                                        ctypes.POINTER(ctypes.c_size_t)]
+    lib.gsvdec_flow_info.argtypes = [vp, ctypes.POINTER(i), ctypes.POINTER(i)]
+    lib.gsvdec_flow_inverse.argtypes = [vp, vp, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_flow_decode.argtypes = [vp, vp, vp, vp, i, i, vp, i, vp]
     _lib = lib
     return lib
 
@@ -260,6 +264,72 @@ class Decoder:
             None if g is None else ctypes.c_void_p(g.data_ptr()),
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
             B, T0, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(st)))
+        return out
+
+    # -- ResidualCouplingBlock::forward(reverse = true) ----------------------
+    @property
+    def flow_couplings(self) -> int:
+        """Coupling layers of the flow loaded with this handle (0: none)."""
+        n, c = ctypes.c_int(), ctypes.c_int()
+        _check(library().gsvdec_flow_info(self._h, ctypes.byref(n), ctypes.byref(c)))
+        return n.value
+
+    def flow_inverse(self, z_p, g=None, lengths: Optional[Sequence[int]] = None) -> np.ndarray:
+        """z = flow^-1(z_p) * y_mask (src/models/sovits_flow.rs:385-405 with
+        reverse = true, src/models/sovits.rs:391-394) on host arrays:
+        z_p [B, 192, T0], g [B, gin, 1] or None, lengths [B] or None."""
+        zp = _host_f32(z_p)
+        if zp.ndim != 3:
+            raise ValueError("z_p must be [B, C, T]")
+        B, C, T0 = zp.shape
+        gg = _host_f32(g)
+        ln = None if lengths is None else np.ascontiguousarray(np.asarray(lengths, np.int32))
+        if ln is not None and ln.shape != (B,):
+            raise ValueError("lengths must hold one value per utterance")
+        z = np.empty((B, C, T0), np.float32)
+        _check(library().gsvdec_flow_inverse(self._h, _ptr(zp), _ptr(gg), _ptr(ln), B, T0, _ptr(z),
+                                             MEM_HOST, None))
+        return z
+
+    def flow_decode(self, z_p, g=None, lengths: Optional[Sequence[int]] = None, out=None) -> np.ndarray:
+        """Flow inverse then Decoder::forward with the same g and lengths
+        (src/models/sovits.rs:389-400): the flattened fp32 waveform."""
+        zp = _host_f32(z_p)
+        B, _, T0 = zp.shape
+        gg = _host_f32(g)
+        ln = None if lengths is None else np.ascontiguousarray(np.asarray(lengths, np.int32))
+        if out is None:
+            out = np.empty(B * self.out_len(T0), np.float32)
+        _check(library().gsvdec_flow_decode(self._h, _ptr(zp), _ptr(gg), _ptr(ln), B, T0, _ptr(out),
+                                            MEM_HOST, None))
+        return out
+
+    def flow_inverse_device(self, z_p, g=None, lengths=None, out=None, stream=None):
+        """Stream-async flow inverse on CUDA tensors (torch)."""
+        import torch
+        B, C, T0 = z_p.shape
+        assert z_p.is_cuda and z_p.dtype == torch.float32 and z_p.is_contiguous()
+        if out is None:
+            out = torch.empty((B, C, T0), device=z_p.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream(z_p.device).cuda_stream
+        _check(library().gsvdec_flow_inverse(
+            self._h, ctypes.c_void_p(z_p.data_ptr()), None if g is None else ctypes.c_void_p(g.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T0,
+            ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    def flow_decode_device(self, z_p, g=None, lengths=None, out=None, stream=None):
+        """Stream-async flow inverse + decoder on CUDA tensors (torch)."""
+        import torch
+        B, _, T0 = z_p.shape
+        assert z_p.is_cuda and z_p.dtype == torch.float32 and z_p.is_contiguous()
+        if out is None:
+            out = torch.empty(B * self.out_len(T0), device=z_p.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream(z_p.device).cuda_stream
+        _check(library().gsvdec_flow_decode(
+            self._h, ctypes.c_void_p(z_p.data_ptr()), None if g is None else ctypes.c_void_p(g.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T0,
+            ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
         return out
 
     def forward_chunk(self, x, g, frame_begin: int, frame_end: int, halo: int = 16) -> np.ndarray:

@@ -62,7 +62,16 @@ struct PostWeights {
 cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, const PostWeights* wh,
                         int K, int pad, float bias, const int* len, float* wav, float* pre_tanh,
                         cudaStream_t st);
-// Time-major [B][L][C] (mode dtype) -> [B][C][L] fp32, the reference's layout (taps).
-cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st);
+// Time-major [B][L][C] (mode dtype) -> [B][C][L] fp32, the reference's layout
+// (taps, flow output).  With perm (device, C ints) output channel c reads
+// input channel perm[c].
+cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st,
+                          const int* perm = nullptr);
+// WN gated activation (src/models/sovits_flow.rs:171-184):
+// out[b][t][c] = tanh(xin[b][t][c] + g[c]) * sigmoid(xin[b][t][H + c] + g[H + c]),
+// g = cond[b][off ..] (or 0 without cond); rows t >= len[b] give 0.
+// xin [B][L][2H], out [B][L][H] in the mode dtype; H % 8 == 0.
+cudaError_t launch_gate(const void* xin, const float* cond, int cond_ld, int cond_off, int B, int L,
+                        int H, const int* len, void* out, Dt dt, cudaStream_t st);
 
 }  // namespace gsv

@@ -237,6 +237,58 @@ int load_model(const gsvdec_tensor* ts, int n, HostModel& m) {
 }
 
 // ---------------------------------------------------------------------------
+// Host-side flow, following ResidualCouplingBlock::load
+// (src/models/sovits_flow.rs:346-368): coupling layers at indices 0..7 that
+// carry "<i>.pre.weight"; per layer pre/post (weight-norm pair if present,
+// else the plain weight: :225-279), and a WN (:19-109) of in_layers (k, pad
+// (k-1)/2, dilation 1), res_skip_layers and an optional cond_layer.
+
+struct HostCoupling {
+  HostConv pre, post, cond;
+  std::vector<HostConv> in, rs;
+  bool has_cond = false;
+};
+
+struct HostFlow {
+  std::vector<HostCoupling> layers;
+};
+
+int load_pre_post(const TensorMap& tm, const std::string& pfx, HostConv& c) {
+  if (tm.get(pfx + ".weight_v")) return load_wn(tm, pfx, c);
+  return load_plain(tm, pfx, c);
+}
+
+int load_flow(const gsvdec_tensor* ts, int n, const std::string& prefix, HostFlow& f) {
+  TensorMap tm;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].name) tm.m[ts[i].name] = &ts[i];
+  for (int i = 0; i < 8; ++i) {
+    const std::string p = prefix + "." + std::to_string(i);
+    if (!tm.get(p + ".pre.weight")) continue;
+    HostCoupling c;
+    GSV_TRY(load_pre_post(tm, p + ".pre", c.pre));
+    GSV_TRY(load_pre_post(tm, p + ".post", c.post));
+    for (int j = 0; tm.get(p + ".enc.in_layers." + std::to_string(j) + ".weight_v"); ++j) {
+      HostConv a;
+      GSV_TRY(load_wn(tm, p + ".enc.in_layers." + std::to_string(j), a));
+      c.in.push_back(std::move(a));
+    }
+    for (size_t j = 0; j < c.in.size(); ++j) {
+      HostConv r;
+      GSV_TRY(load_wn(tm, p + ".enc.res_skip_layers." + std::to_string(j), r));
+      c.rs.push_back(std::move(r));
+    }
+    if (tm.get(p + ".enc.cond_layer.weight_v")) {
+      GSV_TRY(load_wn(tm, p + ".enc.cond_layer", c.cond));
+      c.has_cond = true;
+    }
+    if (c.in.empty()) return set_err(GSV_E_MISSING_KEY, "Key '%s.enc.in_layers.0.weight_v' not found in state dict", p.c_str());
+    f.layers.push_back(std::move(c));
+  }
+  return GSV_OK;
+}
+
+// ---------------------------------------------------------------------------
 // Packed device form of one conv as a tap GEMM (see gsv_internal.h).
 
 struct GemmConv {
@@ -380,12 +432,135 @@ struct gsvdec {
   std::vector<std::vector<Rec>> run_recs;
   std::vector<cudaEvent_t> pool;
   std::vector<gsvdec_launch_stat> stats;
+  // Flow inverse (present when the tensors include flow.flows.*).  Channels
+  // are never moved for the flips: each layer's weights are packed against
+  // the physical channel order that layer sees.
+  struct FlowLayer {
+    GemmConv pre;                  // 1x1, all C physical channels in (x1 weights zero) -> hid
+    std::vector<GemmConv> in;      // WN in_layers, hid -> 2 hid, k taps
+    std::vector<GemmConv> res;     // residual halves of res_skip 0 .. n-2, hid -> hid
+    std::vector<GemmConv> post;    // coupling update, one segment per WN layer, hid -> C
+    float* d_cond_w = nullptr;     // [2 hid n][gin]
+    float* d_cond_b = nullptr;
+    bool has_cond = false;
+  };
+  std::vector<FlowLayer> flow;
+  int flow_C = 0, flow_half = 0, flow_hid = 0, flow_nwn = 0, flow_gin = 0;
+  int* d_flow_perm = nullptr;      // physical channel of each output channel
+  std::vector<int> flow_perm_host;
+  void* fws = nullptr;
+  size_t fws_bytes = 0;
 };
 
 namespace gsv {
 namespace {
 
 size_t act_bytes(const gsvdec* h) { return h->dt == Dt::F32 ? 4 : 2; }
+
+// Packs the flow for the inverse direction (ResidualCouplingBlock::forward
+// with reverse = true, src/models/sovits_flow.rs:385-405).  With the
+// activations time-major the channel flips (:408-414) become permutations of
+// packed weight rows/columns: layer l sees the physical order pi_l (its
+// logical channel j lives at physical pi_l[j]).  The coupling update of a
+// mean-only layer, x1 <- x1 - mask * (post(mask * sum_j skip_j(acts_j)) +
+// b_post) (:286-335, WN :155-167), is linear in the WN activations, so it is
+// packed as ONE tap GEMM with a segment per WN layer, weights
+// -W_post * W_skip_j (folded in double precision) and bias
+// -(W_post * sum_j b_skip_j + b_post), placed on x1's physical rows; the
+// residual x enters as an identity segment and x0 passes through unchanged.
+int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector<float>>& cond_w,
+              std::vector<std::vector<float>>& cond_b) {
+  const HostCoupling& c0 = hf.layers[0];
+  const int half = c0.pre.d1, hid = c0.pre.d0, C = 2 * half, nl = (int)c0.in.size();
+  const int gin = c0.has_cond ? c0.cond.d1 : 0;
+  for (const HostCoupling& c : hf.layers) {
+    if (c.pre.d1 != half || c.pre.d0 != hid || c.pre.K != 1 || (int)c.in.size() != nl)
+      return set_err(GSV_E_SHAPE, "%s: flow coupling layers differ in shape", c.pre.name.c_str());
+    if (c.post.d1 != hid || c.post.K != 1)
+      return set_err(GSV_E_SHAPE, "%s: post must be a 1x1 conv from %d channels", c.post.name.c_str(), hid);
+    if (c.post.d0 != half)
+      return set_err(GSV_E_UNSUPPORTED, "%s: only mean-only coupling layers (%d outputs) are supported, got %d",
+                     c.post.name.c_str(), half, c.post.d0);
+    for (int j = 0; j < nl; ++j) {
+      if (c.in[j].d0 != 2 * hid || c.in[j].d1 != hid || c.in[j].K % 2 == 0)
+        return set_err(GSV_E_SHAPE, "%s: expected [%d, %d, odd k]", c.in[j].name.c_str(), 2 * hid, hid);
+      if (c.rs[j].d0 != (j < nl - 1 ? 2 * hid : hid) || c.rs[j].d1 != hid || c.rs[j].K != 1)
+        return set_err(GSV_E_SHAPE, "%s: unexpected res/skip shape", c.rs[j].name.c_str());
+    }
+    if (c.has_cond != c0.has_cond || (c.has_cond && (c.cond.d0 != 2 * hid * nl || c.cond.K != 1 || c.cond.d1 != gin)))
+      return set_err(GSV_E_SHAPE, "%s: cond_layer must be [%d, gin, 1] in every layer", c.pre.name.c_str(), 2 * hid * nl);
+  }
+  const int n = (int)hf.layers.size();
+  h->flow.assign(n, {});
+  h->flow_C = C; h->flow_half = half; h->flow_hid = hid; h->flow_nwn = nl; h->flow_gin = gin;
+  cond_w.assign(n, {});
+  cond_b.assign(n, {});
+  std::vector<int> pi(C);
+  for (int j = 0; j < C; ++j) pi[j] = j;
+  for (int l = n - 1; l >= 0; --l) {
+    const HostCoupling& c = hf.layers[l];
+    gsvdec::FlowLayer& F = h->flow[l];
+    std::vector<int> q(C);
+    for (int j = 0; j < C; ++j) q[j] = pi[C - 1 - j];  // flip
+    pi = q;
+    HostConv pre;
+    pre.name = c.pre.name; pre.d0 = hid; pre.d1 = C; pre.K = 1; pre.pad = 0;
+    pre.w.assign((size_t)hid * C, 0.0f);
+    for (int o = 0; o < hid; ++o)
+      for (int j = 0; j < half; ++j) pre.w[(size_t)o * C + pi[j]] = c.pre.w[(size_t)o * half + j];
+    pre.b = c.pre.b;
+    F.pre = pk.conv(pre);
+    for (int j = 0; j < nl; ++j) F.in.push_back(pk.conv(c.in[j]));
+    for (int j = 0; j + 1 < nl; ++j) {
+      HostConv r;
+      r.name = c.rs[j].name; r.d0 = hid; r.d1 = hid; r.K = 1; r.pad = 0;
+      r.w.assign(c.rs[j].w.begin(), c.rs[j].w.begin() + (size_t)hid * hid);
+      if (!c.rs[j].b.empty()) r.b.assign(c.rs[j].b.begin(), c.rs[j].b.begin() + hid);
+      F.res.push_back(pk.conv(r));
+    }
+    // Coupling update weights and bias (double precision fold).
+    std::vector<double> cb(half, 0.0);
+    for (int i = 0; i < half; ++i) cb[i] = c.post.b.empty() ? 0.0 : c.post.b[i];
+    std::vector<std::vector<double>> wp(nl, std::vector<double>((size_t)half * hid, 0.0));
+    for (int j = 0; j < nl; ++j) {
+      const HostConv& rs = c.rs[j];
+      const int r0 = j < nl - 1 ? hid : 0;  // skip rows of res_skip j
+      for (int i = 0; i < half; ++i) {
+        for (int k = 0; k < hid; ++k) {
+          const double wpk = c.post.w[(size_t)i * hid + k];
+          if (!rs.b.empty()) cb[i] += wpk * rs.b[r0 + k];
+          const float* srow = &rs.w[(size_t)(r0 + k) * hid];
+          double* dst = &wp[j][(size_t)i * hid];
+          for (int m = 0; m < hid; ++m) dst[m] += wpk * srow[m];
+        }
+      }
+    }
+    for (int j = 0; j < nl; ++j) {
+      HostConv u;
+      u.name = c.post.name; u.d0 = C; u.d1 = hid; u.K = 1; u.pad = 0;
+      u.w.assign((size_t)C * hid, 0.0f);
+      u.b.assign(C, 0.0f);
+      for (int i = 0; i < half; ++i) {
+        const int row = pi[half + i];
+        for (int m = 0; m < hid; ++m) u.w[(size_t)row * hid + m] = (float)-wp[j][(size_t)i * hid + m];
+        if (j == 0) u.b[row] = (float)-cb[i];
+      }
+      F.post.push_back(pk.conv(u));
+    }
+    if (c.has_cond) {
+      F.has_cond = true;
+      cond_w[l] = c.cond.w;  // [2 hid n][gin][1]
+      cond_b[l] = c.cond.b.empty() ? std::vector<float>(c.cond.d0, 0.0f) : c.cond.b;
+    }
+  }
+  std::vector<int>& perm = pi;  // output channel j = physical pi[j]
+  h->flow_perm_host = perm;
+  if (h->dt == Dt::BF16) {
+    if (!h->ident_off.count(C)) h->ident_off[C] = pk.identity(C);
+    if (!h->ident_off.count(hid)) h->ident_off[hid] = pk.identity(hid);
+  }
+  return GSV_OK;
+}
 
 // Largest activation (elements per utterance) over all layers, for T0 frames.
 size_t max_act_elems(const gsvdec* h, int T0) {
@@ -792,6 +967,157 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   return GSV_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Flow inverse on device buffers.
+
+struct FlowWs {
+  void* x[2];      // [B][T][C] activations (ping-pong: the coupling update is not in place)
+  void* hb[2];     // [B][T][hid] WN residual stream (ping-pong)
+  void* xin;       // [B][T][2 hid] in_layer output
+  void* act[16];   // [B][T][hid] gated activations, one per WN layer
+  float* cond;     // [B][2 hid n] per-utterance cond projection of one coupling layer
+  int* lens;       // [B] valid frames
+  float* zstage;   // host-mode staging of z_p / g / lengths and of z
+  float* gstage;
+  int* lstage;
+  float* zout;     // [B][C][T] fp32
+};
+
+int ensure_flow_ws(gsvdec* h, int B, int T0, FlowWs& w) {
+  const size_t eb = act_bytes(h);
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t C = h->flow_C, hid = h->flow_hid, nl = h->flow_nwn;
+  const size_t bt = (size_t)B * T0;
+  size_t need = 0;
+  size_t o_x = need; need += 2 * al(bt * C * eb);
+  size_t o_h = need; need += 2 * al(bt * hid * eb);
+  size_t o_xin = need; need += al(bt * 2 * hid * eb);
+  size_t o_act = need; need += nl * al(bt * hid * eb);
+  size_t o_cond = need; need += al((size_t)B * 2 * hid * nl * 4);
+  size_t o_len = need; need += al((size_t)B * 4);
+  size_t o_zs = need; need += al(bt * C * 4);
+  size_t o_gs = need; need += al((size_t)B * std::max(h->flow_gin, 1) * 4);
+  size_t o_ls = need; need += al((size_t)B * 4);
+  size_t o_zo = need; need += al(bt * C * 4);
+  if (need > h->fws_bytes) {
+    if (h->fws) CUDA_TRY(cudaFree(h->fws));
+    h->fws = nullptr;
+    h->fws_bytes = 0;
+    CUDA_TRY(cudaMalloc(&h->fws, need));
+    h->fws_bytes = need;
+  }
+  char* p = static_cast<char*>(h->fws);
+  for (int i = 0; i < 2; ++i) {
+    w.x[i] = p + o_x + i * al(bt * C * eb);
+    w.hb[i] = p + o_h + i * al(bt * hid * eb);
+  }
+  w.xin = p + o_xin;
+  for (size_t j = 0; j < nl && j < 16; ++j) w.act[j] = p + o_act + j * al(bt * hid * eb);
+  w.cond = reinterpret_cast<float*>(p + o_cond);
+  w.lens = reinterpret_cast<int*>(p + o_len);
+  w.zstage = reinterpret_cast<float*>(p + o_zs);
+  w.gstage = reinterpret_cast<float*>(p + o_gs);
+  w.lstage = reinterpret_cast<int*>(p + o_ls);
+  w.zout = reinterpret_cast<float*>(p + o_zo);
+  return GSV_OK;
+}
+
+void begin_run(gsvdec* h, cudaStream_t st) {
+  h->launches = 0;
+  h->n_ev = 0;
+  if (h->timing >= 2) {
+    cudaEvent_t e;
+    if (!h->pool.empty()) {
+      e = h->pool.back();
+      h->pool.pop_back();
+    } else if (cudaEventCreate(&e) != cudaSuccess) {
+      return;
+    }
+    cudaEventRecord(e, st);
+    h->runs.push_back({e});
+    h->run_recs.push_back({});
+  }
+}
+
+// z = flow^-1(z_p) * y_mask (src/models/sovits_flow.rs:385-405 with reverse =
+// true, then src/models/sovits.rs:394).  zp [B][C][T0] fp32, gdev [B][gin] or
+// null, lens_in [B] or null, z_dev [B][C][T0] fp32.
+int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_in, int B, int T0,
+                float* z_dev, FlowWs& w, cudaStream_t st) {
+  begin_run(h, st);
+  const double eb = (double)act_bytes(h);
+  const int C = h->flow_C, hid = h->flow_hid, nl = h->flow_nwn;
+  const int* lens = nullptr;
+  if (lens_in) {
+    CUDA_TRY(launch_lengths(lens_in, B, T0, nullptr, nullptr, 0, w.lens, st));
+    GSV_TRY(after_launch(h, st, "flow.lengths", 1, 0, 0.0, 8.0 * B));
+    lens = w.lens;
+  }
+  CUDA_TRY(launch_transpose_in(zp, B, C, T0, 0, T0, lens, w.x[0], h->dt, st));
+  GSV_TRY(after_launch(h, st, "flow.input_relayout", 1, 0, 0.0, (4.0 + eb) * B * C * T0));
+  int cur = 0;
+  const int n = (int)h->flow.size();
+  for (int l = n - 1; l >= 0; --l) {
+    const gsvdec::FlowLayer& F = h->flow[l];
+    const std::string nm = "flow." + std::to_string(l);
+    const bool cond = F.has_cond && gdev;
+    if (cond) {
+      CUDA_TRY(launch_cond(gdev, F.d_cond_w, F.d_cond_b, B, h->flow_gin, 2 * hid * nl, w.cond, st));
+      GSV_TRY(after_launch(h, st, nm + ".cond", 1, 1, 2.0 * B * h->flow_gin * 2 * hid * nl,
+                           4.0 * ((double)B * h->flow_gin + (double)h->flow_gin * 2 * hid * nl)));
+    }
+    {
+      TapConv op = make_op(h, F.pre, B, w.x[cur], T0);
+      op.len = lens;
+      op.out_raw = w.hb[0];
+      Work wk;
+      wk.add(F.pre, B, T0, 0, eb);
+      GSV_TRY(run_one(h, op, st, nm + ".pre", wk));
+    }
+    int hc = 0;
+    for (int j = 0; j < nl; ++j) {
+      {
+        TapConv op = make_op(h, F.in[j], B, w.hb[hc], T0);
+        op.len = lens;
+        op.out_raw = w.xin;
+        Work wk;
+        wk.add(F.in[j], B, T0, 0, eb);
+        GSV_TRY(run_one(h, op, st, nm + ".in" + std::to_string(j), wk));
+      }
+      CUDA_TRY(launch_gate(w.xin, cond ? w.cond : nullptr, 2 * hid * nl, j * 2 * hid, B, T0, hid, lens,
+                           w.act[j], h->dt, st));
+      GSV_TRY(after_launch(h, st, nm + ".gate" + std::to_string(j), 1, 0, 0.0, 3.0 * eb * B * hid * T0));
+      if (j + 1 < nl) {
+        TapConv op = make_op(h, F.res[j], B, w.act[j], T0);
+        op.len = lens;
+        op.res[0] = w.hb[hc];
+        op.nres = 1;
+        op.out_raw = w.hb[hc ^ 1];
+        Work wk;
+        wk.add(F.res[j], B, T0, 1, eb);
+        GSV_TRY(run_one(h, op, st, nm + ".res" + std::to_string(j), wk));
+        hc ^= 1;
+      }
+    }
+    {
+      TapConv op = make_op(h, F.post[0], B, w.act[0], T0);
+      for (int j = 1; j < nl; ++j) op.seg[j] = make_seg(h, F.post[j], w.act[j], T0);
+      op.nseg = nl;
+      op.len = lens;
+      op.res[0] = w.x[cur];
+      op.nres = 1;
+      op.out_raw = w.x[cur ^ 1];
+      Work wk;
+      for (int j = 0; j < nl; ++j) wk.add(F.post[j], B, T0, j == 0 ? 1 : 0, eb);
+      GSV_TRY(run_one(h, op, st, nm + ".couple", wk));
+      cur ^= 1;
+    }
+  }
+  CUDA_TRY(launch_to_ncl(w.x[cur], h->dt, B, T0, C, z_dev, st, h->d_flow_perm));
+  GSV_TRY(after_launch(h, st, "flow.output_relayout", 1, 0, 0.0, (4.0 + eb) * B * C * T0));
+  return GSV_OK;
+}
+
 // A kernel whose bounded wait gave up leaves a non-zero word in d_err.
 int check_device_error(gsvdec* h) {
   int v = 0;
@@ -909,6 +1235,29 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     }
     if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the bf16 tcgen05 kernel");
   }
+  // The flow (optional), packed into the same weight arena.
+  HostFlow hf;
+  GSV_TRY(load_flow(ts, n, "flow.flows", hf));
+  std::vector<std::vector<float>> flow_cond_w, flow_cond_b;
+  if (!hf.layers.empty()) {
+    GSV_TRY(pack_flow(h.get(), pk, hf, flow_cond_w, flow_cond_b));
+    if (h->dt == Dt::BF16) {
+      auto ok = [&](const GemmConv& g) {
+        TapConv op{};
+        op.nseg = 1; op.seg[0].Cin = g.Cin; op.seg[0].ntaps = g.ntaps; op.seg[0].offstep = g.offstep;
+        op.seg[0].off0 = g.off0; op.N = g.N; op.Cout = g.Cout;
+        return tapconv_tc_supported(op);
+      };
+      bool all = true;
+      for (auto& F : h->flow) {
+        all = all && ok(F.pre);
+        for (auto& g : F.in) all = all && ok(g);
+        for (auto& g : F.res) all = all && ok(g);
+        for (auto& g : F.post) all = all && ok(g);
+      }
+      if (!all) return set_err(GSV_E_UNSUPPORTED, "a flow layer geometry is not supported by the bf16 tcgen05 kernel");
+    }
+  }
   h->layer_names += m.post.name + "\n";
   h->post_K = m.post.K;
   h->post_pad = m.post.pad;
@@ -939,6 +1288,20 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     CUDA_TRY(cudaMalloc(&h->d_cond_b, sizeof(float) * cb.size()));
     CUDA_TRY(cudaMemcpy(h->d_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
+  for (size_t l = 0; l < h->flow.size(); ++l) {
+    if (!h->flow[l].has_cond) continue;
+    CUDA_TRY(cudaMalloc(&h->flow[l].d_cond_w, sizeof(float) * flow_cond_w[l].size()));
+    CUDA_TRY(cudaMemcpy(h->flow[l].d_cond_w, flow_cond_w[l].data(), sizeof(float) * flow_cond_w[l].size(),
+                        cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMalloc(&h->flow[l].d_cond_b, sizeof(float) * flow_cond_b[l].size()));
+    CUDA_TRY(cudaMemcpy(h->flow[l].d_cond_b, flow_cond_b[l].data(), sizeof(float) * flow_cond_b[l].size(),
+                        cudaMemcpyHostToDevice));
+  }
+  if (!h->flow.empty()) {
+    CUDA_TRY(cudaMalloc(&h->d_flow_perm, sizeof(int) * h->flow_perm_host.size()));
+    CUDA_TRY(cudaMemcpy(h->d_flow_perm, h->flow_perm_host.data(), sizeof(int) * h->flow_perm_host.size(),
+                        cudaMemcpyHostToDevice));
+  }
   CUDA_TRY(cudaMalloc(&h->d_err, sizeof(int)));
   CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
   for (auto& e : h->ev) CUDA_TRY(cudaEventCreate(&e));
@@ -958,6 +1321,12 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->d_err);
   cudaFree(h->ws);
   cudaFree(h->lws);
+  cudaFree(h->fws);
+  cudaFree(h->d_flow_perm);
+  for (auto& F : h->flow) {
+    cudaFree(F.d_cond_w);
+    cudaFree(F.d_cond_b);
+  }
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
   for (auto& run : h->runs)
@@ -1094,6 +1463,67 @@ int layer_impl(gsvdec* h, const char* name, const float* x, int B, int L, float*
   return GSV_OK;
 }
 
+// Flow inverse (and, with `decode`, the decoder after it) through host or
+// device buffers.
+int flow_impl(gsvdec* h, const float* zp, const float* g, const int32_t* lengths, int B, int T0,
+              float* out, int mem_kind, cudaStream_t st, bool decode) {
+  if (!h) return set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (h->flow.empty()) return set_err(GSV_E_UNSUPPORTED, "this handle was created without flow.flows.* tensors");
+  if (!zp || !out) return set_err(GSV_E_INVALID_ARG, "z_p and the output must not be NULL");
+  if (B <= 0 || T0 <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+    return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
+  if (decode && h->flow_C != h->in_ch)
+    return set_err(GSV_E_SHAPE, "flow width %d != decoder input width %d", h->flow_C, h->in_ch);
+  if ((int64_t)B * T0 * std::max(h->flow_C, 2 * h->flow_hid) > (int64_t)1 << 36)
+    return set_err(GSV_E_INVALID_ARG, "request too large");
+  CUDA_TRY(cudaSetDevice(h->device));
+  FlowWs fw;
+  GSV_TRY(ensure_flow_ws(h, B, T0, fw));
+  const float* zd = zp;
+  const float* gd = g;
+  const int* ld = lengths;
+  if (mem_kind == GSV_MEM_HOST) {
+    CUDA_TRY(cudaMemcpyAsync(fw.zstage, zp, sizeof(float) * (size_t)B * h->flow_C * T0, cudaMemcpyHostToDevice, st));
+    zd = fw.zstage;
+    if (g && h->flow_gin > 0) {
+      CUDA_TRY(cudaMemcpyAsync(fw.gstage, g, sizeof(float) * (size_t)B * h->flow_gin, cudaMemcpyHostToDevice, st));
+      gd = fw.gstage;
+    }
+    if (lengths) {
+      CUDA_TRY(cudaMemcpyAsync(fw.lstage, lengths, sizeof(int) * (size_t)B, cudaMemcpyHostToDevice, st));
+      ld = fw.lstage;
+    }
+  }
+  if (h->flow_gin == 0) gd = nullptr;
+  float* zout = (!decode && mem_kind == GSV_MEM_DEVICE) ? out : fw.zout;
+  GSV_TRY(flow_device(h, zd, gd, ld, B, T0, zout, fw, st));
+  if (!decode) {
+    if (mem_kind == GSV_MEM_HOST) {
+      CUDA_TRY(cudaMemcpyAsync(out, zout, sizeof(float) * (size_t)B * h->flow_C * T0, cudaMemcpyDeviceToHost, st));
+      CUDA_TRY(cudaStreamSynchronize(st));
+      GSV_TRY(check_device_error(h));
+    }
+    return GSV_OK;
+  }
+  // The decoder reads the same g (src/models/sovits.rs:391-400; gin must match).
+  const float* gdec = (h->has_cond && gd && h->gin == h->flow_gin) ? gd : nullptr;
+  if (h->has_cond && gd && h->gin != h->flow_gin)
+    return set_err(GSV_E_SHAPE, "flow cond width %d != decoder cond width %d", h->flow_gin, h->gin);
+  Workspace w;
+  GSV_TRY(ensure_ws(h, B, T0, false, w));
+  const int L = out_len(h, T0);
+  float* wd = mem_kind == GSV_MEM_DEVICE ? out : w.wav;
+  GSV_TRY(forward_device(h, zout, T0, 0, gdec, ld, B, T0, wd, w, nullptr, st));
+  if (mem_kind == GSV_MEM_HOST) {
+    CUDA_TRY(cudaMemcpyAsync(out, wd, sizeof(float) * (size_t)B * L, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    GSV_TRY(check_device_error(h));
+  }
+  GSV_TRY(collect_timing(h, st));
+  return GSV_OK;
+}
+
 }  // namespace
 }  // namespace gsv
 
@@ -1120,10 +1550,10 @@ int gsvdec_create_from_file(const char* path, int mode, int device, gsvdec_t** o
     gsv::StFile f;
     std::string err;
     if (!f.open(path, err)) return gsv::set_err(GSV_E_INVALID_ARG, "%s", err.c_str());
-    // Only the decoder's tensors; float dtypes as in src/utils/weights.rs:140-151.
+    // The decoder's tensors and the flow's; float dtypes as in src/utils/weights.rs:140-151.
     std::vector<gsvdec_tensor> ts;
     for (const gsv::StEntry& e : f.entries()) {
-      if (e.name.compare(0, 4, "dec.") != 0) continue;
+      if (e.name.compare(0, 4, "dec.") != 0 && e.name.compare(0, 11, "flow.flows.") != 0) continue;
       gsvdec_tensor t{};
       t.name = e.name.c_str();
       if (e.dtype == "F32") t.dtype = GSV_DTYPE_F32;
@@ -1211,6 +1641,23 @@ int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int 
   const int64_t L = gsv::out_len(h, T0 > 0 ? T0 : 1);
   return gsv::forward_impl(h, z, g, nullptr, B, T0, 0, T0, wav, GSV_MEM_HOST, nullptr, taps, 0,
                            (int64_t)B * L);
+}
+
+int gsvdec_flow_info(const gsvdec_t* h, int* n_couplings, int* channels) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (n_couplings) *n_couplings = (int)h->flow.size();
+  if (channels) *channels = h->flow_C;
+  return GSV_OK;
+}
+
+int gsvdec_flow_inverse(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths, int B,
+                        int T0, float* z, int mem_kind, void* stream) {
+  return gsv::flow_impl(h, z_p, g, lengths, B, T0, z, mem_kind, static_cast<cudaStream_t>(stream), false);
+}
+
+int gsvdec_flow_decode(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths, int B,
+                       int T0, float* wav, int mem_kind, void* stream) {
+  return gsv::flow_impl(h, z_p, g, lengths, B, T0, wav, mem_kind, static_cast<cudaStream_t>(stream), true);
 }
 
 int gsvdec_layer_forward(gsvdec_t* h, const char* layer, const float* x, int B, int L, float* y,

@@ -4,6 +4,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
 
@@ -209,10 +211,20 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
 }
 
 template <typename T>
-__global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __restrict__ y) {
+__global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __restrict__ y,
+                              const int* __restrict__ perm) {
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  if (perm != nullptr) {
+    // Permuted channels: output channel c reads input channel perm[c]
+    // (gathered directly; used for the flow's small output).
+    for (int i = threadIdx.y; i < 32; i += 8) {
+      const int c = c0 + i, t = t0 + threadIdx.x;
+      if (c < C && t < L) y[((size_t)b * C + c) * L + t] = ld_act<T>(x, ((size_t)b * L + t) * C + perm[c]);
+    }
+    return;
+  }
   for (int i = threadIdx.y; i < 32; i += 8) {
     const int t = t0 + i, c = c0 + threadIdx.x;
     tile[i][threadIdx.x] = (t < L && c < C) ? ld_act<T>(x, ((size_t)b * L + t) * C + c) : 0.0f;
@@ -221,6 +233,37 @@ __global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __re
   for (int i = threadIdx.y; i < 32; i += 8) {
     const int c = c0 + i, t = t0 + threadIdx.x;
     if (c < C && t < L) y[((size_t)b * C + c) * L + t] = tile[threadIdx.x][i];
+  }
+}
+
+// WN gated activation, 8 channels per thread.
+template <typename T>
+__global__ void gate_kernel(const T* __restrict__ xin, const float* __restrict__ cond, int cond_ld,
+                            int cond_off, int B, int L, int H, const int* __restrict__ len,
+                            T* __restrict__ out) {
+  const int groups = H / 8;
+  const long long total = (long long)B * L * groups;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int cg = (int)(i % groups);
+    const long long bt = i / groups;
+    const int b = (int)(bt / L), t = (int)(bt % L);
+    const bool live = len == nullptr || t < len[b];
+    const T* row = xin + bt * 2 * H;
+    const float* g = cond ? cond + (size_t)b * cond_ld + cond_off : nullptr;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = cg * 8 + e;
+      float a = ld_act<T>(row, c), s = ld_act<T>(row, H + c);
+      if (g) {
+        a = a + g[c];
+        s = s + g[H + c];
+      }
+      o[e] = live ? tanhf(a) * (1.0f / (1.0f + expf(-s))) : 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) st_act<T>(out, bt * H + cg * 8 + e, o[e]);
   }
 }
 
@@ -277,13 +320,29 @@ cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* 
   return cudaGetLastError();
 }
 
-cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st) {
+cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st,
+                          const int* perm) {
   dim3 grid(cdiv(L, 32), cdiv(C, 32), B), block(32, 8);
   if (dt == Dt::F32)
-    to_ncl_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(x), L, C, y);
+    to_ncl_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(x), L, C, y, perm);
   else
     to_ncl_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(x), L,
-                                                         C, y);
+                                                         C, y, perm);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gate(const void* xin, const float* cond, int cond_ld, int cond_off, int B, int L,
+                        int H, const int* len, void* out, Dt dt, cudaStream_t st) {
+  if (H % 8 || B <= 0 || L <= 0) return cudaErrorInvalidValue;
+  const long long total = (long long)B * L * (H / 8);
+  const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
+  if (dt == Dt::F32)
+    gate_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(xin), cond, cond_ld, cond_off, B, L,
+                                             H, len, static_cast<float*>(out));
+  else
+    gate_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(xin), cond, cond_ld,
+                                                     cond_off, B, L, H, len,
+                                                     static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
 

@@ -127,6 +127,28 @@ int gsvdec_forward_chunk(gsvdec_t* h, const float* z, const float* g, int T0, in
 int gsvdec_forward_taps(gsvdec_t* h, const float* z, const float* g, int B, int T0,
                         float* wav, float* const* taps, int n_taps);
 
+/* Flow inverse of the SoVITS v2 model, present when gsvdec_create received
+ * flow.flows.* tensors (ResidualCouplingBlock::load, src/models/sovits_flow.rs:
+ * 346-368; the layer list of ResidualCouplingLayer::load :186-223 and WN::load
+ * :19-109).  *n_couplings = 0 when the handle has no flow. */
+int gsvdec_flow_info(const gsvdec_t* h, int* n_couplings, int* channels);
+
+/* z = flow^-1(z_p) * y_mask: ResidualCouplingBlock::forward(x, x_mask, g,
+ * reverse = true) (src/models/sovits_flow.rs:385-405) followed by
+ * z.broadcast_mul(&y_mask) (src/models/sovits.rs:391-394).  z_p and z are
+ * [B, C, T0] fp32 (C = 192), g [B, gin, 1] or NULL (no conditioning),
+ * lengths [B] valid frames or NULL (all T0: y_mask of ones).  Host or device
+ * pointers per mem_kind.  Only mean-only coupling layers (post with C/2
+ * outputs, as in v2) are supported (GSV_E_UNSUPPORTED otherwise). */
+int gsvdec_flow_inverse(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths,
+                        int B, int T0, float* z, int mem_kind, void* stream);
+
+/* The flow inverse and then the decoder on its output with the same g and
+ * lengths -- the sequence at src/models/sovits.rs:389-400 -- in one call:
+ * z_p [B, C, T0] -> wav [B, hop * T0]. */
+int gsvdec_flow_decode(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths,
+                       int B, int T0, float* wav, int mem_kind, void* stream);
+
 /* One conv layer of the Generator, named by its dec.* prefix ("dec.conv_pre",
  * "dec.ups.3", "dec.resblocks.7.convs1.2", "dec.conv_post", ...; see
  * gsvdec_layer_names), on x [B, Cin, L] -> y [B, Cout, Lout] in the
