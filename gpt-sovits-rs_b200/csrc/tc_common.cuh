@@ -247,9 +247,13 @@ bool encode_w(CUtensorMap* m, const void* w, int rows, int Cin, int ck, int nt) 
 }
 
 int ck_for(int cin) { return cin % 64 == 0 ? 64 : (cin == 32 ? 32 : (cin == 16 ? 16 : 0)); }
+// Column tile of an N-column GEMM: the widest of 256 / 128 / 64 that divides N
+// (N = 192 or 384 tile by 64 / 128), else N itself for the 16/32-column convs.
 int nt_for(int n) {
-  if (n <= 256) return (n % 16 == 0 && n >= 16) ? n : 0;
-  return n % 256 == 0 ? 256 : (n % 128 == 0 ? 128 : 0);
+  if (n % 256 == 0) return 256;
+  if (n % 128 == 0) return 128;
+  if (n % 64 == 0) return 64;
+  return (n == 32 || n == 16) ? n : 0;
 }
 
 int window_rows(const TapSeg& s) { return kM + (s.ntaps - 1) * abs(s.offstep); }
