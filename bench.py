@@ -268,6 +268,77 @@ def run_sweep(args):
     dec.close()
 
 
+def run_flow(args):
+    """The flow inverse before the decoder (ResidualCouplingBlock reverse +
+    y_mask, src/models/sovits.rs:389-394) at B x T0 frames on one GPU: the flow
+    alone and flow + decoder, device-resident inputs, CUDA events around K
+    steps; the flow's layer-weighted roofline from per-launch events; the CPU
+    oracle on one utterance as the baseline."""
+    import torch
+    gsv = load_pkg()
+    pk, pk_kind = peaks()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    sd.update(gsv.synth.make_flow_state_dict(init="n001", bias="zero"))
+    B, T0 = args.batch, args.frames
+    rng = np.random.default_rng(21)
+    zp = rng.standard_normal((B, 192, T0)).astype(np.float32)
+    g = rng.standard_normal((B, 512, 1)).astype(np.float32)
+    dec = gsv.Decoder.load(sd, device=0, mode=args.mode)
+    secs = audio_seconds(B, T0, dec.hop)
+    zd, gd = torch.from_numpy(zp).cuda(), torch.from_numpy(g).cuda()
+    zo = torch.empty_like(zd)
+    wav = torch.empty(B * T0 * dec.hop, device="cuda", dtype=torch.float32)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    ms_flow = timed(lambda: dec.flow_inverse_device(zd, gd, out=zo))
+    ms_both = timed(lambda: dec.flow_decode_device(zd, gd, out=wav))
+    dec.set_stage_timing(2)
+    for _ in range(3):
+        dec.flow_inverse_device(zd, gd, out=zo)
+    torch.cuda.synchronize()
+    stats = dec.launch_stats()
+    dec.set_stage_timing(0)
+    roof_s, meas_s, rows = layer_roofline(stats, args.mode, pk)
+    if args.layers:
+        for r in rows:
+            log(f"{r['name']:<22s} {r['ms']:9.4f} ms  roof {r['roof_ms']:9.4f} ms  frac {r['frac']}  {r['bound']}")
+    flops = sum(s["flops"] for s in stats if s["kind"] == 0)
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        one = zp[:1, :, :T0]
+        t0 = time.perf_counter()
+        oracle.flow_inverse(sd, one, g[:1], None, acc64=False)
+        dt = time.perf_counter() - t0
+        cpu = {"value": audio_seconds(1, T0, dec.hop) / dt, "unit": UNIT, "cores": oracle.num_threads(),
+               "kind": "port", "sample": f"1 utterance of {T0 / 50:g} s (z_p [1,192,{T0}]), C restatement "
+                                         "of the reference flow, float accumulation"}
+    print(json.dumps({
+        "metric": f"flow inverse audio-sec/sec at B={B}x{T0 / 50:g} s {args.mode}",
+        "value": secs / (ms_flow / 1e3), "unit": UNIT, "ms_per_step": ms_flow, "steps": args.steps,
+        "warmup": args.warmup, "dtype": args.mode, "data": "synthetic: seeded N(0,1) z_p/g, N(0,0.01) "
+        "random-init weights, zero bias",
+        "config": {"workload": f"flow inverse + y_mask, z_p [{B},192,{T0}] (4 coupling layers, WN 4 x k5)",
+                   "batch": B, "frames": T0, "mode": args.mode},
+        "flow_plus_decode": {"value": secs / (ms_both / 1e3), "unit": UNIT, "ms_per_step": ms_both},
+        "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
+                           "sum_meas_ms": 1e3 * meas_s, "conv_tflops": flops / meas_s / 1e12 if meas_s else None,
+                           "peaks": pk_kind},
+        "launches": len(stats), "cpu_baseline": cpu}), flush=True)
+    dec.close()
+
+
 def run_sharded(args, ws, rank, local):
     """Strong-scaling workloads over torch.distributed (NCCL): every rank gets the
     same inputs, decodes its share and the finished waveform pieces are gathered
@@ -373,10 +444,11 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
-    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60"), default="batch16",
+    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60", "flow"), default="batch16",
                     help="batch16: 16 x 10 s per GPU (weak scaling, the headline); varlen256: "
                          "256 utterances of 2-20 s sharded by utterance (strong scaling); long60: "
-                         "one 60 s utterance split in halo time chunks (strong scaling)")
+                         "one 60 s utterance split in halo time chunks (strong scaling); flow: the "
+                         "flow inverse before the decoder (and flow + decoder), one GPU")
     ap.add_argument("--sweep", action="store_true",
                     help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
                          "x --frames, in --mode; prints one JSON line per mode")
@@ -391,6 +463,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.workload == "flow":
+        run_flow(args)
         return
     if args.workload != "batch16":
         run_sharded(args, ws, rank, local)

@@ -693,6 +693,15 @@ struct Work {
     bytes += by;
     nconv++;
   }
+  // A reference conv Cin -> Cout, k taps, over L frames (unfused layer I/O).
+  void add_ref(int Cin, int Cout, int k, int L, int B, double e) {
+    const double f = 2.0 * Cin * Cout * k * (double)L * B;
+    const double by = e * B * ((double)Cin + Cout) * L + e * (double)Cin * Cout * k;
+    if (nconv < 6) { cf[nconv] = f; cb[nconv] = by; }
+    flops += f;
+    bytes += by;
+    nconv++;
+  }
 };
 
 constexpr int kIdentityResidualMinC = 32;
@@ -1071,7 +1080,7 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
       op.len = lens;
       op.out_raw = w.hb[0];
       Work wk;
-      wk.add(F.pre, B, T0, 0, eb);
+      wk.add_ref(h->flow_half, hid, 1, T0, B, eb);  // pre reads x0 only
       GSV_TRY(run_one(h, op, st, nm + ".pre", wk));
     }
     int hc = 0;
@@ -1094,7 +1103,7 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
         op.nres = 1;
         op.out_raw = w.hb[hc ^ 1];
         Work wk;
-        wk.add(F.res[j], B, T0, 1, eb);
+        wk.add_ref(hid, 2 * hid, 1, T0, B, eb);  // res_skip j (its skip half is folded into the update)
         GSV_TRY(run_one(h, op, st, nm + ".res" + std::to_string(j), wk));
         hc ^= 1;
       }
@@ -1108,7 +1117,8 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
       op.nres = 1;
       op.out_raw = w.x[cur ^ 1];
       Work wk;
-      for (int j = 0; j < nl; ++j) wk.add(F.post[j], B, T0, j == 0 ? 1 : 0, eb);
+      wk.add_ref(hid, hid, 1, T0, B, eb);                 // the last res_skip (skip only)
+      wk.add_ref(hid, h->flow_half, 1, T0, B, eb);        // post
       GSV_TRY(run_one(h, op, st, nm + ".couple", wk));
       cur ^= 1;
     }

@@ -365,18 +365,11 @@ cudaError_t launch_c(RbParams& P, cudaStream_t st) {
                       (P.len_smem ? sizeof(int) * (size_t)P.B : 0);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = rbstep_kernel<C>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  int nregs = 0;
+  cudaError_t e = kernel_setup(kern, smem, &nregs);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared);
-  if (e != cudaSuccess) return e;
-  int dev = 0, smem_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, kern);
-  if (e != cudaSuccess) return e;
-  const int regs_cta = ((fa.numRegs * 32 + 255) / 256 * 256) * (kRbThreads / 32);
+  const int smem_sm = smem_per_sm();
+  const int regs_cta = ((nregs * 32 + 255) / 256 * 256) * (kRbThreads / 32);
   const int per_sm = std::max(1, std::min({smem_sm / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
                                            2048 / kRbThreads, (int)(512 / S::kTmemCols)}));
   // Split the persistent CTAs over the branches in proportion to their tiles.

@@ -710,20 +710,13 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
                       (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                           cudaSharedmemCarveoutMaxShared);
-  if (e != cudaSuccess) return e;
   // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
   // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
-  int dev = 0, smem_sm = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-  cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, kern);
+  int nregs = 0;
+  cudaError_t e = kernel_setup(kern, smem, &nregs);
   if (e != cudaSuccess) return e;
-  const int regs_cta = ((fa.numRegs * 32 + 255) / 256 * 256) * (kThreads / 32);
+  const int smem_sm = smem_per_sm();
+  const int regs_cta = ((nregs * 32 + 255) / 256 * 256) * (kThreads / 32);
   int per_sm = std::min({smem_sm / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
                          2048 / kThreads, (int)(512 / S::kTmemCols)});
   per_sm = std::max(1, per_sm);

@@ -275,5 +275,64 @@ int sm_count() {
   return cached[dev];
 }
 
+int smem_per_sm() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 228 * 1024;
+  if (!cached[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cached[dev] = n > 0 ? n : 228 * 1024;
+  }
+  return cached[dev];
+}
+
+// Launch setup of a kernel done once per (kernel, device) instead of per
+// launch: the shared-memory carveout, the register count, and the dynamic
+// shared-memory limit (raised only when a launch needs more).  Short launches
+// (the flow's) were bound by these host calls.
+template <typename K>
+cudaError_t kernel_setup(K kern, size_t smem, int* regs) {
+  struct Entry {
+    int regs = 0, smem = 0;
+    bool ready = false;
+  };
+  static std::mutex mu;
+  static Entry table[64][8];
+  static const void* keys[64][8] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* en = nullptr;
+  for (int i = 0; i < 8 && !en; ++i) {
+    if (keys[dev][i] == (const void*)kern) en = &table[dev][i];
+    else if (!keys[dev][i]) {
+      keys[dev][i] = (const void*)kern;
+      en = &table[dev][i];
+    }
+  }
+  Entry scratch;
+  if (!en) en = &scratch;  // more than 8 instantiations on one device: no caching
+  if (!en->ready) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                         cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    en->regs = fa.numRegs;
+    en->ready = true;
+  }
+  if ((int)smem > en->smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    en->smem = (int)smem;
+  }
+  *regs = en->regs;
+  return cudaSuccess;
+}
+
 }  // namespace
 }  // namespace gsv
