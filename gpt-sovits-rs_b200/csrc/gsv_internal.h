@@ -58,6 +58,11 @@ struct TapConv {
   float slope;           // LeakyReLU slope of out_act
   const int* len;        // [B] valid output rows, or null
   int row_tiles;         // tiles per utterance along q (set by the launcher)
+  int bias_bc_ld;        // row stride of bias_bc (0: Cout)
+  // Gated-activation epilogue (bf16 tcgen05 only): the N = 2H GEMM columns are
+  // interleaved in 16-column (a, b) pairs and the op writes
+  // out_raw[b][q][H] = tanh(a + bias + bias_bc) * sigmoid(b + bias + bias_bc).
+  int gate;
 };
 
 struct TapConvGroup {

@@ -440,10 +440,11 @@ struct gsvdec {
     std::vector<GemmConv> in;      // WN in_layers, hid -> 2 hid, k taps
     std::vector<GemmConv> res;     // residual halves of res_skip 0 .. n-2, hid -> hid
     std::vector<GemmConv> post;    // coupling update, one segment per WN layer, hid -> C
-    float* d_cond_w = nullptr;     // [2 hid n][gin]
-    float* d_cond_b = nullptr;
     bool has_cond = false;
   };
+  float* d_flow_cond_w = nullptr;  // every layer's cond_layer stacked: [layers * 2 hid n][gin]
+  float* d_flow_cond_b = nullptr;
+  bool flow_gate_fused = false;    // bf16: the WN gate runs in the in_layer GEMM's epilogue
   std::vector<FlowLayer> flow;
   int flow_C = 0, flow_half = 0, flow_hid = 0, flow_nwn = 0, flow_gin = 0;
   int* d_flow_perm = nullptr;      // physical channel of each output channel
@@ -456,6 +457,14 @@ namespace gsv {
 namespace {
 
 size_t act_bytes(const gsvdec* h) { return h->dt == Dt::F32 ? 4 : 2; }
+
+// GEMM column col of a fused-gate in_layer holds original channel gate_src:
+// column 32p + r is tanh-half channel 16p + r (r < 16), else sigmoid-half
+// channel hid + 16p + (r - 16).
+int gate_src(int col, int hid) {
+  const int p = col / 32, r = col % 32;
+  return r < 16 ? 16 * p + r : hid + 16 * p + (r - 16);
+}
 
 // Packs the flow for the inverse direction (ResidualCouplingBlock::forward
 // with reverse = true, src/models/sovits_flow.rs:385-405).  With the
@@ -492,6 +501,7 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
   }
   const int n = (int)hf.layers.size();
   h->flow.assign(n, {});
+  h->flow_gate_fused = h->dt == Dt::BF16 && hid % 16 == 0;
   h->flow_C = C; h->flow_half = half; h->flow_hid = hid; h->flow_nwn = nl; h->flow_gin = gin;
   cond_w.assign(n, {});
   cond_b.assign(n, {});
@@ -510,7 +520,23 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
       for (int j = 0; j < half; ++j) pre.w[(size_t)o * C + pi[j]] = c.pre.w[(size_t)o * half + j];
     pre.b = c.pre.b;
     F.pre = pk.conv(pre);
-    for (int j = 0; j < nl; ++j) F.in.push_back(pk.conv(c.in[j]));
+    for (int j = 0; j < nl; ++j) {
+      if (!h->flow_gate_fused) {
+        F.in.push_back(pk.conv(c.in[j]));
+        continue;
+      }
+      // Columns interleaved in 16-channel (tanh half, sigmoid half) pairs, so
+      // one 32-column epilogue run holds both halves of 16 outputs.
+      HostConv a = c.in[j];
+      const size_t per = (size_t)a.d1 * a.K;
+      for (int col = 0; col < 2 * hid; ++col) {
+        const int src = gate_src(col, hid);
+        std::copy(c.in[j].w.begin() + (size_t)src * per, c.in[j].w.begin() + (size_t)(src + 1) * per,
+                  a.w.begin() + (size_t)col * per);
+        if (!a.b.empty()) a.b[col] = c.in[j].b[src];
+      }
+      F.in.push_back(pk.conv(a));
+    }
     for (int j = 0; j + 1 < nl; ++j) {
       HostConv r;
       r.name = c.rs[j].name; r.d0 = hid; r.d1 = hid; r.K = 1; r.pad = 0;
@@ -549,8 +575,17 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
     }
     if (c.has_cond) {
       F.has_cond = true;
-      cond_w[l] = c.cond.w;  // [2 hid n][gin][1]
-      cond_b[l] = c.cond.b.empty() ? std::vector<float>(c.cond.d0, 0.0f) : c.cond.b;
+      // [2 hid n][gin][1]; with the fused gate each WN layer's 2 hid rows are
+      // interleaved like its in_layer columns.
+      cond_w[l].resize(c.cond.w.size());
+      cond_b[l].assign(c.cond.d0, 0.0f);
+      for (int r = 0; r < c.cond.d0; ++r) {
+        const int j = r / (2 * hid), col = r % (2 * hid);
+        const int src = j * 2 * hid + (h->flow_gate_fused ? gate_src(col, hid) : col);
+        std::copy(c.cond.w.begin() + (size_t)src * gin, c.cond.w.begin() + (size_t)(src + 1) * gin,
+                  cond_w[l].begin() + (size_t)r * gin);
+        if (!c.cond.b.empty()) cond_b[l][r] = c.cond.b[src];
+      }
     }
   }
   std::vector<int>& perm = pi;  // output channel j = physical pi[j]
@@ -984,7 +1019,7 @@ struct FlowWs {
   void* hb[2];     // [B][T][hid] WN residual stream (ping-pong)
   void* xin;       // [B][T][2 hid] in_layer output
   void* act[16];   // [B][T][hid] gated activations, one per WN layer
-  float* cond;     // [B][2 hid n] per-utterance cond projection of one coupling layer
+  float* cond;     // [B][layers * 2 hid n] per-utterance cond projections of every coupling layer
   int* lens;       // [B] valid frames
   float* zstage;   // host-mode staging of z_p / g / lengths and of z
   float* gstage;
@@ -1002,7 +1037,7 @@ int ensure_flow_ws(gsvdec* h, int B, int T0, FlowWs& w) {
   size_t o_h = need; need += 2 * al(bt * hid * eb);
   size_t o_xin = need; need += al(bt * 2 * hid * eb);
   size_t o_act = need; need += nl * al(bt * hid * eb);
-  size_t o_cond = need; need += al((size_t)B * 2 * hid * nl * 4);
+  size_t o_cond = need; need += al((size_t)B * 2 * hid * nl * h->flow.size() * 4);
   size_t o_len = need; need += al((size_t)B * 4);
   size_t o_zs = need; need += al(bt * C * 4);
   size_t o_gs = need; need += al((size_t)B * std::max(h->flow_gin, 1) * 4);
@@ -1066,15 +1101,17 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
   GSV_TRY(after_launch(h, st, "flow.input_relayout", 1, 0, 0.0, (4.0 + eb) * B * C * T0));
   int cur = 0;
   const int n = (int)h->flow.size();
+  const int cond_ld = 2 * hid * nl * n;  // every layer's projection in one row per utterance
+  const bool cond = h->d_flow_cond_w && gdev;
+  if (cond) {
+    CUDA_TRY(launch_cond(gdev, h->d_flow_cond_w, h->d_flow_cond_b, B, h->flow_gin, cond_ld, w.cond, st));
+    GSV_TRY(after_launch(h, st, "flow.cond", 1, 1, 2.0 * B * h->flow_gin * cond_ld,
+                         4.0 * ((double)B * h->flow_gin + (double)h->flow_gin * cond_ld)));
+  }
   for (int l = n - 1; l >= 0; --l) {
     const gsvdec::FlowLayer& F = h->flow[l];
     const std::string nm = "flow." + std::to_string(l);
-    const bool cond = F.has_cond && gdev;
-    if (cond) {
-      CUDA_TRY(launch_cond(gdev, F.d_cond_w, F.d_cond_b, B, h->flow_gin, 2 * hid * nl, w.cond, st));
-      GSV_TRY(after_launch(h, st, nm + ".cond", 1, 1, 2.0 * B * h->flow_gin * 2 * hid * nl,
-                           4.0 * ((double)B * h->flow_gin + (double)h->flow_gin * 2 * hid * nl)));
-    }
+    const int coff = l * 2 * hid * nl;
     {
       TapConv op = make_op(h, F.pre, B, w.x[cur], T0);
       op.len = lens;
@@ -1088,14 +1125,23 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
       {
         TapConv op = make_op(h, F.in[j], B, w.hb[hc], T0);
         op.len = lens;
-        op.out_raw = w.xin;
         Work wk;
         wk.add(F.in[j], B, T0, 0, eb);
-        GSV_TRY(run_one(h, op, st, nm + ".in" + std::to_string(j), wk));
+        if (h->flow_gate_fused) {
+          // in_layer + cond + tanh * sigmoid in one launch (gated epilogue).
+          op.gate = 1;
+          op.out_raw = w.act[j];
+          op.bias_bc = cond ? w.cond + coff + j * 2 * hid : nullptr;
+          op.bias_bc_ld = cond_ld;
+          GSV_TRY(run_one(h, op, st, nm + ".in" + std::to_string(j) + "+gate", wk));
+        } else {
+          op.out_raw = w.xin;
+          GSV_TRY(run_one(h, op, st, nm + ".in" + std::to_string(j), wk));
+          CUDA_TRY(launch_gate(w.xin, cond ? w.cond : nullptr, cond_ld, coff + j * 2 * hid, B, T0, hid, lens,
+                               w.act[j], h->dt, st));
+          GSV_TRY(after_launch(h, st, nm + ".gate" + std::to_string(j), 1, 0, 0.0, 3.0 * eb * B * hid * T0));
+        }
       }
-      CUDA_TRY(launch_gate(w.xin, cond ? w.cond : nullptr, 2 * hid * nl, j * 2 * hid, B, T0, hid, lens,
-                           w.act[j], h->dt, st));
-      GSV_TRY(after_launch(h, st, nm + ".gate" + std::to_string(j), 1, 0, 0.0, 3.0 * eb * B * hid * T0));
       if (j + 1 < nl) {
         TapConv op = make_op(h, F.res[j], B, w.act[j], T0);
         op.len = lens;
@@ -1298,14 +1344,16 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     CUDA_TRY(cudaMalloc(&h->d_cond_b, sizeof(float) * cb.size()));
     CUDA_TRY(cudaMemcpy(h->d_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
-  for (size_t l = 0; l < h->flow.size(); ++l) {
-    if (!h->flow[l].has_cond) continue;
-    CUDA_TRY(cudaMalloc(&h->flow[l].d_cond_w, sizeof(float) * flow_cond_w[l].size()));
-    CUDA_TRY(cudaMemcpy(h->flow[l].d_cond_w, flow_cond_w[l].data(), sizeof(float) * flow_cond_w[l].size(),
-                        cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMalloc(&h->flow[l].d_cond_b, sizeof(float) * flow_cond_b[l].size()));
-    CUDA_TRY(cudaMemcpy(h->flow[l].d_cond_b, flow_cond_b[l].data(), sizeof(float) * flow_cond_b[l].size(),
-                        cudaMemcpyHostToDevice));
+  if (!h->flow.empty() && h->flow[0].has_cond) {
+    std::vector<float> cw, cb;
+    for (size_t l = 0; l < h->flow.size(); ++l) {
+      cw.insert(cw.end(), flow_cond_w[l].begin(), flow_cond_w[l].end());
+      cb.insert(cb.end(), flow_cond_b[l].begin(), flow_cond_b[l].end());
+    }
+    CUDA_TRY(cudaMalloc(&h->d_flow_cond_w, sizeof(float) * cw.size()));
+    CUDA_TRY(cudaMemcpy(h->d_flow_cond_w, cw.data(), sizeof(float) * cw.size(), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMalloc(&h->d_flow_cond_b, sizeof(float) * cb.size()));
+    CUDA_TRY(cudaMemcpy(h->d_flow_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
   if (!h->flow.empty()) {
     CUDA_TRY(cudaMalloc(&h->d_flow_perm, sizeof(int) * h->flow_perm_host.size()));
@@ -1333,10 +1381,8 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->lws);
   cudaFree(h->fws);
   cudaFree(h->d_flow_perm);
-  for (auto& F : h->flow) {
-    cudaFree(F.d_cond_w);
-    cudaFree(F.d_cond_b);
-  }
+  cudaFree(h->d_flow_cond_w);
+  cudaFree(h->d_flow_cond_b);
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
   for (auto& run : h->runs)

@@ -126,6 +126,8 @@ cudaError_t launch_tn(TapConvGroup g, cudaStream_t st) {
 }  // namespace
 
 cudaError_t launch_tapconv_f32(const TapConvGroup& g, cudaStream_t st) {
+  for (int i = 0; i < g.n; ++i)
+    if (g.op[i].gate || (g.op[i].bias_bc_ld && g.op[i].bias_bc_ld != g.op[i].Cout)) return cudaErrorNotSupported;
   int nmax = 0;
   for (int i = 0; i < g.n; ++i) nmax = max(nmax, g.op[i].N);
   if (nmax <= 16) return launch_tn<16>(g, st);

@@ -72,7 +72,7 @@ struct SmSeg {
 struct SmOp {
   int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
   int nres, out_mode, scw, stride;
-  int pad, pad_[3];
+  int pad, gate, bias_bc_ld, pad_;
   const __nv_bfloat16* res[4];
   const int* len;
   const float* bias;
@@ -112,7 +112,7 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   a.shift = o.cout_shift;
   a.lim = o.len ? o.len[b] : 0x7fffffff;
   a.bias = sbias + o.bias_off;
-  a.bias_bc = o.bias_bc ? o.bias_bc + (size_t)b * o.Cout : nullptr;
+  a.bias_bc = o.bias_bc ? o.bias_bc + (size_t)b * o.bias_bc_ld : nullptr;
   a.raw = o.out_raw ? o.out_raw + (size_t)b * a.total : nullptr;
   a.act = o.out_act ? o.out_act + (size_t)b * a.total : nullptr;
   a.slope = o.slope;
@@ -387,6 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     o.scw = P.out_scw[threadIdx.x];
     o.stride = P.out_s[threadIdx.x];
     o.pad = P.out_pad[threadIdx.x];
+    o.gate = g.gate;
+    o.bias_bc_ld = g.bias_bc_ld ? g.bias_bc_ld : g.Cout;
     for (int r = 0; r < kMaxRes; ++r)
       o.res[r] = r < g.nres ? static_cast<const __nv_bfloat16*>(g.res[r]) : nullptr;
     o.bias_off = P.bias_off[threadIdx.x];
@@ -597,6 +599,39 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const bool live = q < o.Q;
       const EpiArgs ea = epi_args(o, sbias, b);
       const int mode = STG ? o.out_mode : kOutPlain, scw = STG ? o.scw : 16;
+      if (o.gate) {
+        // Gated activation: 32-column runs (a | b) -> 16 outputs of channel
+        // block (n0 + c0) / 2 (WN, src/models/sovits_flow.rs:171-184).
+        const int H = o.Cout / 2;
+        const bool dead = q >= ea.lim || q >= o.Q;
+#pragma unroll 1
+        for (int c0 = 0; c0 < NT; c0 += 32) {
+          float va[16], vb[16];
+          if (!masked) {
+            tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, va);
+            tmem_ld16(lane_addr + buf * NT + (uint32_t)(c0 + 16), vb);
+          }
+          if (!live) continue;
+          const int n = n0 + c0;
+          float y[16];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            float a = va[k] + ea.bias[n + k], sg = vb[k] + ea.bias[n + 16 + k];
+            if (ea.bias_bc) {
+              a = a + __ldg(ea.bias_bc + n + k);
+              sg = sg + __ldg(ea.bias_bc + n + 16 + k);
+            }
+            y[k] = (masked || dead) ? 0.0f : tanhf(a) * (1.0f / (1.0f + expf(-sg)));
+          }
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(o.out_raw) + ((size_t)b * o.Lout + q) * H + n / 2;
+          store8(dst, y);
+          store8(dst + 8, y + 8);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
+        continue;
+      }
 #pragma unroll 1
       for (int cc = 0; cc < NT; cc += scw) {
         // Destination of this warp's chunk: rows q0 + 32 * quarter .. + 31,
@@ -738,6 +773,7 @@ bool tapconv_tc_supported(const TapConv& op) {
   const int ck = ck_for(cin), nt = nt_for(op.N);
   if (!ck || !nt || op.N % nt) return false;
   if (op.Cout % 16) return false;  // 16-element epilogue runs stay 16-byte aligned
+  if (op.gate && (op.N != op.Cout || op.N % 32 || op.crop || op.Q != op.Lout || op.nres)) return false;
   if ((long long)op.Lout * op.Cout >= (1ll << 31) || (long long)op.Q * op.N >= (1ll << 31))
     return false;  // 32-bit per-utterance index math
   return (ck == 64 && (nt == 256 || nt == 128 || nt == 64)) || (ck == 32 && nt == 32) ||
