@@ -343,8 +343,10 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 
 // SA: activation-window ring depth; SB: streamed weight ring depth (RES = false);
 // NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
-// STG: outputs leave through shared-memory staging and TMA tensor stores.
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
+// STG: outputs leave through shared-memory staging and TMA tensor stores;
+// GATE: the ops are gated-activation ops (kept out of the other
+// instantiations, whose register budget it would raise).
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG, bool GATE>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
   using S = TcShape<CK, NT, NBUF, STG>;
   extern __shared__ uint8_t smem_raw[];
@@ -599,7 +601,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const bool live = q < o.Q;
       const EpiArgs ea = epi_args(o, sbias, b);
       const int mode = STG ? o.out_mode : kOutPlain, scw = STG ? o.scw : 16;
-      if (o.gate) {
+      if (GATE) {
         // Gated activation: 32-column runs (a | b) -> 16 outputs of channel
         // block (n0 + c0) / 2 (WN, src/models/sovits_flow.rs:171-184).
         const int H = o.Cout / 2;
@@ -736,15 +738,27 @@ bool encode_out(CUtensorMap* m, void* y, int mode, int B, int Lout, int Cout, in
 }
 
 template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
-cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
+size_t cfg_smem(const TcParams& P) {
   using S = TcShape<CK, NT, NBUF, STG>;
   const int nbt = RES ? P.w_tiles : SB;
-  const size_t smem = 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
-                      8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
-                      sizeof(float) * (size_t)P.bias_floats +
-                      (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
+  return 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
+         8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
+         sizeof(float) * (size_t)P.bias_floats +
+         (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
+}
+
+// True when `per_sm` CTAs of this configuration fit one SM's shared memory.
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
+bool cfg_fits(const TcParams& P, int per_sm) {
+  return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P) + 1024) <= (size_t)smem_per_sm();
+}
+
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG, bool GATE = false>
+cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
+  using S = TcShape<CK, NT, NBUF, STG>;
+  const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG, GATE>;
   // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
   // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
   int nregs = 0;
@@ -848,19 +862,37 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   P.w_tiles = wtiles;
   if (P.total_tiles <= 0) return cudaSuccess;
   // Narrow layers keep every weight tile of the launch resident in shared memory.
-  bool stg = false;
-  for (int i = 0; i < g.n; ++i) stg = stg || P.out_mode[i] != kOutPlain;
-  // With staging, ring depths shrink to keep two CTAs per SM (one for NT = 256)
-  // next to the 16 KB of staging.
+  bool stg = false, gate = false;
+  for (int i = 0; i < g.n; ++i) {
+    stg = stg || P.out_mode[i] != kOutPlain;
+    gate = gate || g.op[i].gate;
+  }
+  if (gate) {
+    for (int i = 0; i < g.n; ++i)
+      if (!g.op[i].gate) return cudaErrorInvalidValue;  // a group is all gated or none
+    if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, false, true>(P, st);
+    return cudaErrorNotSupported;
+  }
+  // With staging the deeper rings are kept when two CTAs per SM (one for
+  // NT = 256) still fit next to the 16 KB of staging, else they shrink.
   if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4, false>(P, st);
-  if (ck == 32 && nt == 32 && P.n_tiles == 1)
-    return stg ? launch_cfg<32, 32, true, 3, 1, 4, true>(P, st) : launch_cfg<32, 32, true, 4, 1, 4, false>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1) {
+    if (!stg) return launch_cfg<32, 32, true, 4, 1, 4, false>(P, st);
+    if (cfg_fits<32, 32, true, 4, 1, 4, true>(P, 2)) return launch_cfg<32, 32, true, 4, 1, 4, true>(P, st);
+    return launch_cfg<32, 32, true, 3, 1, 4, true>(P, st);
+  }
   if (ck == 64 && nt == 256)
     return stg ? launch_cfg<64, 256, false, 2, 4, 2, true>(P, st) : launch_cfg<64, 256, false, 2, 4, 2, false>(P, st);
-  if (ck == 64 && nt == 128)
-    return stg ? launch_cfg<64, 128, false, 2, 2, 2, true>(P, st) : launch_cfg<64, 128, false, 2, 3, 2, false>(P, st);
-  if (ck == 64 && nt == 64)
-    return stg ? launch_cfg<64, 64, false, 2, 4, 4, true>(P, st) : launch_cfg<64, 64, false, 3, 4, 4, false>(P, st);
+  if (ck == 64 && nt == 128) {
+    if (!stg) return launch_cfg<64, 128, false, 2, 3, 2, false>(P, st);
+    if (cfg_fits<64, 128, false, 2, 3, 2, true>(P, 2)) return launch_cfg<64, 128, false, 2, 3, 2, true>(P, st);
+    return launch_cfg<64, 128, false, 2, 2, 2, true>(P, st);
+  }
+  if (ck == 64 && nt == 64) {
+    if (!stg) return launch_cfg<64, 64, false, 3, 4, 4, false>(P, st);
+    if (cfg_fits<64, 64, false, 3, 4, 4, true>(P, 2)) return launch_cfg<64, 64, false, 3, 4, 4, true>(P, st);
+    return launch_cfg<64, 64, false, 2, 4, 4, true>(P, st);
+  }
   return cudaErrorInvalidValue;
 }
 
