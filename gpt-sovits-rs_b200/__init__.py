@@ -343,6 +343,22 @@ class Decoder:
                                               frame_end, halo, _ptr(wav), MEM_HOST, None))
         return wav
 
+    def forward_chunk_device(self, z, g, frame_begin: int, frame_end: int, halo: int = 16, out=None,
+                             stream=None):
+        """forward_chunk on CUDA tensors (z [1, C, T0], g [1, gin, 1]): frames
+        [frame_begin, frame_end) with a recomputed halo, into a device tensor."""
+        import torch
+        assert z.is_cuda and z.dtype == torch.float32 and z.is_contiguous() and z.shape[0] == 1
+        n = max(1, frame_end - frame_begin) * self.hop
+        if out is None:
+            out = torch.empty(n, device=z.device, dtype=torch.float32)
+        st = stream if stream is not None else torch.cuda.current_stream(z.device).cuda_stream
+        _check(library().gsvdec_forward_chunk(
+            self._h, ctypes.c_void_p(z.data_ptr()), None if g is None else ctypes.c_void_p(g.data_ptr()),
+            z.shape[2], frame_begin, frame_end, halo, ctypes.c_void_p(out.data_ptr()), MEM_DEVICE,
+            ctypes.c_void_p(st)))
+        return out
+
     def forward_debug(self, x, g=None):
         """Decoder::forward_debug (src/models/sovits_decoder.rs:473-526): the
         waveform plus the per-layer taps [conv_pre(+cond), ups0, rb0, ...,

@@ -283,15 +283,15 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t sr
                : "memory");
 }
 
-template <int CK, int NT, int NBUF, bool STG>
+template <int CK, int NT, int NBUF, int STG>
 struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
   // TMA-store staging: per epilogue warp, 32 rows x 32 channels bf16 for each
-  // of the two outputs (raw, act).
+  // of the STG staged outputs (raw and/or act).
   static constexpr uint32_t kStageOut = 32 * 32 * 2;
-  static constexpr uint32_t kStageWarp = 2 * kStageOut;
-  static constexpr uint32_t kStageBytes = STG ? 4 * kStageWarp : 0;
+  static constexpr uint32_t kStageWarp = STG * kStageOut;
+  static constexpr uint32_t kStageBytes = 4 * kStageWarp;
   static constexpr int kCols = NBUF * NT;  // NBUF accumulators of NT fp32 columns
   static constexpr uint32_t kTmemCols =
       kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
@@ -343,10 +343,10 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 
 // SA: activation-window ring depth; SB: streamed weight ring depth (RES = false);
 // NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
-// STG: outputs leave through shared-memory staging and TMA tensor stores;
-// GATE: the ops are gated-activation ops (kept out of the other
-// instantiations, whose register budget it would raise).
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG, bool GATE>
+// STG: 1 or 2 outputs leave through shared-memory staging and TMA tensor
+// stores (0: plain stores); GATE: the ops are gated-activation ops (kept out
+// of the other instantiations, whose register budget it would raise).
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
   using S = TcShape<CK, NT, NBUF, STG>;
   extern __shared__ uint8_t smem_raw[];
@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const uint32_t stg_raw = smem_u32(sStage) + (uint32_t)quarter * S::kStageWarp;
-    const uint32_t stg_act = stg_raw + S::kStageOut;
+    const uint32_t stg_act = STG == 2 ? stg_raw + S::kStageOut : stg_raw;  // one output: one buffer
     bool pending = false;  // a TMA store of this warp may still be reading its staging
     uint32_t i = 0;
     for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total; w.next(), ++i) {
@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       const int q = q0 + row;
       const bool live = q < o.Q;
       const EpiArgs ea = epi_args(o, sbias, b);
-      const int mode = STG ? o.out_mode : kOutPlain, scw = STG ? o.scw : 16;
+      const int mode = STG > 0 ? o.out_mode : kOutPlain, scw = STG > 0 ? o.scw : 16;
       if (GATE) {
         // Gated activation: 32-column runs (a | b) -> 16 outputs of channel
         // block (n0 + c0) / 2 (WN, src/models/sovits_flow.rs:171-184).
@@ -737,7 +737,7 @@ bool encode_out(CUtensorMap* m, void* y, int mode, int B, int Lout, int Cout, in
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG>
 size_t cfg_smem(const TcParams& P) {
   using S = TcShape<CK, NT, NBUF, STG>;
   const int nbt = RES ? P.w_tiles : SB;
@@ -748,12 +748,12 @@ size_t cfg_smem(const TcParams& P) {
 }
 
 // True when `per_sm` CTAs of this configuration fit one SM's shared memory.
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG>
 bool cfg_fits(const TcParams& P, int per_sm) {
   return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P) + 1024) <= (size_t)smem_per_sm();
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool STG, bool GATE = false>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE = false>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   using S = TcShape<CK, NT, NBUF, STG>;
   const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P);
@@ -773,6 +773,13 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   if (grid <= 0) return cudaSuccess;
   kern<<<grid, kThreads, smem, st>>>(P);
   return cudaGetLastError();
+}
+
+template <int CK, int NT, bool RES, int SA, int SB, int SA2, int SB2, int NBUF>
+cudaError_t launch_staged(TcParams& P, int stg, int per_sm, cudaStream_t st) {
+  if (stg == 0) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 0>(P, st);
+  if (cfg_fits<CK, NT, RES, SA, SB, NBUF, 2>(P, per_sm)) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 2>(P, st);
+  return launch_cfg<CK, NT, RES, SA2, SB2, NBUF, 2>(P, st);
 }
 
 }  // namespace
@@ -843,6 +850,8 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     // Staged TMA stores pay off where a tile writes two outputs (raw and act)
     // in rows of at least 64 bytes that a TMA box covers densely: Conv1d, and
     // ConvTranspose of stride 2.  Elsewhere the plain 16-byte stores win.
+    // (Measured: one-output layers are slower staged -- the per-chunk wait for
+    // the staging buffer costs more than their plain stores.)
     const bool dense = op.out_raw && op.out_act && op.Cout >= 32 &&
                        (P.out_mode[i] == kOutConv || (P.out_mode[i] == kOutConvT && P.out_s[i] == 2));
     if (!dense) P.out_mode[i] = kOutPlain;
@@ -862,37 +871,26 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   P.w_tiles = wtiles;
   if (P.total_tiles <= 0) return cudaSuccess;
   // Narrow layers keep every weight tile of the launch resident in shared memory.
-  bool stg = false, gate = false;
+  int stg = 0;  // outputs per tile staged for TMA stores (0: plain stores, else 2)
+  bool gate = false;
   for (int i = 0; i < g.n; ++i) {
-    stg = stg || P.out_mode[i] != kOutPlain;
+    if (P.out_mode[i] != kOutPlain)
+      stg = std::max(stg, (g.op[i].out_raw != nullptr) + (g.op[i].out_act != nullptr));
     gate = gate || g.op[i].gate;
   }
   if (gate) {
     for (int i = 0; i < g.n; ++i)
       if (!g.op[i].gate) return cudaErrorInvalidValue;  // a group is all gated or none
-    if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, false, true>(P, st);
+    if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, 0, true>(P, st);
     return cudaErrorNotSupported;
   }
-  // With staging the deeper rings are kept when two CTAs per SM (one for
-  // NT = 256) still fit next to the 16 KB of staging, else they shrink.
-  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4, false>(P, st);
-  if (ck == 32 && nt == 32 && P.n_tiles == 1) {
-    if (!stg) return launch_cfg<32, 32, true, 4, 1, 4, false>(P, st);
-    if (cfg_fits<32, 32, true, 4, 1, 4, true>(P, 2)) return launch_cfg<32, 32, true, 4, 1, 4, true>(P, st);
-    return launch_cfg<32, 32, true, 3, 1, 4, true>(P, st);
-  }
-  if (ck == 64 && nt == 256)
-    return stg ? launch_cfg<64, 256, false, 2, 4, 2, true>(P, st) : launch_cfg<64, 256, false, 2, 4, 2, false>(P, st);
-  if (ck == 64 && nt == 128) {
-    if (!stg) return launch_cfg<64, 128, false, 2, 3, 2, false>(P, st);
-    if (cfg_fits<64, 128, false, 2, 3, 2, true>(P, 2)) return launch_cfg<64, 128, false, 2, 3, 2, true>(P, st);
-    return launch_cfg<64, 128, false, 2, 2, 2, true>(P, st);
-  }
-  if (ck == 64 && nt == 64) {
-    if (!stg) return launch_cfg<64, 64, false, 3, 4, 4, false>(P, st);
-    if (cfg_fits<64, 64, false, 3, 4, 4, true>(P, 2)) return launch_cfg<64, 64, false, 3, 4, 4, true>(P, st);
-    return launch_cfg<64, 64, false, 2, 4, 4, true>(P, st);
-  }
+  // With staging the deeper rings (SA, SB) are kept when `per_sm` CTAs still
+  // fit next to the 16 KB of staging, else they shrink to (SA2, SB2).
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_staged<32, 32, true, 4, 1, 3, 1, 4>(P, stg, 2, st);
+  if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 2, 4, 2, 3, 2>(P, stg, 1, st);
+  if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
+  if (ck == 64 && nt == 64) return launch_staged<64, 64, false, 3, 4, 2, 4, 4>(P, stg, 2, st);
   return cudaErrorInvalidValue;
 }
 

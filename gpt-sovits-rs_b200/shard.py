@@ -42,6 +42,41 @@ def plan_utterances(lengths: Sequence[int], nranks: int) -> List[List[int]]:
     return [sorted(x) for x in out]
 
 
+def plan_buckets(lengths: Sequence[int], max_buckets: int = 8, overhead: int = 300) -> List[List[int]]:
+    """Split utterances into at most `max_buckets` batches of similar length.
+
+    A masked batch costs (its size x its longest length) padded frames plus a
+    fixed `overhead` (the per-forward launch cost, in frame units); the split
+    minimises the total over contiguous runs of the length-sorted order
+    (dynamic programming).  Returns lists of indices into `lengths`, each
+    ascending, the buckets ordered by length.
+    """
+    n = len(lengths)
+    if n == 0:
+        return []
+    order = sorted(range(n), key=lambda i: (int(lengths[i]), i))
+    ls = [int(lengths[i]) for i in order]
+    K = max(1, min(max_buckets, n))
+    INF = float("inf")
+    # best[k][j]: min cost of the first j sorted utterances in k buckets
+    best = [[INF] * (n + 1) for _ in range(K + 1)]
+    cut = [[0] * (n + 1) for _ in range(K + 1)]
+    best[0][0] = 0.0
+    for k in range(1, K + 1):
+        for j in range(1, n + 1):
+            for i in range(k - 1, j):
+                c = best[k - 1][i] + (j - i) * ls[j - 1] + overhead
+                if c < best[k][j]:
+                    best[k][j], cut[k][j] = c, i
+    k = min(range(1, K + 1), key=lambda kk: best[kk][n])
+    out, j = [], n
+    while k > 0:
+        i = cut[k][j]
+        out.append(sorted(order[i:j]))
+        j, k = i, k - 1
+    return out[::-1]
+
+
 def plan_chunks(T0: int, nranks: int) -> List[Tuple[int, int]]:
     """Contiguous frame ranges [begin, end) covering [0, T0), one per rank
     (sizes differ by at most one frame; trailing ranks may be empty when
@@ -63,9 +98,10 @@ def halo_window(begin: int, end: int, T0: int, halo: int) -> Tuple[int, int]:
     return max(0, begin - halo), min(T0, end + halo)
 
 
-def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device):
+def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device, as_numpy: bool = True):
     """Gather variable-length 1-D float32 pieces to rank 0 (zero-padded to
-    `maxlen`); returns the list of trimmed numpy pieces on rank 0, else None."""
+    `maxlen`); returns the list of trimmed pieces on rank 0 (numpy, or device
+    tensors with as_numpy=False), else None."""
     import torch
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
@@ -79,35 +115,61 @@ def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device):
     dist.gather(buf, gather_list=gl, dst=0, group=group)
     if rank != 0:
         return None
+    if not as_numpy:
+        return [gl[r][: int(all_sizes[r].item())] for r in range(world)]
     return [gl[r][: int(all_sizes[r].item())].cpu().numpy() for r in range(world)]
 
 
 def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray],
-                         lengths: Sequence[int], hop: int, dist, group=None, device="cpu"):
+                         lengths: Sequence[int], hop: int, dist, group=None, device="cpu",
+                         max_buckets: int = 8):
     """Decode a right-padded batch across the ranks of `group`.
 
-    `decode(z_b, g_b, lengths_b)` runs this rank's share (a masked batch) and
-    returns its flattened waveform [n_b * hop * T_b].  Every rank passes the
-    same z / g / lengths.  Rank 0 returns the list of per-utterance waveforms
-    (each hop * lengths[i] samples), other ranks return None.
+    `decode(z_b, g_b, lengths_b)` runs one masked batch and returns its
+    flattened waveform [n_b * hop * T_b].  Each rank decodes its share in up
+    to `max_buckets` length buckets (plan_buckets), so short utterances are
+    not padded to the longest one.  Every rank passes the same z / g /
+    lengths.  Rank 0 returns the list of per-utterance waveforms (each
+    hop * lengths[i] samples), other ranks return None.
+
+    With z (and g) as CUDA tensors the whole path stays on the device: the
+    bucket batches are gathered from z on the device, `decode` receives
+    device tensors (lengths as an int32 device tensor) and returns a device
+    waveform, the pieces are gathered over the process group as device
+    tensors, and rank 0 gets device tensors back.
     """
     import torch
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     plan = plan_utterances(lengths, world)
     mine = plan[rank]
-    lens = [int(lengths[i]) for i in mine]
+    on_dev = isinstance(z, torch.Tensor)
     if mine:
-        T = max(lens)
-        zb = np.ascontiguousarray(z[mine, :, :T])
-        gb = None if g is None else np.ascontiguousarray(g[mine])
-        wav = np.asarray(decode(zb, gb, lens), np.float32).reshape(len(mine), T * hop)
-        piece = np.concatenate([wav[k, : lens[k] * hop] for k in range(len(mine))])
+        parts = {}
+        for bucket in plan_buckets([int(lengths[i]) for i in mine], max_buckets):
+            idx = [mine[k] for k in bucket]
+            lens = [int(lengths[i]) for i in idx]
+            T = max(lens)
+            if on_dev:
+                it = torch.tensor(idx, device=z.device)
+                zb = z.index_select(0, it)[:, :, :T].contiguous()
+                gb = None if g is None else g.index_select(0, it).contiguous()
+                lb = torch.tensor(lens, dtype=torch.int32, device=z.device)
+                wav = decode(zb, gb, lb).reshape(len(idx), T * hop)
+            else:
+                zb = np.ascontiguousarray(z[idx, :, :T])
+                gb = None if g is None else np.ascontiguousarray(g[idx])
+                wav = np.asarray(decode(zb, gb, lens), np.float32).reshape(len(idx), T * hop)
+            for k, i in enumerate(idx):
+                parts[i] = wav[k, : lens[k] * hop]
+        piece = torch.cat([parts[i] for i in mine]) if on_dev else np.concatenate([parts[i] for i in mine])
     else:
-        piece = np.zeros(0, np.float32)
+        piece = torch.zeros(0, device=z.device) if on_dev else np.zeros(0, np.float32)
     maxlen = max(sum(int(lengths[i]) for i in p) for p in plan) * hop
     maxlen = max(maxlen, 1)
-    got = _gather_to_root(torch.from_numpy(piece).to(device), piece.size, maxlen, dist, group, device)
+    n_valid = int(piece.numel()) if on_dev else piece.size
+    src = piece if on_dev else torch.from_numpy(piece).to(device)
+    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev)
     if got is None:
         return None
     out: List[Optional[np.ndarray]] = [None] * len(lengths)
@@ -125,17 +187,23 @@ def decode_long_chunked(decode_chunk: Callable, T0: int, hop: int, dist, group=N
     """Decode one long utterance split in time across the ranks of `group`.
 
     `decode_chunk(begin, end)` returns the hop * (end - begin) samples of
-    frames [begin, end) (computed with its own halo).  Rank 0 returns the
-    whole waveform, other ranks None.
+    frames [begin, end) (computed with its own halo), as numpy or as a device
+    tensor (then the pieces are gathered and joined on the device).  Rank 0
+    returns the whole waveform, other ranks None.
     """
     import torch
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     chunks = plan_chunks(T0, world)
     b, e = chunks[rank]
-    piece = np.asarray(decode_chunk(b, e), np.float32) if e > b else np.zeros(0, np.float32)
+    piece = decode_chunk(b, e) if e > b else None
+    on_dev = isinstance(piece, torch.Tensor)
+    if piece is None:
+        piece = np.zeros(0, np.float32)
     maxlen = max(1, max(ee - bb for bb, ee in chunks) * hop)
-    got = _gather_to_root(torch.from_numpy(piece).to(device), piece.size, maxlen, dist, group, device)
+    n_valid = int(piece.numel()) if on_dev else int(np.asarray(piece).size)
+    src = piece if on_dev else torch.from_numpy(np.asarray(piece, np.float32)).to(device)
+    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev)
     if got is None:
         return None
-    return np.concatenate(got)
+    return torch.cat(got) if on_dev else np.concatenate(got)

@@ -39,6 +39,30 @@ def test_plan_utterances_balances_and_covers(gsv):
         assert plan == shard.plan_utterances(lens, world)  # deterministic
 
 
+def test_plan_buckets_cover_and_minimise_padding(gsv):
+    import itertools
+    shard = gsv.shard
+    rng = np.random.default_rng(1)
+    for n in (1, 2, 5, 7):
+        lens = [int(x) for x in rng.integers(100, 1001, n)]
+        for K in (1, 2, 3):
+            plan = shard.plan_buckets(lens, K, overhead=300)
+            assert sorted(i for b in plan for i in b) == list(range(n))
+            assert len(plan) <= K and all(b == sorted(b) for b in plan)
+            cost = sum(len(b) * max(lens[i] for i in b) + 300 for b in plan)
+            # brute force over cut points of the length-sorted order
+            order = sorted(range(n), key=lambda i: (lens[i], i))
+            best = None
+            for k in range(1, min(K, n) + 1):
+                for cuts in itertools.combinations(range(1, n), k - 1):
+                    edges = (0,) + cuts + (n,)
+                    c = sum((edges[j + 1] - edges[j]) * lens[order[edges[j + 1] - 1]] + 300 for j in range(k))
+                    best = c if best is None else min(best, c)
+            assert cost == best
+    assert shard.plan_buckets([500] * 6, 8) == [list(range(6))]  # equal lengths: one batch
+    assert shard.plan_buckets([], 8) == []
+
+
 def test_plan_chunks_cover_contiguously(gsv):
     shard = gsv.shard
     for T0, world in ((3000, 8), (3000, 1), (5, 8), (11, 3)):
