@@ -238,6 +238,21 @@ def test_bf16_length_masking_is_exact(gsv, dec_bf16):
         assert not wav[b, 640 * n:].any()
 
 
+def test_bf16_masking_beyond_1024_utterances(gsv, dec_bf16):
+    # More than 1024 utterances: the kernels read the lengths from global
+    # memory instead of their shared-memory copy; masking must still be exact.
+    B, T0 = 1100, 3
+    rng = np.random.default_rng(83)
+    lens = rng.integers(1, T0 + 1, B).astype(np.int32)
+    z, g = gsv.synth.make_inputs(B, T0, seed_z=84, seed_g=85)
+    wav = dec_bf16.forward(z, g, lengths=lens).reshape(B, -1)
+    for b in (0, 511, 1024, 1099):
+        n = int(lens[b])
+        alone = dec_bf16.forward(z[b:b + 1, :, :n], g[b:b + 1])
+        assert np.array_equal(wav[b, :640 * n], alone), b
+        assert not wav[b, 640 * n:].any()
+
+
 def test_bf16_chunked_equals_whole(gsv, dec_bf16):
     T0 = 90
     z, g = gsv.synth.make_inputs(1, T0, seed_z=91, seed_g=92)
