@@ -91,16 +91,6 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ uint4 lrelu_bf16x8(uint4 u, float slope) {
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    h[i] = __floats2bfloat162_rn(lrelu(f.x, slope), lrelu(f.y, slope));
-  }
-  return u;
-}
-
 template <int C>
 __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_constant__ RbParams P) {
   using S = RbShape<C>;
@@ -246,6 +236,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
     const uint32_t ax = smem_u32(sAX), tb = smem_u32(sT);
     const float slope = P.slope;
+    const __nv_bfloat162 slope2 = __float2bfloat162_rn(slope);
     const int L = P.L;
     bool ok = true;
     // a(i): lrelu of window i into the conv1 operand buffer (same swizzle).
@@ -255,7 +246,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
       const uint32_t src = smem_u32(sX + s * P.a_stage);
       const int n16 = win_rows * S::kRow / 16;
       for (int c = tid; c < n16; c += 128)
-        st_shared_v4(ax + c * 16, lrelu_bf16x8(ld_shared_v4(src + c * 16), slope));
+        st_shared_v4(ax + c * 16, lrelu_bf16x8(ld_shared_v4(src + c * 16), slope2));
       fence_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(ax_full);
@@ -280,17 +271,10 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
         for (int c0 = 0; c0 < C; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + (uint32_t)c0, v);
-          float w[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) w[e] = live ? lrelu(v[e] + sb[c0 + e], slope) : 0.0f;
-          uint4 u0, u1;
-          __nv_bfloat162* p0 = reinterpret_cast<__nv_bfloat162*>(&u0);
-          __nv_bfloat162* p1 = reinterpret_cast<__nv_bfloat162*>(&u1);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            p0[e] = __floats2bfloat162_rn(w[2 * e], w[2 * e + 1]);
-            p1[e] = __floats2bfloat162_rn(w[8 + 2 * e], w[8 + 2 * e + 1]);
-          }
+          for (int e = 0; e < 16; ++e) v[e] = v[e] + sb[c0 + e];
+          uint4 u0 = lrelu_bf16x8(pack_bf16x8(v), slope2), u1 = lrelu_bf16x8(pack_bf16x8(v + 8), slope2);
+          if (!live) u0 = u1 = make_uint4(0, 0, 0, 0);
           st_shared_v4(swz<C>(tb, r, c0 / 8), u0);
           st_shared_v4(swz<C>(tb, r, c0 / 8 + 1), u1);
         }
@@ -322,20 +306,17 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
         for (int c0 = 0; c0 < C; c0 += 16) {
           float v[16];
           tmem_ld16(lane_addr + (uint32_t)(C + c0), v);
-          float x[16], a[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            x[e] = dead ? 0.0f : v[e] + sb[C + c0 + e];
-            a[e] = lrelu(x[e], slope);
-          }
+          for (int e = 0; e < 16; ++e) v[e] = dead ? 0.0f : v[e] + sb[C + c0 + e];
+          const uint4 x0 = pack_bf16x8(v), x1 = pack_bf16x8(v + 8);
           if (store) {
             if (op.out_raw) {
-              store8(op.out_raw + base + c0, x);
-              store8(op.out_raw + base + c0 + 8, x + 8);
+              *reinterpret_cast<uint4*>(op.out_raw + base + c0) = x0;
+              *reinterpret_cast<uint4*>(op.out_raw + base + c0 + 8) = x1;
             }
             if (op.out_act) {
-              store8(op.out_act + base + c0, a);
-              store8(op.out_act + base + c0 + 8, a + 8);
+              *reinterpret_cast<uint4*>(op.out_act + base + c0) = lrelu_bf16x8(x0, slope2);
+              *reinterpret_cast<uint4*>(op.out_act + base + c0 + 8) = lrelu_bf16x8(x1, slope2);
             }
           }
         }

@@ -177,16 +177,15 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
       for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
     }
   }
+  const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
   if (a.raw) {
-    store8(a.raw + e0, v);
-    store8(a.raw + e0 + 8, v + 8);
+    *reinterpret_cast<uint4*>(a.raw + e0) = u0;
+    *reinterpret_cast<uint4*>(a.raw + e0 + 8) = u1;
   }
   if (a.act) {
-    float w[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) w[i] = lrelu(v[i], a.slope);
-    store8(a.act + e0, w);
-    store8(a.act + e0 + 8, w + 8);
+    const __nv_bfloat162 s2 = __float2bfloat162_rn(a.slope);
+    *reinterpret_cast<uint4*>(a.act + e0) = lrelu_bf16x8(u0, s2);
+    *reinterpret_cast<uint4*>(a.act + e0 + 8) = lrelu_bf16x8(u1, s2);
   }
 }
 
@@ -245,14 +244,6 @@ __device__ __forceinline__ bool epi16_values(const EpiArgs& a, int q, int n, flo
     for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
   }
   return true;
-}
-
-__device__ __forceinline__ uint4 pack8(const float* v) {
-  uint4 o;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  return o;
 }
 
 __device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
@@ -670,16 +661,15 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           // Rows outside the output are clipped by the tensor map.
           epi16_values(ea, q, n0 + c0, v);
           const int h = (c0 - cc) / 8;
+          const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
           if (ea.raw) {
-            sts128(stage_addr(stg_raw, lane, h, scw), pack8(v));
-            sts128(stage_addr(stg_raw, lane, h + 1, scw), pack8(v + 8));
+            sts128(stage_addr(stg_raw, lane, h, scw), u0);
+            sts128(stage_addr(stg_raw, lane, h + 1, scw), u1);
           }
           if (ea.act) {
-            float w[16];
-#pragma unroll
-            for (int k = 0; k < 16; ++k) w[k] = lrelu(v[k], ea.slope);
-            sts128(stage_addr(stg_act, lane, h, scw), pack8(w));
-            sts128(stage_addr(stg_act, lane, h + 1, scw), pack8(w + 8));
+            const __nv_bfloat162 s2 = __float2bfloat162_rn(ea.slope);
+            sts128(stage_addr(stg_act, lane, h, scw), lrelu_bf16x8(u0, s2));
+            sts128(stage_addr(stg_act, lane, h + 1, scw), lrelu_bf16x8(u1, s2));
           }
         }
         if (tma) {

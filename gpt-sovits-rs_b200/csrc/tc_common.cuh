@@ -204,6 +204,26 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = o;
 }
 
+// 8 floats -> 8 packed bf16 (round to nearest even).
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+  uint4 o;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return o;
+}
+
+// LeakyReLU of 8 packed bf16 values in bf16 arithmetic, max(x, x * slope)
+// (slope in [0, 1]): two instructions per pair instead of unpack, fp32
+// multiply, max and repack.  For x < 0 it rounds x * bf16(slope) once, which
+// can differ from rounding fp32(x) * slope by one bf16 ulp.
+__device__ __forceinline__ uint4 lrelu_bf16x8(uint4 u, __nv_bfloat162 s2) {
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __hmax2(h[i], __hmul2(h[i], s2));
+  return u;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
