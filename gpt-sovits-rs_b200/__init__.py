@@ -39,8 +39,12 @@ EXPORTS = (
     "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
     "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_layer_forward",
     "gsvdec_layer_names", "gsvdec_last_error", "gsvdec_flow_info", "gsvdec_flow_inverse",
-    "gsvdec_flow_decode",
+    "gsvdec_flow_decode", "gsvdec_encp_info", "gsvdec_encp_add_norm", "gsvdec_encp_ffn",
+    "gsvdec_encp_speed_len", "gsvdec_encp_interpolate", "gsvdec_encp_project",
 )
+
+# EncP encoder stacks (GSV_ENCP_SSL / _TEXT / _2), by their enc_p.* names.
+ENCP_STACKS = {"encoder_ssl": 0, "encoder_text": 1, "encoder2": 2}
 
 
 class GsvDecError(RuntimeError):
@@ -105,6 +109,13 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
     lib.gsvdec_flow_info.argtypes = [vp, ctypes.POINTER(i), ctypes.POINTER(i)]
     lib.gsvdec_flow_inverse.argtypes = [vp, vp, vp, vp, i, i, vp, i, vp]
     lib.gsvdec_flow_decode.argtypes = [vp, vp, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_encp_info.argtypes = [vp, ctypes.POINTER(i), ctypes.POINTER(i), ctypes.POINTER(i),
+                                     ctypes.POINTER(i)]
+    lib.gsvdec_encp_add_norm.argtypes = [vp, i, i, i, vp, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_encp_ffn.argtypes = [vp, i, i, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_encp_speed_len.argtypes = [i, ctypes.c_float, ctypes.POINTER(i)]
+    lib.gsvdec_encp_interpolate.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
+    lib.gsvdec_encp_project.argtypes = [vp, vp, vp, i, i, vp, ctypes.c_float, vp, vp, vp, i, vp]
     _lib = lib
     return lib
 
@@ -331,6 +342,103 @@ class Decoder:
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T0,
             ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
         return out
+
+    # -- EncP fused elementwise chains (src/models/sovits_encp.rs) -----------
+    @property
+    def encp_info(self) -> dict:
+        """Layers per enc_p stack, hidden / FFN filter / projection widths."""
+        n = (ctypes.c_int * 3)()
+        c, f, p = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        _check(library().gsvdec_encp_info(self._h, n, ctypes.byref(c), ctypes.byref(f), ctypes.byref(p)))
+        return {"layers": {k: n[v] for k, v in ENCP_STACKS.items()}, "channels": c.value,
+                "filter_channels": f.value, "proj_channels": p.value}
+
+    @staticmethod
+    def _stack(stack) -> int:
+        return ENCP_STACKS[stack] if isinstance(stack, str) else int(stack)
+
+    @staticmethod
+    def _lengths(lengths, B):
+        if lengths is None:
+            return None
+        ln = np.ascontiguousarray(np.asarray(lengths, np.int32))
+        if ln.shape != (B,):
+            raise ValueError("lengths must hold one value per utterance")
+        return ln
+
+    def encp_add_norm(self, stack, layer: int, x, y=None, lengths=None, norm: int = 1) -> np.ndarray:
+        """norm_layers_<norm>[layer](x + y) (src/models/sovits_encp.rs:102, :107),
+        times x_mask when lengths are given; x, y [B, C, T]."""
+        xa, ya = _host_f32(x), _host_f32(y)
+        B, C, T = xa.shape
+        if ya is not None and ya.shape != xa.shape:
+            raise ValueError("x and y must have the same shape")
+        ln = self._lengths(lengths, B)
+        out = np.empty_like(xa)
+        _check(library().gsvdec_encp_add_norm(self._h, self._stack(stack), layer, norm, _ptr(xa), _ptr(ya),
+                                              _ptr(ln), B, T, _ptr(out), MEM_HOST, None))
+        return out
+
+    def encp_ffn(self, stack, layer: int, x, lengths=None) -> np.ndarray:
+        """norm_layers_2[layer](x + FFN(x)) * x_mask (src/models/sovits_encp.rs:104-109)."""
+        xa = _host_f32(x)
+        B, C, T = xa.shape
+        ln = self._lengths(lengths, B)
+        out = np.empty_like(xa)
+        _check(library().gsvdec_encp_ffn(self._h, self._stack(stack), layer, _ptr(xa), _ptr(ln), B, T,
+                                         _ptr(out), MEM_HOST, None))
+        return out
+
+    def encp_ffn_device(self, stack, layer: int, x, lengths=None, out=None, stream=None):
+        """Stream-async FFN half on CUDA tensors (torch): x, out [B, C, T] fp32."""
+        import torch
+        B, C, T = x.shape
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+        _check(library().gsvdec_encp_ffn(
+            self._h, self._stack(stack), layer, ctypes.c_void_p(x.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T,
+            ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    @staticmethod
+    def encp_speed_len(T: int, speed: float) -> int:
+        """Frames after the speed change (src/models/sovits_encp.rs:857-867)."""
+        n = ctypes.c_int()
+        _check(library().gsvdec_encp_speed_len(T, speed, ctypes.byref(n)))
+        return n.value
+
+    def encp_interpolate(self, y, speed: float = None, T_out: int = None) -> np.ndarray:
+        """linear_interpolate_last_dim (src/models/sovits_encp.rs:10-40) of
+        y [B, C, T] to T_out frames (or the length `speed` gives)."""
+        ya = _host_f32(y)
+        B, C, T = ya.shape
+        if T_out is None:
+            T_out = self.encp_speed_len(T, 1.0 if speed is None else speed)
+        out = np.empty((B, C, T_out), np.float32)
+        _check(library().gsvdec_encp_interpolate(self._h, _ptr(ya), B, C, T, T_out, _ptr(out),
+                                                 MEM_HOST, None))
+        return out
+
+    def encp_project(self, y, lengths=None, noise=None, noise_scale: float = 0.5):
+        """(m, logs, z_p): stats = proj(y) * y_mask, logs clamped to [-5, 2]
+        (src/models/sovits_encp.rs:871-879), z_p = m + noise * exp(logs) *
+        noise_scale (src/models/sovits.rs:378-385); z_p is None without noise."""
+        ya = _host_f32(y)
+        B, C, T = ya.shape
+        ln = self._lengths(lengths, B)
+        co = self.encp_info["proj_channels"] // 2
+        na = _host_f32(noise)
+        if na is not None and na.shape != (B, co, T):
+            raise ValueError(f"noise must be [{B}, {co}, {T}]")
+        m = np.empty((B, co, T), np.float32)
+        logs = np.empty_like(m)
+        zp = np.empty_like(m) if na is not None else None
+        _check(library().gsvdec_encp_project(self._h, _ptr(ya), _ptr(ln), B, T, _ptr(na), noise_scale,
+                                             _ptr(m), _ptr(logs), _ptr(zp), MEM_HOST, None))
+        return m, logs, zp
 
     def forward_chunk(self, x, g, frame_begin: int, frame_end: int, halo: int = 16) -> np.ndarray:
         """Frames [frame_begin, frame_end) of one utterance with a recomputed halo."""

@@ -1,0 +1,239 @@
+// encp_kernels.cu -- fused elementwise chains of the SoVITS text encoder
+// (EncP, src/models/sovits_encp.rs) that sit around its tap-GEMM convs:
+//
+//  * add + LayerNorm over channels (+ x_mask) on the reference's [B][C][T]
+//    fp32 layout: EncoderLayer::forward's norm1(x + attn(x))
+//    (src/models/sovits_encp.rs:102) with LayerNorm::forward's channel branch
+//    (src/utils/weights.rs:461-502);
+//  * LayerNorm + x_mask + relayout of a time-major GEMM output (the FFN half,
+//    norm2(x + ffn(x)) * x_mask, :104-109): the residual add is already in the
+//    conv_2 epilogue, so this one pass reads v once and writes the reference
+//    layout;
+//  * linear_interpolate_last_dim (:10-40), the speed change before the output
+//    projection (:857-867), evaluated with the reference's f32 operation order
+//    so the result is bit-identical;
+//  * the projection tail and prior sample: stats = proj(y) * y_mask,
+//    m / logs split, logs clamped to [-5, 2] (:871-879), then
+//    z_p = m + noise * exp(logs) * noise_scale (src/models/sovits.rs:378-385).
+//
+// All four are HBM-bound streaming kernels: each element is read once and
+// written once; shared-memory tiles turn the time-major <-> channel-major
+// transposes into coalesced 128-byte rows on both sides.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "gsv_kernels.h"
+
+namespace gsv {
+namespace {
+
+constexpr int kTile = 32;      // frames per block (one warp-width of time)
+constexpr int kWarps = 8;      // 256 threads
+constexpr int kLnMaxC = 1024;  // channel limit of the LayerNorm tiles
+
+__device__ __forceinline__ float ldv(const float* p) { return *p; }
+__device__ __forceinline__ float ldv(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Normalises one column of C values held at s[c * stride] (lanes split c),
+// in place: (v - mean) / sqrt(var + eps) * gamma + beta, times mask.
+// mean and the biased variance are two-pass sums over the column.
+__device__ __forceinline__ void ln_column(float* s, int stride, int C, int lane, const float* gamma,
+                                          const float* beta, float eps, float mask) {
+  float sum = 0.0f;
+  for (int c = lane; c < C; c += 32) sum += s[c * stride];
+  const float mean = warp_sum(sum) / (float)C;
+  float sq = 0.0f;
+  for (int c = lane; c < C; c += 32) {
+    const float d = s[c * stride] - mean;
+    sq += d * d;
+  }
+  const float sd = sqrtf(warp_sum(sq) / (float)C + eps);
+  for (int c = lane; c < C; c += 32) {
+    const float o = (s[c * stride] - mean) / sd * gamma[c] + beta[c];
+    s[c * stride] = o * mask;
+  }
+}
+
+// x, y, out: [B][C][T] fp32.  Block = 32 frames of one utterance; the tile
+// s[c][33] holds x + y for all C channels of those frames.
+__global__ void __launch_bounds__(kWarps * 32) add_ln_ncl_kernel(const float* __restrict__ x,
+                                                                  const float* __restrict__ y,
+                                                                  const float* __restrict__ gamma,
+                                                                  const float* __restrict__ beta, int C,
+                                                                  int T, float eps, const int* __restrict__ len,
+                                                                  float* __restrict__ out) {
+  extern __shared__ float s[];
+  const int b = blockIdx.y, t0 = blockIdx.x * kTile;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const size_t base = (size_t)b * C * T;
+  const int t = t0 + lane;
+  for (int c = w; c < C; c += kWarps) {
+    float v = 0.0f;
+    if (t < T) {
+      v = x[base + (size_t)c * T + t];
+      if (y) v = v + y[base + (size_t)c * T + t];
+    }
+    s[c * (kTile + 1) + lane] = v;
+  }
+  __syncthreads();
+  for (int j = w; j < kTile; j += kWarps) {
+    const float m = (len && t0 + j >= len[b]) ? 0.0f : 1.0f;
+    ln_column(s + j, kTile + 1, C, lane, gamma, beta, eps, m);
+  }
+  __syncthreads();
+  if (t < T)
+    for (int c = w; c < C; c += kWarps) out[base + (size_t)c * T + t] = s[c * (kTile + 1) + lane];
+}
+
+// v: [B][T][C] time-major (mode dtype) -> out [B][C][T] fp32.  The tile
+// s[32][C + 1] holds 32 frames; C + 1 is odd for even C, so the column reads
+// of the transposed store hit 32 different banks.
+template <typename Tv>
+__global__ void __launch_bounds__(kWarps * 32) ln_tm_ncl_kernel(const Tv* __restrict__ v, int C, int T,
+                                                                 const float* __restrict__ gamma,
+                                                                 const float* __restrict__ beta, float eps,
+                                                                 const int* __restrict__ len,
+                                                                 float* __restrict__ out) {
+  extern __shared__ float s[];
+  const int b = blockIdx.y, t0 = blockIdx.x * kTile;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int ld = C + 1;
+  for (int r = w; r < kTile; r += kWarps) {
+    const int t = t0 + r;
+    const Tv* row = v + ((size_t)b * T + t) * C;
+    for (int c = lane; c < C; c += 32) s[r * ld + c] = t < T ? ldv(row + c) : 0.0f;
+    __syncwarp();
+    const float m = (len && t >= len[b]) ? 0.0f : 1.0f;
+    ln_column(s + r * ld, 1, C, lane, gamma, beta, eps, m);
+  }
+  __syncthreads();
+  const int t = t0 + lane;
+  if (t < T)
+    for (int c = w; c < C; c += kWarps) out[((size_t)b * C + c) * T + t] = s[lane * ld + c];
+}
+
+// out[row][i], rows = B*C, from x[row][T]: the reference's index table and
+// blend, each step rounded in f32 as written there (no contraction).
+__global__ void interp_kernel(const float* __restrict__ x, int T, int Tout, float scale, long long rows,
+                              float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= Tout) return;
+  float src = __fsub_rn(__fmul_rn(__fadd_rn((float)i, 0.5f), scale), 0.5f);
+  src = fmaxf(src, 0.0f);
+  const int low = min((int)floorf(src), T - 1);
+  const int up = min(low + 1, T - 1);
+  const float wu = __fsub_rn(src, (float)low);
+  const float wl = __fadd_rn(__fmul_rn(wu, -1.0f), 1.0f);
+  for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float* xr = x + r * T;
+    out[r * Tout + i] = __fadd_rn(__fmul_rn(xr[low], wl), __fmul_rn(xr[up], wu));
+  }
+}
+
+// stats [B][T][2 Co] time-major (mode dtype); noise, m, logs, zp [B][Co][T]
+// fp32.  Block = 32 frames x 32 channels, transposed through shared memory.
+template <typename Tv>
+__global__ void __launch_bounds__(kWarps * 32) prior_kernel(const Tv* __restrict__ stats, int Co, int T,
+                                                            const int* __restrict__ len,
+                                                            const float* __restrict__ noise, float scale,
+                                                            float* __restrict__ m, float* __restrict__ logs,
+                                                            float* __restrict__ zp) {
+  __shared__ float sm[kTile][kTile + 1], sl[kTile][kTile + 1];
+  const int b = blockIdx.z, t0 = blockIdx.x * kTile, c0 = blockIdx.y * kTile;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int r = w; r < kTile; r += kWarps) {
+    const int t = t0 + r, c = c0 + lane;
+    float a = 0.0f, l = 0.0f;
+    if (t < T && c < Co) {
+      const float mk = (len && t >= len[b]) ? 0.0f : 1.0f;
+      const Tv* row = stats + ((size_t)b * T + t) * 2 * Co;
+      a = ldv(row + c) * mk;
+      l = ldv(row + Co + c) * mk;
+    }
+    sm[r][lane] = a;
+    sl[r][lane] = l;
+  }
+  __syncthreads();
+  for (int r = w; r < kTile; r += kWarps) {
+    const int c = c0 + r, t = t0 + lane;
+    if (c >= Co || t >= T) continue;
+    const size_t o = ((size_t)b * Co + c) * T + t;
+    const float mv = sm[lane][r];
+    const float lv = fminf(fmaxf(sl[lane][r], -5.0f), 2.0f);
+    if (m) m[o] = mv;
+    if (logs) logs[o] = lv;
+    if (zp) zp[o] = __fadd_rn(mv, __fmul_rn(__fmul_rn(noise[o], expf(lv)), scale));
+  }
+}
+
+cudaError_t set_smem(const void* fn, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+
+cudaError_t launch_add_layernorm_ncl(const float* x, const float* y, const float* gamma, const float* beta,
+                                     int B, int C, int T, float eps, const int* len, float* out,
+                                     cudaStream_t st) {
+  if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (size_t)C * (kTile + 1);
+  cudaError_t e = set_smem((const void*)add_ln_ncl_kernel, smem);
+  if (e != cudaSuccess) return e;
+  add_ln_ncl_kernel<<<dim3(cdiv(T, kTile), B), kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T, eps, len, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_layernorm_tm_ncl(const void* v, Dt dt, int B, int T, int C, const float* gamma,
+                                    const float* beta, float eps, const int* len, float* out, cudaStream_t st) {
+  if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (size_t)kTile * (C + 1);
+  const dim3 grid(cdiv(T, kTile), B);
+  cudaError_t e;
+  if (dt == Dt::F32) {
+    e = set_smem((const void*)ln_tm_ncl_kernel<float>, smem);
+    if (e != cudaSuccess) return e;
+    ln_tm_ncl_kernel<float><<<grid, kWarps * 32, smem, st>>>(static_cast<const float*>(v), C, T, gamma, beta,
+                                                             eps, len, out);
+  } else {
+    e = set_smem((const void*)ln_tm_ncl_kernel<__nv_bfloat16>, smem);
+    if (e != cudaSuccess) return e;
+    ln_tm_ncl_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(v), C, T, gamma, beta, eps, len, out);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_interpolate(const float* x, long long rows, int T, int Tout, float* out, cudaStream_t st) {
+  if (rows <= 0 || T <= 0 || Tout <= 0) return cudaErrorInvalidValue;
+  const float scale = (float)T / (float)Tout;
+  const int threads = 128;
+  const dim3 grid(cdiv(Tout, threads), (unsigned)std::min<long long>(rows, 65535));
+  interp_kernel<<<grid, threads, 0, st>>>(x, T, Tout, scale, rows, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prior_sample(const void* stats, Dt dt, int B, int T, int Co, const int* len,
+                                const float* noise, float noise_scale, float* m, float* logs, float* zp,
+                                cudaStream_t st) {
+  if (B <= 0 || T <= 0 || Co <= 0 || B > 65535) return cudaErrorInvalidValue;
+  if (zp && !noise) return cudaErrorInvalidValue;
+  const dim3 grid(cdiv(T, kTile), cdiv(Co, kTile), B);
+  if (dt == Dt::F32)
+    prior_kernel<float><<<grid, kWarps * 32, 0, st>>>(static_cast<const float*>(stats), Co, T, len, noise,
+                                                      noise_scale, m, logs, zp);
+  else
+    prior_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(stats), Co,
+                                                              T, len, noise, noise_scale, m, logs, zp);
+  return cudaGetLastError();
+}
+
+}  // namespace gsv

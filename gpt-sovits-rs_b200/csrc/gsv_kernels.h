@@ -74,4 +74,25 @@ cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, c
 cudaError_t launch_gate(const void* xin, const float* cond, int cond_ld, int cond_off, int B, int L,
                         int H, const int* len, void* out, Dt dt, cudaStream_t st);
 
+// EncP elementwise chains (encp_kernels.cu).
+// out = LayerNorm_C(x + y) * mask over [B][C][T] fp32 (y or len may be null):
+// mean and biased variance over channels, (v - mean) / sqrt(var + eps) *
+// gamma + beta; frames t >= len[b] are multiplied by 0.
+cudaError_t launch_add_layernorm_ncl(const float* x, const float* y, const float* gamma, const float* beta,
+                                     int B, int C, int T, float eps, const int* len, float* out,
+                                     cudaStream_t st);
+// The same LayerNorm (+ mask) of a time-major [B][T][C] tensor in the mode
+// dtype, written as [B][C][T] fp32.
+cudaError_t launch_layernorm_tm_ncl(const void* v, Dt dt, int B, int T, int C, const float* gamma,
+                                    const float* beta, float eps, const int* len, float* out, cudaStream_t st);
+// Half-pixel linear interpolation of each of `rows` rows from T to Tout
+// samples, bit-identical to the reference's f32 evaluation.
+cudaError_t launch_interpolate(const float* x, long long rows, int T, int Tout, float* out, cudaStream_t st);
+// stats [B][T][2 Co] time-major (mode dtype) -> m = stats[:Co] * mask,
+// logs = clamp(stats[Co:] * mask, -5, 2), zp = m + noise * exp(logs) *
+// noise_scale, all [B][Co][T] fp32; any output may be null (zp needs noise).
+cudaError_t launch_prior_sample(const void* stats, Dt dt, int B, int T, int Co, const int* len,
+                                const float* noise, float noise_scale, float* m, float* logs, float* zp,
+                                cudaStream_t st);
+
 }  // namespace gsv

@@ -5,10 +5,13 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <cfloat>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -288,6 +291,68 @@ int load_flow(const gsvdec_tensor* ts, int n, const std::string& prefix, HostFlo
   return GSV_OK;
 }
 
+// Host-side EncP chains, following EncoderLayer::load and FeedForward::load
+// (src/models/sovits_encp.rs:54-96, :348-369): per stack, layers 0, 1, ...
+// while "<stack>.ffn_layers.<i>.conv_1.weight" exists, convs with pad (k-1)/2
+// (load_conv1d :378-410) and both LayerNorm pairs required.  enc_p.proj is a
+// 1x1 conv with pad 0 (:752-771).
+struct HostEncpLayer {
+  HostConv c1, c2;
+  std::vector<float> g1, b1, g2, b2;
+};
+
+struct HostEncp {
+  std::vector<HostEncpLayer> stacks[3];
+  HostConv proj;
+  bool has_proj = false;
+};
+
+const char* const kEncpStacks[3] = {"enc_p.encoder_ssl", "enc_p.encoder_text", "enc_p.encoder2"};
+
+int load_vec(const TensorMap& tm, const std::string& key, int n, std::vector<float>& v) {
+  const gsvdec_tensor* t = tm.get(key);
+  if (!t) return set_err(GSV_E_MISSING_KEY, "Key '%s' not found in state dict", key.c_str());
+  if (numel(t) != n) return set_err(GSV_E_SHAPE, "%s must have %d values", key.c_str(), n);
+  return to_f32(t, v);
+}
+
+int load_encp(const gsvdec_tensor* ts, int n, HostEncp& e) {
+  TensorMap tm;
+  for (int i = 0; i < n; ++i)
+    if (ts[i].name) tm.m[ts[i].name] = &ts[i];
+  int C = 0;
+  for (int s = 0; s < 3; ++s) {
+    const std::string p = kEncpStacks[s];
+    for (int i = 0; i < 64; ++i) {
+      const std::string f = p + ".ffn_layers." + std::to_string(i);
+      if (!tm.get(f + ".conv_1.weight")) break;
+      HostEncpLayer L;
+      GSV_TRY(load_plain(tm, f + ".conv_1", L.c1));
+      GSV_TRY(load_plain(tm, f + ".conv_2", L.c2));
+      if (L.c2.d0 != L.c1.d1 || L.c2.d1 != L.c1.d0)
+        return set_err(GSV_E_SHAPE, "%s: conv_2 [%d,%d] does not invert conv_1 [%d,%d]", f.c_str(), L.c2.d0,
+                       L.c2.d1, L.c1.d0, L.c1.d1);
+      if (C && L.c1.d1 != C) return set_err(GSV_E_SHAPE, "%s: hidden width %d != %d", f.c_str(), L.c1.d1, C);
+      C = L.c1.d1;
+      const std::string is = std::to_string(i);
+      GSV_TRY(load_vec(tm, p + ".norm_layers_1." + is + ".gamma", C, L.g1));
+      GSV_TRY(load_vec(tm, p + ".norm_layers_1." + is + ".beta", C, L.b1));
+      GSV_TRY(load_vec(tm, p + ".norm_layers_2." + is + ".gamma", C, L.g2));
+      GSV_TRY(load_vec(tm, p + ".norm_layers_2." + is + ".beta", C, L.b2));
+      e.stacks[s].push_back(std::move(L));
+    }
+  }
+  if (tm.get("enc_p.proj.weight")) {
+    GSV_TRY(load_plain(tm, "enc_p.proj", e.proj));
+    if (e.proj.K != 1) return set_err(GSV_E_UNSUPPORTED, "enc_p.proj with kernel %d (1 expected)", e.proj.K);
+    if (C && e.proj.d1 != C) return set_err(GSV_E_SHAPE, "enc_p.proj input width %d != %d", e.proj.d1, C);
+    if (e.proj.d0 % 2) return set_err(GSV_E_SHAPE, "enc_p.proj has an odd output width %d", e.proj.d0);
+    e.proj.pad = 0;
+    e.has_proj = true;
+  }
+  return GSV_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Packed device form of one conv as a tap GEMM (see gsv_internal.h).
 
@@ -451,6 +516,18 @@ struct gsvdec {
   std::vector<int> flow_perm_host;
   void* fws = nullptr;
   size_t fws_bytes = 0;
+  // EncP chains (present when the tensors include enc_p.* encoder layers).
+  struct EncpLayer {
+    GemmConv ffn1, ffn2;
+    size_t norm = 0;  // float offset of gamma1, beta1, gamma2, beta2 (C each) in d_encp_norm
+  };
+  std::vector<EncpLayer> encp[3];
+  GemmConv encp_proj;
+  bool has_encp_proj = false;
+  int encp_C = 0, encp_F = 0;
+  float* d_encp_norm = nullptr;
+  void* ews = nullptr;
+  size_t ews_bytes = 0;
 };
 
 namespace gsv {
@@ -750,10 +827,12 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
   } else {
     // Residuals of wide layers enter the tensor-core GEMM as identity-weight
     // segments (no global loads in the epilogue); narrow layers read them in
-    // the epilogue instead (an extra TMA window costs more there than the MMA saves).
+    // the epilogue instead (an extra TMA window costs more there than the MMA
+    // saves), and so do convs whose input width differs from Cout (every GEMM
+    // segment shares one input width).
     for (int i = 0; i < grp.n; ++i) {
       TapConv& op = grp.op[i];
-      if (op.nres == 0 || op.Cout < kIdentityResidualMinC) continue;
+      if (op.nres == 0 || op.Cout < kIdentityResidualMinC || op.seg[0].Cin != op.Cout) continue;
       auto it = h->ident_off.find(op.Cout);
       if (it == h->ident_off.end() || op.N != op.Cout || op.crop != 0 || op.Q != op.Lout ||
           op.nseg + op.nres > kMaxSeg)
@@ -1314,6 +1393,39 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
       if (!all) return set_err(GSV_E_UNSUPPORTED, "a flow layer geometry is not supported by the bf16 tcgen05 kernel");
     }
   }
+  // The EncP chains (optional), packed into the same weight arena.
+  HostEncp he;
+  GSV_TRY(load_encp(ts, n, he));
+  std::vector<float> encp_norm;
+  for (int s = 0; s < 3; ++s)
+    for (const HostEncpLayer& L : he.stacks[s]) {
+      gsvdec::EncpLayer E;
+      E.ffn1 = pk.conv(L.c1);
+      E.ffn2 = pk.conv(L.c2);
+      E.norm = encp_norm.size();
+      for (const std::vector<float>* v : {&L.g1, &L.b1, &L.g2, &L.b2}) encp_norm.insert(encp_norm.end(), v->begin(), v->end());
+      h->encp_C = L.c1.d1;
+      h->encp_F = std::max(h->encp_F, L.c1.d0);
+      h->encp[s].push_back(E);
+    }
+  if (he.has_proj) {
+    h->encp_proj = pk.conv(he.proj);
+    h->has_encp_proj = true;
+    if (!h->encp_C) h->encp_C = he.proj.d1;
+  }
+  if (h->dt == Dt::BF16 && !encp_norm.empty()) {
+    if (!h->ident_off.count(h->encp_C)) h->ident_off[h->encp_C] = pk.identity(h->encp_C);
+    auto ok = [&](const GemmConv& g) {
+      TapConv op{};
+      op.nseg = 1; op.seg[0].Cin = g.Cin; op.seg[0].ntaps = g.ntaps; op.seg[0].offstep = g.offstep;
+      op.seg[0].off0 = g.off0; op.N = g.N; op.Cout = g.Cout;
+      return tapconv_tc_supported(op);
+    };
+    bool all = !h->has_encp_proj || ok(h->encp_proj);
+    for (int s = 0; s < 3; ++s)
+      for (auto& E : h->encp[s]) all = all && ok(E.ffn1) && ok(E.ffn2);
+    if (!all) return set_err(GSV_E_UNSUPPORTED, "an enc_p layer geometry is not supported by the bf16 tcgen05 kernel");
+  }
   h->layer_names += m.post.name + "\n";
   h->post_K = m.post.K;
   h->post_pad = m.post.pad;
@@ -1360,6 +1472,11 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     CUDA_TRY(cudaMemcpy(h->d_flow_perm, h->flow_perm_host.data(), sizeof(int) * h->flow_perm_host.size(),
                         cudaMemcpyHostToDevice));
   }
+  if (!encp_norm.empty()) {
+    CUDA_TRY(cudaMalloc(&h->d_encp_norm, sizeof(float) * encp_norm.size()));
+    CUDA_TRY(cudaMemcpy(h->d_encp_norm, encp_norm.data(), sizeof(float) * encp_norm.size(),
+                        cudaMemcpyHostToDevice));
+  }
   CUDA_TRY(cudaMalloc(&h->d_err, sizeof(int)));
   CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
   for (auto& e : h->ev) CUDA_TRY(cudaEventCreate(&e));
@@ -1383,6 +1500,8 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->d_flow_perm);
   cudaFree(h->d_flow_cond_w);
   cudaFree(h->d_flow_cond_b);
+  cudaFree(h->d_encp_norm);
+  cudaFree(h->ews);
   for (auto& e : h->ev)
     if (e) cudaEventDestroy(e);
   for (auto& run : h->runs)
@@ -1580,6 +1699,219 @@ int flow_impl(gsvdec* h, const float* zp, const float* g, const int32_t* lengths
   return GSV_OK;
 }
 
+// ---------------------------------------------------------------------------
+// EncP fused elementwise chains.
+
+constexpr float kLayerNormEps = 1e-5f;  // LayerNorm::new (src/utils/weights.rs:419-425)
+
+// Scratch of the EncP entry points: `n` regions of the given byte sizes.
+int encp_scratch(gsvdec* h, std::initializer_list<size_t> sizes, std::vector<char*>& out) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  size_t need = 0;
+  for (size_t b : sizes) need += al(b);
+  if (need > h->ews_bytes) {
+    if (h->ews) CUDA_TRY(cudaFree(h->ews));
+    h->ews = nullptr;
+    h->ews_bytes = 0;
+    CUDA_TRY(cudaMalloc(&h->ews, need));
+    h->ews_bytes = need;
+  }
+  char* p = static_cast<char*>(h->ews);
+  out.clear();
+  for (size_t b : sizes) {
+    out.push_back(p);
+    p += al(b);
+  }
+  return GSV_OK;
+}
+
+int encp_common(gsvdec* h, int B, int T, int mem_kind) {
+  if (!h) return set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (B <= 0 || T <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T=%d must be positive", B, T);
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+    return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
+  return GSV_OK;
+}
+
+int encp_layer(gsvdec* h, int stack, int layer, const gsvdec::EncpLayer** L) {
+  if (stack < 0 || stack > 2) return set_err(GSV_E_INVALID_ARG, "bad enc_p stack %d", stack);
+  if (layer < 0 || layer >= (int)h->encp[stack].size())
+    return set_err(GSV_E_INVALID_ARG, "%s has no layer %d (%d loaded)", kEncpStacks[stack], layer,
+                   (int)h->encp[stack].size());
+  *L = &h->encp[stack][layer];
+  return GSV_OK;
+}
+
+// Copies `n` values host -> device scratch in host mode; returns the device pointer.
+template <typename T>
+const T* stage_in(const T* src, size_t n, char* scratch, int mem_kind, cudaStream_t st, int* rc) {
+  if (!src || mem_kind == GSV_MEM_DEVICE) return src;
+  const cudaError_t e = cudaMemcpyAsync(scratch, src, sizeof(T) * n, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) *rc = set_err(GSV_E_CUDA, "host to device copy failed: %s", cudaGetErrorString(e));
+  return reinterpret_cast<const T*>(scratch);
+}
+
+int finish_host(gsvdec* h, cudaStream_t st, std::initializer_list<std::pair<float*, const float*>> outs,
+                size_t n, int mem_kind) {
+  if (mem_kind != GSV_MEM_HOST) return GSV_OK;
+  for (const auto& o : outs)
+    if (o.first) CUDA_TRY(cudaMemcpyAsync(o.first, o.second, sizeof(float) * n, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  return check_device_error(h);
+}
+
+int encp_add_norm_impl(gsvdec* h, int stack, int layer, int norm, const float* x, const float* y,
+                       const int32_t* lengths, int B, int T, float* out, int mem_kind, cudaStream_t st) {
+  GSV_TRY(encp_common(h, B, T, mem_kind));
+  if (!x || !out) return set_err(GSV_E_INVALID_ARG, "x and out must not be NULL");
+  if (norm != 1 && norm != 2) return set_err(GSV_E_INVALID_ARG, "norm must be 1 or 2, got %d", norm);
+  const gsvdec::EncpLayer* L = nullptr;
+  GSV_TRY(encp_layer(h, stack, layer, &L));
+  const int C = h->encp_C;
+  const size_t n = (size_t)B * C * T;
+  CUDA_TRY(cudaSetDevice(h->device));
+  std::vector<char*> sc;
+  GSV_TRY(encp_scratch(h, {n * 4, n * 4, n * 4, (size_t)B * 4}, sc));
+  int rc = GSV_OK;
+  const float* xd = stage_in(x, n, sc[0], mem_kind, st, &rc);
+  const float* yd = stage_in(y, n, sc[1], mem_kind, st, &rc);
+  const int* ld = stage_in(lengths, (size_t)B, sc[3], mem_kind, st, &rc);
+  GSV_TRY(rc);
+  float* od = mem_kind == GSV_MEM_DEVICE ? out : reinterpret_cast<float*>(sc[2]);
+  begin_run(h, st);
+  const float* g = h->d_encp_norm + L->norm + (size_t)(norm - 1) * 2 * C;
+  CUDA_TRY(launch_add_layernorm_ncl(xd, yd, g, g + C, B, C, T, kLayerNormEps, ld, od, st));
+  GSV_TRY(after_launch(h, st, "encp.add_norm", 1, 0, 0.0, 4.0 * n * (y ? 3 : 2)));
+  return finish_host(h, st, {{out, od}}, n, mem_kind);
+}
+
+int encp_ffn_impl(gsvdec* h, int stack, int layer, const float* x, const int32_t* lengths, int B, int T,
+                  float* out, int mem_kind, cudaStream_t st) {
+  GSV_TRY(encp_common(h, B, T, mem_kind));
+  if (!x || !out) return set_err(GSV_E_INVALID_ARG, "x and out must not be NULL");
+  const gsvdec::EncpLayer* L = nullptr;
+  GSV_TRY(encp_layer(h, stack, layer, &L));
+  const int C = h->encp_C, F = L->ffn1.Cout;
+  if ((int64_t)B * T * F > (int64_t)1 << 34) return set_err(GSV_E_INVALID_ARG, "request too large");
+  const size_t n = (size_t)B * C * T, eb = act_bytes(h);
+  CUDA_TRY(cudaSetDevice(h->device));
+  std::vector<char*> sc;
+  GSV_TRY(encp_scratch(h, {n * 4, n * 4, n * eb, (size_t)B * T * F * eb, n * eb, (size_t)B * 4}, sc));
+  int rc = GSV_OK;
+  const float* xd = stage_in(x, n, sc[0], mem_kind, st, &rc);
+  const int* ld = stage_in(lengths, (size_t)B, sc[5], mem_kind, st, &rc);
+  GSV_TRY(rc);
+  float* od = mem_kind == GSV_MEM_DEVICE ? out : reinterpret_cast<float*>(sc[1]);
+  void* xt = sc[2];
+  void* ht = sc[3];
+  void* vt = sc[4];
+  begin_run(h, st);
+  const double e = (double)eb;
+  CUDA_TRY(launch_transpose_in(xd, B, C, T, 0, T, nullptr, xt, h->dt, st));
+  GSV_TRY(after_launch(h, st, "encp.input_relayout", 1, 0, 0.0, (4.0 + e) * n));
+  const std::string nm = std::string(kEncpStacks[stack]) + ".ffn." + std::to_string(layer);
+  {
+    // conv_1 + bias + ReLU (LeakyReLU slope 0) in the epilogue.
+    TapConv op = make_op(h, L->ffn1, B, xt, T);
+    op.out_act = ht;
+    op.slope = 0.0f;
+    Work wk;
+    wk.add(L->ffn1, B, T, 0, e);
+    GSV_TRY(run_one(h, op, st, nm + ".conv_1+relu", wk));
+  }
+  {
+    // conv_2 + bias + the residual x.
+    TapConv op = make_op(h, L->ffn2, B, ht, T);
+    op.res[0] = xt;
+    op.nres = 1;
+    op.out_raw = vt;
+    Work wk;
+    wk.add(L->ffn2, B, T, 1, e);
+    GSV_TRY(run_one(h, op, st, nm + ".conv_2+res", wk));
+  }
+  const float* g = h->d_encp_norm + L->norm + 2 * (size_t)C;
+  CUDA_TRY(launch_layernorm_tm_ncl(vt, h->dt, B, T, C, g, g + C, kLayerNormEps, ld, od, st));
+  GSV_TRY(after_launch(h, st, nm + ".norm2+mask", 1, 0, 0.0, (e + 4.0) * n));
+  return finish_host(h, st, {{out, od}}, n, mem_kind);
+}
+
+int encp_speed_len(int T, float speed, int* T_out) {
+  if (!T_out) return set_err(GSV_E_INVALID_ARG, "T_out is NULL");
+  if (T <= 0) return set_err(GSV_E_INVALID_ARG, "T=%d must be positive", T);
+  if (std::fabs(speed - 1.0f) <= FLT_EPSILON) {
+    *T_out = T;
+    return GSV_OK;
+  }
+  if (!std::isfinite(speed) || speed <= 0.0f)
+    return set_err(GSV_E_INVALID_ARG, "speed must be finite and positive, got %g", (double)speed);
+  const float q = (float)T / speed;  // f32 division, then a truncating cast
+  if (!(q < 2147483000.0f)) return set_err(GSV_E_INVALID_ARG, "speed %g gives too many frames", (double)speed);
+  *T_out = std::max(1, (int)q + 1);
+  return GSV_OK;
+}
+
+int encp_interp_impl(gsvdec* h, const float* y, int B, int C, int T, int T_out, float* out, int mem_kind,
+                     cudaStream_t st) {
+  GSV_TRY(encp_common(h, B, T, mem_kind));
+  if (!y || !out) return set_err(GSV_E_INVALID_ARG, "y and out must not be NULL");
+  if (C <= 0 || T_out <= 0) return set_err(GSV_E_INVALID_ARG, "interpolation length must be positive");
+  const size_t ni = (size_t)B * C * T, no = (size_t)B * C * T_out;
+  CUDA_TRY(cudaSetDevice(h->device));
+  if (T_out == T) {  // the reference returns its input unchanged
+    const cudaMemcpyKind k = mem_kind == GSV_MEM_HOST ? cudaMemcpyHostToHost : cudaMemcpyDeviceToDevice;
+    CUDA_TRY(cudaMemcpyAsync(out, y, ni * 4, k, st));
+    if (mem_kind == GSV_MEM_HOST) CUDA_TRY(cudaStreamSynchronize(st));
+    return GSV_OK;
+  }
+  std::vector<char*> sc;
+  GSV_TRY(encp_scratch(h, {ni * 4, no * 4}, sc));
+  int rc = GSV_OK;
+  const float* yd = stage_in(y, ni, sc[0], mem_kind, st, &rc);
+  GSV_TRY(rc);
+  float* od = mem_kind == GSV_MEM_DEVICE ? out : reinterpret_cast<float*>(sc[1]);
+  begin_run(h, st);
+  CUDA_TRY(launch_interpolate(yd, (long long)B * C, T, T_out, od, st));
+  GSV_TRY(after_launch(h, st, "encp.interpolate", 1, 0, 0.0, 4.0 * (double)(ni + no)));
+  return finish_host(h, st, {{out, od}}, no, mem_kind);
+}
+
+int encp_project_impl(gsvdec* h, const float* y, const int32_t* lengths, int B, int T, const float* noise,
+                      float noise_scale, float* m, float* logs, float* zp, int mem_kind, cudaStream_t st) {
+  GSV_TRY(encp_common(h, B, T, mem_kind));
+  if (!h->has_encp_proj) return set_err(GSV_E_UNSUPPORTED, "this handle was created without enc_p.proj");
+  if (!y) return set_err(GSV_E_INVALID_ARG, "y must not be NULL");
+  if (zp && !noise) return set_err(GSV_E_INVALID_ARG, "z_p needs noise");
+  const int C = h->encp_proj.Cin, Co = h->encp_proj.Cout / 2;
+  const size_t n = (size_t)B * C * T, no = (size_t)B * Co * T, eb = act_bytes(h);
+  CUDA_TRY(cudaSetDevice(h->device));
+  std::vector<char*> sc;
+  GSV_TRY(encp_scratch(h, {n * 4, n * eb, 2 * no * eb, no * 4, no * 4, no * 4, no * 4, (size_t)B * 4}, sc));
+  int rc = GSV_OK;
+  const float* yd = stage_in(y, n, sc[0], mem_kind, st, &rc);
+  const float* nd = stage_in(noise, no, sc[3], mem_kind, st, &rc);
+  const int* ld = stage_in(lengths, (size_t)B, sc[7], mem_kind, st, &rc);
+  GSV_TRY(rc);
+  const bool dev = mem_kind == GSV_MEM_DEVICE;
+  float* md = m ? (dev ? m : reinterpret_cast<float*>(sc[4])) : nullptr;
+  float* lsd = logs ? (dev ? logs : reinterpret_cast<float*>(sc[5])) : nullptr;
+  float* zd = zp ? (dev ? zp : reinterpret_cast<float*>(sc[6])) : nullptr;
+  begin_run(h, st);
+  const double e = (double)eb;
+  CUDA_TRY(launch_transpose_in(yd, B, C, T, 0, T, nullptr, sc[1], h->dt, st));
+  GSV_TRY(after_launch(h, st, "encp.input_relayout", 1, 0, 0.0, (4.0 + e) * n));
+  {
+    TapConv op = make_op(h, h->encp_proj, B, sc[1], T);
+    op.out_raw = sc[2];
+    Work wk;
+    wk.add(h->encp_proj, B, T, 0, e);
+    GSV_TRY(run_one(h, op, st, "enc_p.proj", wk));
+  }
+  CUDA_TRY(launch_prior_sample(sc[2], h->dt, B, T, Co, ld, nd, noise_scale, md, lsd, zd, st));
+  GSV_TRY(after_launch(h, st, "encp.prior_sample", 1, 0, 0.0,
+                       2.0 * e * no + 4.0 * no * ((m ? 1 : 0) + (logs ? 1 : 0) + (zp ? 2 : 0))));
+  return finish_host(h, st, {{m, md}, {logs, lsd}, {zp, zd}}, no, mem_kind);
+}
+
 }  // namespace
 }  // namespace gsv
 
@@ -1714,6 +2046,42 @@ int gsvdec_flow_inverse(gsvdec_t* h, const float* z_p, const float* g, const int
 int gsvdec_flow_decode(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths, int B,
                        int T0, float* wav, int mem_kind, void* stream) {
   return gsv::flow_impl(h, z_p, g, lengths, B, T0, wav, mem_kind, static_cast<cudaStream_t>(stream), true);
+}
+
+int gsvdec_encp_info(const gsvdec_t* h, int n_layers[3], int* channels, int* filter_channels,
+                     int* proj_channels) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (n_layers)
+    for (int s = 0; s < 3; ++s) n_layers[s] = (int)h->encp[s].size();
+  if (channels) *channels = h->encp_C;
+  if (filter_channels) *filter_channels = h->encp_F;
+  if (proj_channels) *proj_channels = h->has_encp_proj ? h->encp_proj.Cout : 0;
+  return GSV_OK;
+}
+
+int gsvdec_encp_add_norm(gsvdec_t* h, int stack, int layer, int norm, const float* x, const float* y,
+                         const int32_t* lengths, int B, int T, float* out, int mem_kind, void* stream) {
+  return gsv::encp_add_norm_impl(h, stack, layer, norm, x, y, lengths, B, T, out, mem_kind,
+                                 static_cast<cudaStream_t>(stream));
+}
+
+int gsvdec_encp_ffn(gsvdec_t* h, int stack, int layer, const float* x, const int32_t* lengths, int B,
+                    int T, float* out, int mem_kind, void* stream) {
+  return gsv::encp_ffn_impl(h, stack, layer, x, lengths, B, T, out, mem_kind, static_cast<cudaStream_t>(stream));
+}
+
+int gsvdec_encp_speed_len(int T, float speed, int* T_out) { return gsv::encp_speed_len(T, speed, T_out); }
+
+int gsvdec_encp_interpolate(gsvdec_t* h, const float* y, int B, int C, int T, int T_out, float* out,
+                            int mem_kind, void* stream) {
+  return gsv::encp_interp_impl(h, y, B, C, T, T_out, out, mem_kind, static_cast<cudaStream_t>(stream));
+}
+
+int gsvdec_encp_project(gsvdec_t* h, const float* y, const int32_t* lengths, int B, int T,
+                        const float* noise, float noise_scale, float* m, float* logs, float* z_p,
+                        int mem_kind, void* stream) {
+  return gsv::encp_project_impl(h, y, lengths, B, T, noise, noise_scale, m, logs, z_p, mem_kind,
+                                static_cast<cudaStream_t>(stream));
 }
 
 int gsvdec_layer_forward(gsvdec_t* h, const char* layer, const float* x, int B, int L, float* y,

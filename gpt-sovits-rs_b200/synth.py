@@ -131,6 +131,45 @@ def make_flow_state_dict(seed: int = 10, gin: int = 512, init: str = "unit", bia
     return sd
 
 
+ENCP_HIDDEN = 192
+ENCP_FILTER = 768
+ENCP_KERNEL = 3
+ENCP_LAYERS = {"encoder_ssl": 3, "encoder_text": 6, "encoder2": 3}  # n_layers // 2, n_layers, n_layers // 2
+ENCP_OUT = 192
+
+
+def make_encp_state_dict(seed: int = 20, layers=None, hidden: int = ENCP_HIDDEN,
+                         filter_channels: int = ENCP_FILTER, kernel: int = ENCP_KERNEL,
+                         out_channels: int = ENCP_OUT, with_proj: bool = True) -> dict:
+    """The ``enc_p.*`` tensors (float32) the EncP chains read, seeded, under the
+    keys of EncoderLayer::load / FeedForward::load (reference
+    src/models/sovits_encp.rs:54-96, 348-369, 752-771): per layer i of each
+    stack ``ffn_layers.{i}.conv_1`` [F, C, k] and ``conv_2`` [C, F, k] with
+    biases, ``norm_layers_{1,2}.{i}.{gamma, beta}`` [C]; and ``enc_p.proj``
+    [2 out, C, 1] with bias.  Attention weights are not generated (the
+    attention itself is not part of these chains)."""
+    rng = np.random.default_rng(seed)
+    layers = ENCP_LAYERS if layers is None else layers
+    sd = {}
+    C, F, k = hidden, filter_channels, kernel
+    for stack, n in layers.items():
+        p = f"enc_p.{stack}"
+        for i in range(n):
+            f = f"{p}.ffn_layers.{i}"
+            sd[f + ".conv_1.weight"] = rng.standard_normal((F, C, k), dtype=np.float32) * np.float32((C * k) ** -0.5)
+            sd[f + ".conv_1.bias"] = rng.standard_normal(F, dtype=np.float32) * np.float32(0.05)
+            sd[f + ".conv_2.weight"] = rng.standard_normal((C, F, k), dtype=np.float32) * np.float32((F * k) ** -0.5)
+            sd[f + ".conv_2.bias"] = rng.standard_normal(C, dtype=np.float32) * np.float32(0.05)
+            for nl in (1, 2):
+                sd[f"{p}.norm_layers_{nl}.{i}.gamma"] = (
+                    1.0 + 0.1 * rng.standard_normal(C, dtype=np.float32)).astype(np.float32)
+                sd[f"{p}.norm_layers_{nl}.{i}.beta"] = rng.standard_normal(C, dtype=np.float32) * np.float32(0.1)
+    if with_proj:
+        sd["enc_p.proj.weight"] = rng.standard_normal((2 * out_channels, C, 1), dtype=np.float32) * np.float32(C ** -0.5)
+        sd["enc_p.proj.bias"] = rng.standard_normal(2 * out_channels, dtype=np.float32) * np.float32(0.5)
+    return sd
+
+
 def make_inputs(B: int, T0: int, gin: int = 512, seed_z: int = 1, seed_g: int = 2):
     """z [B,192,T0] ~ N(0,1) and g [B,gin,1] ~ N(0,1), seeded."""
     z = np.random.default_rng(seed_z).standard_normal((B, IN_CHANNELS, T0), dtype=np.float32)

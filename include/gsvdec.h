@@ -149,6 +149,60 @@ int gsvdec_flow_inverse(gsvdec_t* h, const float* z_p, const float* g, const int
 int gsvdec_flow_decode(gsvdec_t* h, const float* z_p, const float* g, const int32_t* lengths,
                        int B, int T0, float* wav, int mem_kind, void* stream);
 
+/* ---- EncP fused elementwise chains (optional) ----------------------------
+ * Present when the tensors include enc_p.* encoder layers: per layer i of a
+ * stack, "<stack>.ffn_layers.<i>.conv_{1,2}.{weight,bias}" and
+ * "<stack>.norm_layers_{1,2}.<i>.{gamma,beta}" (EncoderLayer::load,
+ * src/models/sovits_encp.rs:54-96; FeedForward::load :348-369), and
+ * "enc_p.proj.{weight,bias}" (:752-771).  Stacks: */
+#define GSV_ENCP_SSL 0  /* enc_p.encoder_ssl  */
+#define GSV_ENCP_TEXT 1 /* enc_p.encoder_text */
+#define GSV_ENCP_2 2    /* enc_p.encoder2     */
+
+/* Layers per stack (n_layers[3], 0 when absent), hidden channels, FFN filter
+ * channels and projection outputs (2 * out_channels; 0 without enc_p.proj). */
+int gsvdec_encp_info(const gsvdec_t* h, int n_layers[3], int* channels, int* filter_channels,
+                     int* proj_channels);
+
+/* out = norm_layers_<norm>[layer](x + y) (norm = 1 or 2): the post-norm
+ * residual of EncoderLayer::forward (src/models/sovits_encp.rs:102, :107)
+ * with LayerNorm::forward over the channel axis (src/utils/weights.rs:461-502:
+ * mean, biased variance, (v - mean) / sqrt(var + 1e-5) * gamma + beta).
+ * x, y, out [B, C, T] fp32; y may be NULL (LayerNorm of x alone); with
+ * lengths, frames t >= lengths[b] are multiplied by 0 (the x_mask product,
+ * :109). */
+int gsvdec_encp_add_norm(gsvdec_t* h, int stack, int layer, int norm, const float* x, const float* y,
+                         const int32_t* lengths, int B, int T, float* out, int mem_kind, void* stream);
+
+/* The FFN half of EncoderLayer::forward (src/models/sovits_encp.rs:104-109):
+ * out = norm_layers_2[layer](x + conv_2(relu(conv_1(x)))) * x_mask, convs
+ * with pad (k-1)/2 (FeedForward::forward :371-375, load_conv1d :378-410).
+ * ReLU runs in conv_1's epilogue, the residual in conv_2's, LayerNorm + mask
+ * + relayout in one pass.  x, out [B, C, T] fp32; lengths [B] or NULL. */
+int gsvdec_encp_ffn(gsvdec_t* h, int stack, int layer, const float* x, const int32_t* lengths, int B,
+                    int T, float* out, int mem_kind, void* stream);
+
+/* Output length of the speed change (src/models/sovits_encp.rs:857-867):
+ * T when |speed - 1| <= FLT_EPSILON, else max(1, trunc(T / speed) + 1).
+ * GSV_E_INVALID_ARG for a non-finite or non-positive speed. */
+int gsvdec_encp_speed_len(int T, float speed, int* T_out);
+
+/* linear_interpolate_last_dim (src/models/sovits_encp.rs:10-40): y [B, C, T]
+ * -> out [B, C, T_out] fp32, half-pixel sampling, bit-identical to the
+ * reference's f32 evaluation.  T_out == T copies. */
+int gsvdec_encp_interpolate(gsvdec_t* h, const float* y, int B, int C, int T, int T_out, float* out,
+                            int mem_kind, void* stream);
+
+/* EncP output projection and prior sample: stats = proj(y) * y_mask;
+ * m = stats[:, :Co]; logs = clamp(stats[:, Co:], -5, 2)
+ * (src/models/sovits_encp.rs:871-879); z_p = m + noise * exp(logs) *
+ * noise_scale (src/models/sovits.rs:378-385, the noise drawn by the caller).
+ * y [B, C, T]; noise, m, logs, z_p [B, Co, T] fp32; lengths [B] or NULL.
+ * m, logs and z_p may each be NULL (not written); z_p needs noise. */
+int gsvdec_encp_project(gsvdec_t* h, const float* y, const int32_t* lengths, int B, int T,
+                        const float* noise, float noise_scale, float* m, float* logs, float* z_p,
+                        int mem_kind, void* stream);
+
 /* One conv layer of the Generator, named by its dec.* prefix ("dec.conv_pre",
  * "dec.ups.3", "dec.resblocks.7.convs1.2", "dec.conv_post", ...; see
  * gsvdec_layer_names), on x [B, Cin, L] -> y [B, Cout, Lout] in the

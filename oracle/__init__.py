@@ -61,6 +61,14 @@ def _load():
         lib.gsvo_flow_inverse.argtypes = [ctypes.POINTER(_Tensor), ctypes.c_int, ctypes.c_char_p, fp,
                                           fp, ctypes.POINTER(ctypes.c_int), ctypes.c_int,
                                           ctypes.c_int, fp, ctypes.c_int, ctypes.c_int]
+        ip = ctypes.POINTER(ctypes.c_int)
+        lib.gsvo_layer_norm.argtypes = [fp, fp, fp, fp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_float, ip, fp]
+        lib.gsvo_encp_ffn.argtypes = [fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, fp, fp, ctypes.c_int,
+                                      ctypes.c_int, fp, fp, ctypes.c_int, fp, fp, ip, fp, ctypes.c_int]
+        lib.gsvo_interpolate.argtypes = [fp, ctypes.c_int64, ctypes.c_int, ctypes.c_int, fp]
+        lib.gsvo_encp_project.argtypes = [fp, ctypes.c_int, ctypes.c_int, ctypes.c_int, fp, fp, ctypes.c_int,
+                                          ip, fp, ctypes.c_float, fp, fp, fp, ctypes.c_int]
         _lib = lib
     return _lib
 
@@ -217,3 +225,83 @@ def flow_inverse(state_dict, z_p, g=None, lengths=None, prefix="flow.flows", acc
 
 def num_threads() -> int:
     return os.cpu_count() or 1
+
+
+def _lengths(lengths, B, keep):
+    if lengths is None:
+        return None
+    la = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
+    if la.shape != (B,):
+        raise ValueError("lengths must hold one value per utterance")
+    keep.append(la)
+    return la.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+
+
+def layer_norm(x, gamma, beta, y=None, lengths=None, eps: float = 1e-5):
+    """LayerNorm over channels of x (+ y) [B, C, T], times x_mask with lengths
+    (reference src/utils/weights.rs:461-502; src/models/sovits_encp.rs:102-109)."""
+    x = _f32(x)
+    B, C, T = x.shape
+    yy = _f32(y) if y is not None else None
+    keep = []
+    out = np.empty_like(x)
+    _check(_load().gsvo_layer_norm(_fp(x), _fp(yy), _fp(_f32(gamma)), _fp(_f32(beta)), B, C, T, eps,
+                                   _lengths(lengths, B, keep), _fp(out)))
+    return out
+
+
+def encp_ffn(state_dict, stack: str, layer: int, x, lengths=None, acc64=True):
+    """norm_layers_2[layer](x + conv_2(relu(conv_1(x)))) * x_mask of one enc_p
+    encoder layer (reference src/models/sovits_encp.rs:104-109, 371-375)."""
+    p = f"enc_p.{stack}"
+    f = f"{p}.ffn_layers.{layer}"
+    w1, w2 = _f32(state_dict[f + ".conv_1.weight"]), _f32(state_dict[f + ".conv_2.weight"])
+    b1, b2 = _f32(state_dict[f + ".conv_1.bias"]), _f32(state_dict[f + ".conv_2.bias"])
+    g = _f32(state_dict[f"{p}.norm_layers_2.{layer}.gamma"])
+    be = _f32(state_dict[f"{p}.norm_layers_2.{layer}.beta"])
+    x = _f32(x)
+    B, C, T = x.shape
+    keep = []
+    out = np.empty_like(x)
+    _check(_load().gsvo_encp_ffn(_fp(x), B, C, T, _fp(w1), _fp(b1), w1.shape[0], w1.shape[2], _fp(w2),
+                                 _fp(b2), w2.shape[2], _fp(g), _fp(be), _lengths(lengths, B, keep),
+                                 _fp(out), int(acc64)))
+    return out
+
+
+def speed_len(T: int, speed: float) -> int:
+    """Frames after the speed change (reference src/models/sovits_encp.rs:857-867)."""
+    s = np.float32(speed)
+    if abs(s - np.float32(1.0)) <= np.finfo(np.float32).eps:
+        return T
+    if not np.isfinite(s) or s <= 0:
+        raise OracleError(f"speed must be finite and positive, got {speed}")
+    return max(1, int(np.float32(T) / s) + 1)
+
+
+def interpolate(x, T_out: int):
+    """linear_interpolate_last_dim (reference src/models/sovits_encp.rs:10-40)."""
+    x = _f32(x)
+    T = x.shape[-1]
+    rows = int(np.prod(x.shape[:-1]))
+    out = np.empty(x.shape[:-1] + (T_out,), np.float32)
+    _check(_load().gsvo_interpolate(_fp(x), rows, T, T_out, _fp(out)))
+    return out
+
+
+def encp_project(state_dict, y, lengths=None, noise=None, noise_scale: float = 0.5, acc64=True):
+    """(m, logs, z_p) of the EncP output projection and the prior sample
+    (reference src/models/sovits_encp.rs:871-879; src/models/sovits.rs:378-385)."""
+    w = _f32(state_dict["enc_p.proj.weight"])
+    b = _f32(state_dict["enc_p.proj.bias"]) if "enc_p.proj.bias" in state_dict else None
+    y = _f32(y)
+    B, C, T = y.shape
+    co = w.shape[0] // 2
+    keep = []
+    nz = _f32(noise) if noise is not None else None
+    m = np.empty((B, co, T), np.float32)
+    logs = np.empty_like(m)
+    zp = np.empty_like(m) if nz is not None else None
+    _check(_load().gsvo_encp_project(_fp(y), B, C, T, _fp(w), _fp(b), w.shape[0], _lengths(lengths, B, keep),
+                                     _fp(nz), noise_scale, _fp(m), _fp(logs), _fp(zp), int(acc64)))
+    return m, logs, zp

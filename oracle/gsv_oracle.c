@@ -620,3 +620,134 @@ out:
   free_flow(&f);
   return rc;
 }
+
+/* ---- EncP elementwise chains -------------------------------------------- */
+
+/* LayerNorm over the channel axis of [B, C, T] (src/utils/weights.rs:461-502,
+ * the middle-dimension branch): per (b, t) mean over c, biased variance of
+ * the centred values, (v - mean) / sqrt(var + eps) * gamma + beta.  The input
+ * is x + y when y is given (the post-norm residual add of EncoderLayer::forward,
+ * src/models/sovits_encp.rs:102, :107), added in f32 as the reference does;
+ * statistics accumulate in double.  With lengths, frames t >= lengths[b] are
+ * multiplied by 0.0f (x.broadcast_mul(x_mask), :109). */
+int gsvo_layer_norm(const float* x, const float* y, const float* gamma, const float* beta, int B, int C,
+                    int T, float eps, const int* lengths, float* out) {
+  if (B <= 0 || C <= 0 || T <= 0) return fail("layer_norm: empty shape", NULL);
+#pragma omp parallel for schedule(static)
+  for (int64_t bt = 0; bt < (int64_t)B * T; ++bt) {
+    const int b = (int)(bt / T), t = (int)(bt % T);
+    const int64_t base = (int64_t)b * C * T + t;
+    double sum = 0.0;
+    for (int c = 0; c < C; ++c) {
+      float v = x[base + (int64_t)c * T];
+      if (y) v = v + y[base + (int64_t)c * T];
+      sum += v;
+    }
+    const double mean = sum / C;
+    double sq = 0.0;
+    for (int c = 0; c < C; ++c) {
+      float v = x[base + (int64_t)c * T];
+      if (y) v = v + y[base + (int64_t)c * T];
+      sq += (v - mean) * (v - mean);
+    }
+    const double sd = sqrt(sq / C + (double)eps);
+    const float mk = (lengths && t >= lengths[b]) ? 0.0f : 1.0f;
+    for (int c = 0; c < C; ++c) {
+      float v = x[base + (int64_t)c * T];
+      if (y) v = v + y[base + (int64_t)c * T];
+      const float o = (float)((v - mean) / sd * gamma[c] + beta[c]);
+      out[base + (int64_t)c * T] = o * mk;
+    }
+  }
+  return 0;
+}
+
+/* The FFN half of EncoderLayer::forward (src/models/sovits_encp.rs:104-109):
+ * out = LayerNorm2(x + conv_2(relu(conv_1(x)))) * x_mask, FeedForward::forward
+ * (:371-375) with both convs padded (k - 1) / 2 (load_conv1d :378-410) and no
+ * mask between them.  x, out [B, C, T]; w1 [F, C, k1]; w2 [C, F, k2]. */
+int gsvo_encp_ffn(const float* x, int B, int C, int T, const float* w1, const float* b1, int F, int k1,
+                  const float* w2, const float* b2, int k2, const float* gamma, const float* beta,
+                  const int* lengths, float* out, int acc64) {
+  float* h = (float*)malloc(sizeof(float) * (size_t)B * F * T);
+  float* y = (float*)malloc(sizeof(float) * (size_t)B * C * T);
+  int rc = (h && y) ? 0 : fail("encp_ffn: out of memory", NULL);
+  if (!rc) rc = gsvo_conv1d(x, B, C, T, w1, F, k1, (k1 - 1) / 2, 1, b1, h, acc64);
+  if (!rc) {
+    for (int64_t i = 0; i < (int64_t)B * F * T; ++i) h[i] = h[i] > 0.0f ? h[i] : 0.0f;
+    rc = gsvo_conv1d(h, B, F, T, w2, C, k2, (k2 - 1) / 2, 1, b2, y, acc64);
+  }
+  if (!rc) rc = gsvo_layer_norm(x, y, gamma, beta, B, C, T, 1e-5f, lengths, out);
+  free(h);
+  free(y);
+  return rc;
+}
+
+/* linear_interpolate_last_dim (src/models/sovits_encp.rs:10-40): for each
+ * output index i, source = max((i + 0.5) * (T / T_out) - 0.5, 0), low =
+ * min(floor(source), T - 1), up = min(low + 1, T - 1), wu = source - low,
+ * wl = wu * -1 + 1 (the affine), out = x[low] * wl + x[up] * wu, every step
+ * rounded in f32 (the Makefile builds with -ffp-contract=off, so no step is
+ * fused into an FMA).  T_out == T copies. */
+int gsvo_interpolate(const float* x, int64_t rows, int T, int T_out, float* out) {
+  if (T <= 0 || T_out <= 0) return fail("interpolation length must be positive", NULL);
+  if (T_out == T) {
+    memcpy(out, x, sizeof(float) * (size_t)rows * T);
+    return 0;
+  }
+  const float scale = (float)T / (float)T_out;
+  for (int i = 0; i < T_out; ++i) {
+    float a = (float)i + 0.5f;
+    float bsc = a * scale;
+    float src = bsc - 0.5f;
+    if (src < 0.0f) src = 0.0f;
+    int low = (int)floorf(src);
+    if (low > T - 1) low = T - 1;
+    const int up = low + 1 < T - 1 ? low + 1 : T - 1;
+    float wu = src - (float)low;
+    float neg = wu * -1.0f;
+    const float wl = neg + 1.0f;
+    for (int64_t r = 0; r < rows; ++r) {
+      float p = x[r * T + low] * wl;
+      float q = x[r * T + up] * wu;
+      out[r * T_out + i] = p + q;
+    }
+  }
+  return 0;
+}
+
+/* EncP output projection and prior sample: stats = proj(y) * y_mask (a 1x1
+ * conv, pad 0), m = stats[:, :Co], logs = clamp(stats[:, Co:], -5, 2)
+ * (src/models/sovits_encp.rs:871-879), z_p = m + (noise * exp(logs)) *
+ * noise_scale (src/models/sovits.rs:378-385).  w [2 Co, C, 1].  m, logs, z_p
+ * may be NULL; z_p needs noise. */
+int gsvo_encp_project(const float* y, int B, int C, int T, const float* w, const float* bias, int Co2,
+                      const int* lengths, const float* noise, float noise_scale, float* m, float* logs,
+                      float* z_p, int acc64) {
+  if (Co2 % 2) return fail("encp_project: odd projection width", NULL);
+  const int Co = Co2 / 2;
+  float* st = (float*)malloc(sizeof(float) * (size_t)B * Co2 * T);
+  if (!st) return fail("encp_project: out of memory", NULL);
+  int rc = gsvo_conv1d(y, B, C, T, w, Co2, 1, 0, 1, bias, st, acc64);
+  if (!rc) {
+    for (int b = 0; b < B; ++b)
+      for (int c = 0; c < Co; ++c)
+        for (int t = 0; t < T; ++t) {
+          const float mk = (lengths && t >= lengths[b]) ? 0.0f : 1.0f;
+          const float mv = st[((int64_t)b * Co2 + c) * T + t] * mk;
+          float lv = st[((int64_t)b * Co2 + Co + c) * T + t] * mk;
+          lv = lv < -5.0f ? -5.0f : lv;
+          lv = lv > 2.0f ? 2.0f : lv;
+          const int64_t o = ((int64_t)b * Co + c) * T + t;
+          if (m) m[o] = mv;
+          if (logs) logs[o] = lv;
+          if (z_p) {
+            float e = noise[o] * expf(lv);
+            float s = e * noise_scale;
+            z_p[o] = mv + s;
+          }
+        }
+  }
+  free(st);
+  return rc;
+}

@@ -31,6 +31,17 @@ int gsvo_flow_inverse(const gsvo_tensor* ts, int n_tensors, const char* prefix, 
                       const float* g, const int* lengths, int B, int T0, float* z, int acc64,
                       int nthreads);
 
+/* EncP elementwise chains (src/models/sovits_encp.rs), see gsv_oracle.c. */
+int gsvo_layer_norm(const float* x, const float* y, const float* gamma, const float* beta, int B, int C,
+                    int T, float eps, const int* lengths, float* out);
+int gsvo_encp_ffn(const float* x, int B, int C, int T, const float* w1, const float* b1, int F, int k1,
+                  const float* w2, const float* b2, int k2, const float* gamma, const float* beta,
+                  const int* lengths, float* out, int acc64);
+int gsvo_interpolate(const float* x, int64_t rows, int T, int T_out, float* out);
+int gsvo_encp_project(const float* y, int B, int C, int T, const float* w, const float* bias, int Co2,
+                      const int* lengths, const float* noise, float noise_scale, float* m, float* logs,
+                      float* z_p, int acc64);
+
 #ifdef __cplusplus
 }
 #endif

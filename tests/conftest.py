@@ -37,6 +37,15 @@ def tiny():
 
 
 @pytest.fixture(scope="session")
+def encp_golden():
+    return dict(np.load(GOLDEN / "encp_tiny.npz"))
+
+
+# enc_p layers of the golden fixtures (one per stack).
+ENCP_GOLDEN_LAYERS = {"encoder_ssl": 1, "encoder_text": 1, "encoder2": 1}
+
+
+@pytest.fixture(scope="session")
 def flow_golden():
     return dict(np.load(GOLDEN / "flow_tiny.npz"))
 

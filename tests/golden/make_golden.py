@@ -17,6 +17,10 @@ independent of both the C oracle and the CUDA library.  Inputs:
 * ``decoder_tiny.npz`` -- whole-Generator outputs for seeded weights
   (synth.make_state_dict) at T0 in {1, 2, 3, 7}, B = 2, two inits; the
   state-dict checksum is stored to detect generator drift.
+* ``encp_tiny.npz`` -- the EncP chains for seeded enc_p weights
+  (synth.make_encp_state_dict with one layer per stack): add + LayerNorm,
+  the FFN half, the output projection + prior sample, B = 2, T in {1, 4, 37}
+  with lengths (T, ceil(T/2)); interpolation 37 -> 30 and 37 -> 50 frames.
 * ``flow_tiny.npz`` -- flow inverse (ResidualCouplingBlock reverse, then
   z * y_mask) for seeded flow weights (synth.make_flow_state_dict), B = 2,
   T0 in {1, 5, 24} with lengths (T0, ceil(T0/2)), with and without g; the
@@ -51,6 +55,9 @@ def kats():
     out = {}
     out["lrelu_in"] = np.array([-2.0, 0.0, 3.0, -0.0], np.float32)
     out["lrelu_out"] = np.array([-0.2, 0.0, 3.0, -0.0], np.float32)
+    # linear_interpolate_last_dim([0, 10], 4) (src/models/sovits_encp.rs:928-936)
+    out["interp_in"] = np.array([[[0.0, 10.0]]], np.float32)
+    out["interp_out"] = np.array([[[0.0, 2.5, 7.5, 10.0]]], np.float32)
     x = torch.arange(8, dtype=torch.float64).reshape(1, 2, 4)
     w = (torch.arange(24, dtype=torch.float64) * 0.01 - 0.1).reshape(2, 3, 4)
     out["convt_x"] = x.float().numpy()
@@ -100,8 +107,35 @@ def flows():
     return out
 
 
+ENCP_LAYERS = {"encoder_ssl": 1, "encoder_text": 1, "encoder2": 1}
+
+
+def encps():
+    gsv = load_pkg()
+    import torch_ref
+    sd = gsv.synth.make_encp_state_dict(layers=ENCP_LAYERS)
+    out = {"checksum": np.array(gsv.synth.checksum(sd))}
+    for T in (1, 4, 37):
+        rng = np.random.default_rng(200 + T)
+        x = rng.standard_normal((2, 192, T)).astype(np.float32)
+        y = rng.standard_normal((2, 192, T)).astype(np.float32)
+        noise = rng.standard_normal((2, 192, T)).astype(np.float32)
+        lengths = np.array([T, (T + 1) // 2], np.int32)
+        out[f"T{T}_x"], out[f"T{T}_y"], out[f"T{T}_noise"], out[f"T{T}_len"] = x, y, noise, lengths
+        p = "enc_p.encoder_text.norm_layers_1.0"
+        out[f"T{T}_add_norm"] = torch_ref.layer_norm(x, sd[p + ".gamma"], sd[p + ".beta"], y=y).astype(np.float32)
+        out[f"T{T}_ffn"] = torch_ref.encp_ffn(sd, "encoder_ssl", 0, x, lengths).astype(np.float32)
+        m, logs, zp = torch_ref.encp_project(sd, x, lengths, noise, 0.5)
+        out[f"T{T}_m"], out[f"T{T}_logs"], out[f"T{T}_zp"] = (a.astype(np.float32) for a in (m, logs, zp))
+    x = out["T37_x"]
+    for To in (30, 50):
+        out[f"interp_{To}"] = torch_ref.interpolate(x, To).astype(np.float32)
+    return out
+
+
 if __name__ == "__main__":
     np.savez_compressed(HERE / "kat_ref.npz", **kats())
     np.savez_compressed(HERE / "decoder_tiny.npz", **decoders())
     np.savez_compressed(HERE / "flow_tiny.npz", **flows())
+    np.savez_compressed(HERE / "encp_tiny.npz", **encps())
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))

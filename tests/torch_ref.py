@@ -120,3 +120,56 @@ def flow_inverse(sd, z_p, g=None, lengths=None, prefix="flow.flows"):
             m, logs = stats, torch.zeros_like(stats)
         x = torch.cat([x0, (x1 - m) * torch.exp(-logs)], dim=1)
     return (x * mask).numpy()
+
+
+def _mask(B, T, lengths):
+    ln = torch.full((B,), T) if lengths is None else torch.as_tensor(np.asarray(lengths))
+    return (torch.arange(T)[None, :] < ln[:, None]).to(torch.float64)[:, None, :]
+
+
+def layer_norm(x, gamma, beta, y=None, lengths=None, eps=1e-5):
+    """LayerNorm over channels of x (+ y) [B, C, T] in float64, times x_mask
+    (src/utils/weights.rs:461-502; src/models/sovits_encp.rs:102-109), via
+    F.layer_norm on the channel-last view."""
+    v = torch.as_tensor(np.asarray(x), dtype=torch.float64)
+    if y is not None:
+        v = v + torch.as_tensor(np.asarray(y), dtype=torch.float64)
+    g = torch.as_tensor(np.asarray(gamma), dtype=torch.float64)
+    b = torch.as_tensor(np.asarray(beta), dtype=torch.float64)
+    o = F.layer_norm(v.transpose(1, 2), (v.shape[1],), g, b, eps).transpose(1, 2)
+    if lengths is not None:
+        o = o * _mask(v.shape[0], v.shape[2], lengths)
+    return o.numpy()
+
+
+def encp_ffn(sd, stack, layer, x, lengths=None):
+    """norm2(x + conv_2(relu(conv_1(x)))) * x_mask (src/models/sovits_encp.rs:104-109)."""
+    f = f"enc_p.{stack}.ffn_layers.{layer}"
+    xt = torch.as_tensor(np.asarray(x), dtype=torch.float64)
+    w1, w2 = t64(sd, f + ".conv_1.weight"), t64(sd, f + ".conv_2.weight")
+    h = torch.relu(F.conv1d(xt, w1, t64(sd, f + ".conv_1.bias"), padding=(w1.shape[2] - 1) // 2))
+    y = F.conv1d(h, w2, t64(sd, f + ".conv_2.bias"), padding=(w2.shape[2] - 1) // 2)
+    p = f"enc_p.{stack}.norm_layers_2.{layer}"
+    return layer_norm(xt.numpy(), sd[p + ".gamma"], sd[p + ".beta"], y=y.numpy(), lengths=lengths)
+
+
+def interpolate(x, T_out):
+    """Half-pixel linear interpolation along time (F.interpolate, mode
+    'linear', align_corners False), the PyTorch op linear_interpolate_last_dim
+    restates (src/models/sovits_encp.rs:10-40)."""
+    xt = torch.as_tensor(np.asarray(x), dtype=torch.float64)
+    return F.interpolate(xt, size=T_out, mode="linear", align_corners=False).numpy()
+
+
+def encp_project(sd, y, lengths=None, noise=None, noise_scale=0.5):
+    """(m, logs, z_p) of src/models/sovits_encp.rs:871-879 and
+    src/models/sovits.rs:378-385 in float64."""
+    yt = torch.as_tensor(np.asarray(y), dtype=torch.float64)
+    stats = F.conv1d(yt, t64(sd, "enc_p.proj.weight"), t64(sd, "enc_p.proj.bias"))
+    stats = stats * _mask(yt.shape[0], yt.shape[2], lengths)
+    co = stats.shape[1] // 2
+    m, logs = stats[:, :co], stats[:, co:].clamp(-5.0, 2.0)
+    zp = None
+    if noise is not None:
+        zp = (m + torch.as_tensor(np.asarray(noise), dtype=torch.float64) * torch.exp(logs) * noise_scale).numpy()
+    return m.numpy(), logs.numpy(), zp
