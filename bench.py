@@ -339,6 +339,119 @@ def run_flow(args):
     dec.close()
 
 
+def run_encp(args):
+    """The EncP fused chains around the text encoder's convs at B x T frames on
+    one GPU (T = 50 frames per second of audio): per encoder layer of the
+    v2 stacks (3 + 6 + 3) the attention-side add + LayerNorm (norm1) and the
+    FFN half (conv_1 + ReLU, conv_2 + residual, norm2 + x_mask), then the
+    output projection + prior sample.  The attention itself is outside these
+    chains: a seeded tensor stands in for its output.  Device-resident inputs,
+    CUDA events around K steps, layer-weighted roofline from per-launch events,
+    the CPU oracle on one utterance as the baseline."""
+    import torch
+    gsv = load_pkg()
+    pk, pk_kind = peaks()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    sd.update(gsv.synth.make_encp_state_dict())
+    B, T = args.batch, args.frames
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((B, 192, T)).astype(np.float32)
+    att = rng.standard_normal((B, 192, T)).astype(np.float32)
+    noise = rng.standard_normal((B, 192, T)).astype(np.float32)
+    lengths = np.full(B, T, np.int32)
+    dec = gsv.Decoder.load(sd, device=0, mode=args.mode)
+    secs = B * T / 50.0
+    xd, ad, nd = (torch.from_numpy(a).cuda() for a in (x, att, noise))
+    ld = torch.from_numpy(lengths).cuda()
+    h1, h2 = torch.empty_like(xd), torch.empty_like(xd)
+    m, logs, zp = torch.empty_like(xd), torch.empty_like(xd), torch.empty_like(xd)
+    layers = [(st, i) for st, n in gsv.synth.ENCP_LAYERS.items() for i in range(n)]
+
+    bufs = (h1, h2)
+
+    def step(after=None):
+        cur = xd
+        for k, (st, i) in enumerate(layers):
+            nxt = bufs[k % 2]
+            dec.encp_layer_device(st, i, cur, ad, ld, out=nxt)
+            if after:
+                after()
+            cur = nxt
+        dec.encp_project_device(cur, ld, nd, 0.5, m, logs, zp)
+        if after:
+            after()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    ms_eager = timed(step)  # one API call per layer, launched from Python
+    # The same step captured once in a CUDA graph (every call is stream-async
+    # and allocation-free after warm-up), replayed: device time without the
+    # host's per-call overhead.
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    ms = timed(graph.replay)
+    # per-launch profile of one eager step; each entry point records its own
+    # event list, so the stats are read after every call.
+    dec.set_stage_timing(2)
+    stats = []
+    step(after=lambda: stats.extend(dec.launch_stats()))
+    dec.set_stage_timing(0)
+    roof_s, meas_s, rows = layer_roofline(stats, args.mode, pk)
+    if args.layers:
+        for r in rows:
+            log(f"{r['name']:<34s} {r['ms']:9.4f} ms  roof {r['roof_ms']:9.4f} ms  frac {r['frac']}  {r['bound']}")
+    gemm = [s for s in stats if s["kind"] == 0]
+    gemm_ms = sum(s["ms"] for s in gemm)
+    gemm_flops = sum(s["flops"] for s in gemm)
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        one, a1, n1 = x[:1], att[:1], noise[:1]
+        t0 = time.perf_counter()
+        cur = one
+        for st, i in layers:
+            p = f"enc_p.{st}.norm_layers_1.{i}"
+            cur = oracle.layer_norm(cur, sd[p + ".gamma"], sd[p + ".beta"], y=a1)
+            cur = oracle.encp_ffn(sd, st, i, cur, [T], acc64=False)
+        oracle.encp_project(sd, cur, [T], n1, 0.5, acc64=False)
+        dt = time.perf_counter() - t0
+        cpu = {"value": (T / 50.0) / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+               "sample": f"1 utterance of {T / 50:g} s (x [1,192,{T}]), C restatement of the chains, "
+                         "float accumulation"}
+    print(json.dumps({
+        "metric": f"EncP chains audio-sec/sec at B={B}x{T / 50:g} s {args.mode}",
+        "value": secs / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": args.steps,
+        "warmup": args.warmup, "dtype": args.mode, "timing": "CUDA graph replay of one step",
+        "eager": {"value": secs / (ms_eager / 1e3), "unit": UNIT, "ms_per_step": ms_eager,
+                  "note": "one gsvdec_encp_layer call per layer from Python"},
+        "data": "synthetic: seeded N(0,1) x / attention stand-in / noise, seeded random-init enc_p weights",
+        "config": {"workload": f"12 enc_p layers (norm1(x + attn), FFN 192->768->192 k3, norm2 + mask) + proj "
+                               f"+ prior sample, x [{B},192,{T}]", "batch": B, "frames": T, "mode": args.mode,
+                   "launches_per_step": len(stats)},
+        "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
+                           "sum_meas_ms": 1e3 * meas_s, "peaks": pk_kind},
+        "ffn_gemm": {"ms": gemm_ms, "tflops": gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None,
+                     "launches": len(gemm)},
+        "launches": len(stats), "cpu_baseline": cpu}), flush=True)
+    dec.close()
+
+
 def run_sharded(args, ws, rank, local):
     """Strong-scaling workloads over torch.distributed (NCCL): every rank gets the
     same inputs, decodes its share and the finished waveform pieces are gathered
@@ -463,11 +576,12 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
-    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60", "flow"), default="batch16",
+    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60", "flow", "encp"), default="batch16",
                     help="batch16: 16 x 10 s per GPU (weak scaling, the headline); varlen256: "
                          "256 utterances of 2-20 s sharded by utterance (strong scaling); long60: "
                          "one 60 s utterance split in halo time chunks (strong scaling); flow: the "
-                         "flow inverse before the decoder (and flow + decoder), one GPU")
+                         "flow inverse before the decoder (and flow + decoder), one GPU; encp: the "
+                         "EncP fused chains (12 encoder layers' norms + FFN, projection + prior), one GPU")
     ap.add_argument("--sweep", action="store_true",
                     help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
                          "x --frames, in --mode; prints one JSON line per mode")
@@ -485,6 +599,9 @@ def main():
         return
     if args.workload == "flow":
         run_flow(args)
+        return
+    if args.workload == "encp":
+        run_encp(args)
         return
     if args.workload != "batch16":
         run_sharded(args, ws, rank, local)

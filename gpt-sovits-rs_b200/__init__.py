@@ -39,7 +39,7 @@ EXPORTS = (
     "gsvdec_get_stage_times", "gsvdec_launch_count", "gsvdec_get_launch_stats",
     "gsvdec_forward_noalloc", "gsvdec_noalloc_scratch_bytes", "gsvdec_layer_forward",
     "gsvdec_layer_names", "gsvdec_last_error", "gsvdec_flow_info", "gsvdec_flow_inverse",
-    "gsvdec_flow_decode", "gsvdec_encp_info", "gsvdec_encp_add_norm", "gsvdec_encp_ffn",
+    "gsvdec_flow_decode", "gsvdec_encp_info", "gsvdec_encp_add_norm", "gsvdec_encp_ffn", "gsvdec_encp_layer",
     "gsvdec_encp_speed_len", "gsvdec_encp_interpolate", "gsvdec_encp_project",
 )
 
@@ -113,6 +113,7 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
                                      ctypes.POINTER(i)]
     lib.gsvdec_encp_add_norm.argtypes = [vp, i, i, i, vp, vp, vp, i, i, vp, i, vp]
     lib.gsvdec_encp_ffn.argtypes = [vp, i, i, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_encp_layer.argtypes = [vp, i, i, vp, vp, vp, i, i, vp, i, vp]
     lib.gsvdec_encp_speed_len.argtypes = [i, ctypes.c_float, ctypes.POINTER(i)]
     lib.gsvdec_encp_interpolate.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
     lib.gsvdec_encp_project.argtypes = [vp, vp, vp, i, i, vp, ctypes.c_float, vp, vp, vp, i, vp]
@@ -389,6 +390,32 @@ class Decoder:
                                          _ptr(out), MEM_HOST, None))
         return out
 
+    def encp_layer(self, stack, layer: int, x, attn=None, lengths=None) -> np.ndarray:
+        """EncoderLayer::forward after the attention (src/models/sovits_encp.rs:98-110):
+        norm2(h + FFN(h)) * x_mask, h = norm1(x + attn)."""
+        xa, aa = _host_f32(x), _host_f32(attn)
+        B, C, T = xa.shape
+        if aa is not None and aa.shape != xa.shape:
+            raise ValueError("x and attn must have the same shape")
+        ln = self._lengths(lengths, B)
+        out = np.empty_like(xa)
+        _check(library().gsvdec_encp_layer(self._h, self._stack(stack), layer, _ptr(xa), _ptr(aa), _ptr(ln), B,
+                                           T, _ptr(out), MEM_HOST, None))
+        return out
+
+    def encp_layer_device(self, stack, layer: int, x, attn=None, lengths=None, out=None, stream=None):
+        """Stream-async encp_layer on CUDA tensors (torch)."""
+        import torch
+        B, C, T = x.shape
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _check(library().gsvdec_encp_layer(self._h, self._stack(stack), layer, p(x), p(attn), p(lengths), B, T,
+                                           p(out), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
     def encp_ffn_device(self, stack, layer: int, x, lengths=None, out=None, stream=None):
         """Stream-async FFN half on CUDA tensors (torch): x, out [B, C, T] fp32."""
         import torch
@@ -402,6 +429,35 @@ class Decoder:
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T,
             ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
         return out
+
+    def encp_add_norm_device(self, stack, layer: int, x, y=None, lengths=None, out=None, norm: int = 1,
+                             stream=None):
+        """Stream-async add + LayerNorm on CUDA tensors (torch): x, y, out [B, C, T] fp32."""
+        import torch
+        B, C, T = x.shape
+        assert x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+        _check(library().gsvdec_encp_add_norm(
+            self._h, self._stack(stack), layer, norm, ctypes.c_void_p(x.data_ptr()),
+            None if y is None else ctypes.c_void_p(y.data_ptr()),
+            None if lengths is None else ctypes.c_void_p(lengths.data_ptr()), B, T,
+            ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    def encp_project_device(self, y, lengths=None, noise=None, noise_scale: float = 0.5, m=None, logs=None,
+                            z_p=None, stream=None):
+        """Stream-async projection + prior sample on CUDA tensors (torch); any of
+        m / logs / z_p may be None (not written)."""
+        import torch
+        B, C, T = y.shape
+        assert y.is_cuda and y.dtype == torch.float32 and y.is_contiguous()
+        st = stream if stream is not None else torch.cuda.current_stream(y.device).cuda_stream
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _check(library().gsvdec_encp_project(self._h, p(y), p(lengths), B, T, p(noise), noise_scale, p(m),
+                                             p(logs), p(z_p), MEM_DEVICE, ctypes.c_void_p(st)))
+        return m, logs, z_p
 
     @staticmethod
     def encp_speed_len(T: int, speed: float) -> int:

@@ -62,35 +62,59 @@ __device__ __forceinline__ void ln_column(float* s, int stride, int C, int lane,
   }
 }
 
-// x, y, out: [B][C][T] fp32.  Block = 32 frames of one utterance; the tile
-// s[c][33] holds x + y for all C channels of those frames.
+__device__ __forceinline__ void stv(float* p, float v) { *p = v; }
+__device__ __forceinline__ void stv(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// x, y: [B][C][T] fp32.  Block = 32 frames of one utterance; the tile
+// s[c][33] holds x + y for all C channels of those frames.  The result goes
+// to out as [B][C][T] fp32 (TM = false) or as the time-major [B][T][C] GEMM
+// operand in the mode dtype (TM = true); both stores read the tile
+// conflict-free and write 128-byte (or 64-byte) runs.
+template <typename To, bool TM>
 __global__ void __launch_bounds__(kWarps * 32) add_ln_ncl_kernel(const float* __restrict__ x,
                                                                   const float* __restrict__ y,
                                                                   const float* __restrict__ gamma,
                                                                   const float* __restrict__ beta, int C,
                                                                   int T, float eps, const int* __restrict__ len,
-                                                                  float* __restrict__ out) {
+                                                                  To* __restrict__ out) {
   extern __shared__ float s[];
   const int b = blockIdx.y, t0 = blockIdx.x * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const size_t base = (size_t)b * C * T;
   const int t = t0 + lane;
-  for (int c = w; c < C; c += kWarps) {
-    float v = 0.0f;
-    if (t < T) {
-      v = x[base + (size_t)c * T + t];
-      if (y) v = v + y[base + (size_t)c * T + t];
+  // kIlp independent loads per operand in flight per thread (a latency chain
+  // of C / 8 serial loads otherwise).
+  constexpr int kIlp = 8;
+  for (int c0 = w; c0 < C; c0 += kIlp * kWarps) {
+    float v[kIlp], u[kIlp];
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      const int c = c0 + k * kWarps;
+      const bool in = t < T && c < C;
+      v[k] = in ? x[base + (size_t)c * T + t] : 0.0f;
+      u[k] = (in && y) ? y[base + (size_t)c * T + t] : 0.0f;
     }
-    s[c * (kTile + 1) + lane] = v;
+#pragma unroll
+    for (int k = 0; k < kIlp; ++k) {
+      const int c = c0 + k * kWarps;
+      if (c < C) s[c * (kTile + 1) + lane] = y ? v[k] + u[k] : v[k];
+    }
   }
   __syncthreads();
   for (int j = w; j < kTile; j += kWarps) {
     const float m = (len && t0 + j >= len[b]) ? 0.0f : 1.0f;
     ln_column(s + j, kTile + 1, C, lane, gamma, beta, eps, m);
+    if (TM && t0 + j < T) {
+      __syncwarp();
+      To* row = out + ((size_t)b * T + t0 + j) * C;
+      for (int c = lane; c < C; c += 32) stv(row + c, s[c * (kTile + 1) + j]);
+    }
   }
-  __syncthreads();
-  if (t < T)
-    for (int c = w; c < C; c += kWarps) out[base + (size_t)c * T + t] = s[c * (kTile + 1) + lane];
+  if (!TM) {
+    __syncthreads();
+    if (t < T)
+      for (int c = w; c < C; c += kWarps) stv(out + base + (size_t)c * T + t, s[c * (kTile + 1) + lane]);
+  }
 }
 
 // v: [B][T][C] time-major (mode dtype) -> out [B][C][T] fp32.  The tile
@@ -106,13 +130,23 @@ __global__ void __launch_bounds__(kWarps * 32) ln_tm_ncl_kernel(const Tv* __rest
   const int b = blockIdx.y, t0 = blockIdx.x * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int ld = C + 1;
+  // Rows t0 .. t0 + 31 of one utterance are one contiguous run of
+  // rows * C elements: load it with 16-byte vectors, all in flight at once.
+  constexpr int kVec = 16 / sizeof(Tv);
+  const int rows = min(kTile, T - t0);
+  const Tv* src = v + ((size_t)b * T + t0) * C;
+  const int nvec = rows * C / kVec;  // C % 8 == 0 (host check), so rows * C % kVec == 0
+  for (int i = threadIdx.x; i < nvec; i += kWarps * 32) {
+    const uint4 q = reinterpret_cast<const uint4*>(src)[i];
+    const Tv* e = reinterpret_cast<const Tv*>(&q);
+    const int f = i * kVec, r = f / C, c = f - r * C;  // a vector never crosses a row (C % kVec == 0)
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) s[r * ld + c + k] = ldv(e + k);
+  }
+  __syncthreads();
   for (int r = w; r < kTile; r += kWarps) {
-    const int t = t0 + r;
-    const Tv* row = v + ((size_t)b * T + t) * C;
-    for (int c = lane; c < C; c += 32) s[r * ld + c] = t < T ? ldv(row + c) : 0.0f;
-    __syncwarp();
-    const float m = (len && t >= len[b]) ? 0.0f : 1.0f;
-    ln_column(s + r * ld, 1, C, lane, gamma, beta, eps, m);
+    const float m = (len && t0 + r >= len[b]) ? 0.0f : 1.0f;
+    if (r < rows) ln_column(s + r * ld, 1, C, lane, gamma, beta, eps, m);
   }
   __syncthreads();
   const int t = t0 + lane;
@@ -149,6 +183,7 @@ __global__ void __launch_bounds__(kWarps * 32) prior_kernel(const Tv* __restrict
   __shared__ float sm[kTile][kTile + 1], sl[kTile][kTile + 1];
   const int b = blockIdx.z, t0 = blockIdx.x * kTile, c0 = blockIdx.y * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
   for (int r = w; r < kTile; r += kWarps) {
     const int t = t0 + r, c = c0 + lane;
     float a = 0.0f, l = 0.0f;
@@ -162,6 +197,7 @@ __global__ void __launch_bounds__(kWarps * 32) prior_kernel(const Tv* __restrict
     sl[r][lane] = l;
   }
   __syncthreads();
+#pragma unroll
   for (int r = w; r < kTile; r += kWarps) {
     const int c = c0 + r, t = t0 + lane;
     if (c >= Co || t >= T) continue;
@@ -186,15 +222,38 @@ cudaError_t launch_add_layernorm_ncl(const float* x, const float* y, const float
                                      cudaStream_t st) {
   if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float) * (size_t)C * (kTile + 1);
-  cudaError_t e = set_smem((const void*)add_ln_ncl_kernel, smem);
+  cudaError_t e = set_smem((const void*)add_ln_ncl_kernel<float, false>, smem);
   if (e != cudaSuccess) return e;
-  add_ln_ncl_kernel<<<dim3(cdiv(T, kTile), B), kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T, eps, len, out);
+  add_ln_ncl_kernel<float, false><<<dim3(cdiv(T, kTile), B), kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T,
+                                                                                      eps, len, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add_layernorm_ncl_tm(const float* x, const float* y, const float* gamma, const float* beta,
+                                        int B, int C, int T, float eps, const int* len, void* out, Dt dt,
+                                        cudaStream_t st) {
+  if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (size_t)C * (kTile + 1);
+  const dim3 grid(cdiv(T, kTile), B);
+  cudaError_t e;
+  if (dt == Dt::F32) {
+    e = set_smem((const void*)add_ln_ncl_kernel<float, true>, smem);
+    if (e != cudaSuccess) return e;
+    add_ln_ncl_kernel<float, true><<<grid, kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T, eps, len,
+                                                                    static_cast<float*>(out));
+  } else {
+    e = set_smem((const void*)add_ln_ncl_kernel<__nv_bfloat16, true>, smem);
+    if (e != cudaSuccess) return e;
+    add_ln_ncl_kernel<__nv_bfloat16, true><<<grid, kWarps * 32, smem, st>>>(
+        x, y, gamma, beta, C, T, eps, len, static_cast<__nv_bfloat16*>(out));
+  }
   return cudaGetLastError();
 }
 
 cudaError_t launch_layernorm_tm_ncl(const void* v, Dt dt, int B, int T, int C, const float* gamma,
                                     const float* beta, float eps, const int* len, float* out, cudaStream_t st) {
-  if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC) return cudaErrorInvalidValue;
+  if (B <= 0 || T <= 0 || C <= 0 || C > kLnMaxC || C % 8) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(v) % 16) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float) * (size_t)kTile * (C + 1);
   const dim3 grid(cdiv(T, kTile), B);
   cudaError_t e;

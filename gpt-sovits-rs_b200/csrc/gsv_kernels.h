@@ -81,6 +81,10 @@ cudaError_t launch_gate(const void* xin, const float* cond, int cond_ld, int con
 cudaError_t launch_add_layernorm_ncl(const float* x, const float* y, const float* gamma, const float* beta,
                                      int B, int C, int T, float eps, const int* len, float* out,
                                      cudaStream_t st);
+// The same, written time-major [B][T][C] in the mode dtype (a GEMM operand).
+cudaError_t launch_add_layernorm_ncl_tm(const float* x, const float* y, const float* gamma, const float* beta,
+                                        int B, int C, int T, float eps, const int* len, void* out, Dt dt,
+                                        cudaStream_t st);
 // The same LayerNorm (+ mask) of a time-major [B][T][C] tensor in the mode
 // dtype, written as [B][C][T] fp32.
 cudaError_t launch_layernorm_tm_ncl(const void* v, Dt dt, int B, int T, int C, const float* gamma,

@@ -1785,31 +1785,13 @@ int encp_add_norm_impl(gsvdec* h, int stack, int layer, int norm, const float* x
   return finish_host(h, st, {{out, od}}, n, mem_kind);
 }
 
-int encp_ffn_impl(gsvdec* h, int stack, int layer, const float* x, const int32_t* lengths, int B, int T,
-                  float* out, int mem_kind, cudaStream_t st) {
-  GSV_TRY(encp_common(h, B, T, mem_kind));
-  if (!x || !out) return set_err(GSV_E_INVALID_ARG, "x and out must not be NULL");
-  const gsvdec::EncpLayer* L = nullptr;
-  GSV_TRY(encp_layer(h, stack, layer, &L));
-  const int C = h->encp_C, F = L->ffn1.Cout;
-  if ((int64_t)B * T * F > (int64_t)1 << 34) return set_err(GSV_E_INVALID_ARG, "request too large");
-  const size_t n = (size_t)B * C * T, eb = act_bytes(h);
-  CUDA_TRY(cudaSetDevice(h->device));
-  std::vector<char*> sc;
-  GSV_TRY(encp_scratch(h, {n * 4, n * 4, n * eb, (size_t)B * T * F * eb, n * eb, (size_t)B * 4}, sc));
-  int rc = GSV_OK;
-  const float* xd = stage_in(x, n, sc[0], mem_kind, st, &rc);
-  const int* ld = stage_in(lengths, (size_t)B, sc[5], mem_kind, st, &rc);
-  GSV_TRY(rc);
-  float* od = mem_kind == GSV_MEM_DEVICE ? out : reinterpret_cast<float*>(sc[1]);
-  void* xt = sc[2];
-  void* ht = sc[3];
-  void* vt = sc[4];
-  begin_run(h, st);
-  const double e = (double)eb;
-  CUDA_TRY(launch_transpose_in(xd, B, C, T, 0, T, nullptr, xt, h->dt, st));
-  GSV_TRY(after_launch(h, st, "encp.input_relayout", 1, 0, 0.0, (4.0 + e) * n));
-  const std::string nm = std::string(kEncpStacks[stack]) + ".ffn." + std::to_string(layer);
+// conv_1 + ReLU, conv_2 + residual, norm2 + x_mask + relayout: the FFN half of
+// EncoderLayer::forward on the time-major operand xt ([B][T][C], mode dtype).
+int ffn_tail(gsvdec* h, int stack, int layer, const gsvdec::EncpLayer* L, void* xt, void* ht, void* vt,
+             const int* lens, int B, int T, float* out, cudaStream_t st) {
+  const int C = h->encp_C;
+  const double e = (double)act_bytes(h);
+  const std::string nm = std::string(kEncpStacks[stack]) + "." + std::to_string(layer);
   {
     // conv_1 + bias + ReLU (LeakyReLU slope 0) in the epilogue.
     TapConv op = make_op(h, L->ffn1, B, xt, T);
@@ -1830,8 +1812,44 @@ int encp_ffn_impl(gsvdec* h, int stack, int layer, const float* x, const int32_t
     GSV_TRY(run_one(h, op, st, nm + ".conv_2+res", wk));
   }
   const float* g = h->d_encp_norm + L->norm + 2 * (size_t)C;
-  CUDA_TRY(launch_layernorm_tm_ncl(vt, h->dt, B, T, C, g, g + C, kLayerNormEps, ld, od, st));
-  GSV_TRY(after_launch(h, st, nm + ".norm2+mask", 1, 0, 0.0, (e + 4.0) * n));
+  CUDA_TRY(launch_layernorm_tm_ncl(vt, h->dt, B, T, C, g, g + C, kLayerNormEps, lens, out, st));
+  return after_launch(h, st, nm + ".norm2+mask", 1, 0, 0.0, (e + 4.0) * (double)B * C * T);
+}
+
+// The FFN half alone (x given) or, with `attn`, the whole post-attention
+// EncoderLayer::forward: norm1(x + attn) written straight into the GEMM
+// operand, then the FFN half.
+int encp_ffn_impl(gsvdec* h, int stack, int layer, const float* x, const float* attn, bool with_norm1,
+                  const int32_t* lengths, int B, int T, float* out, int mem_kind, cudaStream_t st) {
+  GSV_TRY(encp_common(h, B, T, mem_kind));
+  if (!x || !out) return set_err(GSV_E_INVALID_ARG, "x and out must not be NULL");
+  const gsvdec::EncpLayer* L = nullptr;
+  GSV_TRY(encp_layer(h, stack, layer, &L));
+  const int C = h->encp_C, F = L->ffn1.Cout;
+  if ((int64_t)B * T * F > (int64_t)1 << 34) return set_err(GSV_E_INVALID_ARG, "request too large");
+  const size_t n = (size_t)B * C * T, eb = act_bytes(h);
+  CUDA_TRY(cudaSetDevice(h->device));
+  std::vector<char*> sc;
+  GSV_TRY(encp_scratch(h, {n * 4, n * 4, n * eb, (size_t)B * T * F * eb, n * eb, (size_t)B * 4,
+                           attn ? n * 4 : 0}, sc));
+  int rc = GSV_OK;
+  const float* xd = stage_in(x, n, sc[0], mem_kind, st, &rc);
+  const float* ad = stage_in(attn, n, sc[6], mem_kind, st, &rc);
+  const int* ld = stage_in(lengths, (size_t)B, sc[5], mem_kind, st, &rc);
+  GSV_TRY(rc);
+  float* od = mem_kind == GSV_MEM_DEVICE ? out : reinterpret_cast<float*>(sc[1]);
+  begin_run(h, st);
+  const double e = (double)eb;
+  if (with_norm1) {
+    const float* g = h->d_encp_norm + L->norm;
+    CUDA_TRY(launch_add_layernorm_ncl_tm(xd, ad, g, g + C, B, C, T, kLayerNormEps, nullptr, sc[2], h->dt, st));
+    GSV_TRY(after_launch(h, st, std::string(kEncpStacks[stack]) + "." + std::to_string(layer) + ".norm1",
+                         1, 0, 0.0, (4.0 * (ad ? 2 : 1) + e) * n));
+  } else {
+    CUDA_TRY(launch_transpose_in(xd, B, C, T, 0, T, nullptr, sc[2], h->dt, st));
+    GSV_TRY(after_launch(h, st, "encp.input_relayout", 1, 0, 0.0, (4.0 + e) * n));
+  }
+  GSV_TRY(ffn_tail(h, stack, layer, L, sc[2], sc[3], sc[4], ld, B, T, od, st));
   return finish_host(h, st, {{out, od}}, n, mem_kind);
 }
 
@@ -1938,10 +1956,17 @@ int gsvdec_create_from_file(const char* path, int mode, int device, gsvdec_t** o
     gsv::StFile f;
     std::string err;
     if (!f.open(path, err)) return gsv::set_err(GSV_E_INVALID_ARG, "%s", err.c_str());
-    // The decoder's tensors and the flow's; float dtypes as in src/utils/weights.rs:140-151.
+    // The decoder's tensors, the flow's and those of the EncP chains (FFN
+    // convs, LayerNorms, proj); float dtypes as in src/utils/weights.rs:140-151.
+    auto wanted = [](const std::string& k) {
+      if (k.compare(0, 4, "dec.") == 0 || k.compare(0, 11, "flow.flows.") == 0) return true;
+      if (k.compare(0, 6, "enc_p.") != 0) return false;
+      return k.find(".ffn_layers.") != std::string::npos || k.find(".norm_layers_") != std::string::npos ||
+             k.compare(0, 11, "enc_p.proj.") == 0;
+    };
     std::vector<gsvdec_tensor> ts;
     for (const gsv::StEntry& e : f.entries()) {
-      if (e.name.compare(0, 4, "dec.") != 0 && e.name.compare(0, 11, "flow.flows.") != 0) continue;
+      if (!wanted(e.name)) continue;
       gsvdec_tensor t{};
       t.name = e.name.c_str();
       if (e.dtype == "F32") t.dtype = GSV_DTYPE_F32;
@@ -2067,7 +2092,14 @@ int gsvdec_encp_add_norm(gsvdec_t* h, int stack, int layer, int norm, const floa
 
 int gsvdec_encp_ffn(gsvdec_t* h, int stack, int layer, const float* x, const int32_t* lengths, int B,
                     int T, float* out, int mem_kind, void* stream) {
-  return gsv::encp_ffn_impl(h, stack, layer, x, lengths, B, T, out, mem_kind, static_cast<cudaStream_t>(stream));
+  return gsv::encp_ffn_impl(h, stack, layer, x, nullptr, false, lengths, B, T, out, mem_kind,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int gsvdec_encp_layer(gsvdec_t* h, int stack, int layer, const float* x, const float* attn,
+                      const int32_t* lengths, int B, int T, float* out, int mem_kind, void* stream) {
+  return gsv::encp_ffn_impl(h, stack, layer, x, attn, true, lengths, B, T, out, mem_kind,
+                            static_cast<cudaStream_t>(stream));
 }
 
 int gsvdec_encp_speed_len(int T, float speed, int* T_out) { return gsv::encp_speed_len(T, speed, T_out); }

@@ -87,7 +87,8 @@ int gsvdec_create(const gsvdec_tensor* tensors, int n_tensors, int mode, int dev
 
 /* Same as gsvdec_create, reading the tensors from a safetensors file
  * (the format written by src/bin/gpt-sovits-convert.rs:282-309 and read by
- * src/utils/weights.rs:116-162).  Non-`dec.` tensors are ignored. */
+ * src/utils/weights.rs:116-162).  Only the tensors the handle uses are read:
+ * dec.*, flow.flows.* and the enc_p.* FFN / LayerNorm / proj tensors. */
 int gsvdec_create_from_file(const char* safetensors_path, int mode, int device, gsvdec_t** out);
 
 int gsvdec_destroy(gsvdec_t* h);
@@ -181,6 +182,15 @@ int gsvdec_encp_add_norm(gsvdec_t* h, int stack, int layer, int norm, const floa
  * + relayout in one pass.  x, out [B, C, T] fp32; lengths [B] or NULL. */
 int gsvdec_encp_ffn(gsvdec_t* h, int stack, int layer, const float* x, const int32_t* lengths, int B,
                     int T, float* out, int mem_kind, void* stream);
+
+/* EncoderLayer::forward after the attention (src/models/sovits_encp.rs:98-110):
+ * out = norm_layers_2(h + FFN(h)) * x_mask with h = norm_layers_1(x + attn),
+ * attn [B, C, T] the self-attention output (NULL: h = norm_layers_1(x)).
+ * norm1 is written straight into the FFN's time-major GEMM operand, so the
+ * layer is four launches: norm1, conv_1 + ReLU, conv_2 + residual, norm2 +
+ * mask + relayout. */
+int gsvdec_encp_layer(gsvdec_t* h, int stack, int layer, const float* x, const float* attn,
+                      const int32_t* lengths, int B, int T, float* out, int mem_kind, void* stream);
 
 /* Output length of the speed change (src/models/sovits_encp.rs:857-867):
  * T when |speed - 1| <= FLT_EPSILON, else max(1, trunc(T / speed) + 1).

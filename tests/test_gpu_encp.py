@@ -184,3 +184,41 @@ def test_handle_without_encp(gsv):
             h.encp_ffn("encoder_ssl", 0, _x(1, 4))
     finally:
         h.close()
+
+
+@pytest.mark.parametrize("mode", ["fp32", "bf16"])
+@pytest.mark.parametrize("with_attn", [True, False])
+@pytest.mark.parametrize("T,lengths", [(3, [3, 2]), (250, [250, 97])])
+def test_layer_matches_oracle(handles, sd_encp, mode, with_attn, T, lengths):
+    x, attn = _x(2, T, 11), (_x(2, T, 12) if with_attn else None)
+    p = "enc_p.encoder2.norm_layers_1.0"
+    h1 = oracle.layer_norm(x, sd_encp[p + ".gamma"], sd_encp[p + ".beta"], y=attn)
+    ref = oracle.encp_ffn(sd_encp, "encoder2", 0, h1, lengths)
+    out = handles[mode].encp_layer("encoder2", 0, x, attn, lengths)
+    _check(mode, out, ref)
+    assert not np.any(out[1, :, lengths[1]:])
+
+
+def test_layer_device_equals_host(handles):
+    import torch
+    x, attn = _x(3, 120, 13), _x(3, 120, 14)
+    ln = [120, 64, 5]
+    h = handles["bf16"]
+    host = h.encp_layer("encoder_text", 1, x, attn, ln)
+    dev = h.encp_layer_device("encoder_text", 1, torch.from_numpy(x).cuda(), torch.from_numpy(attn).cuda(),
+                              torch.tensor(ln, dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert np.array_equal(dev.cpu().numpy(), host)
+
+
+def test_load_file_reads_encp(gsv, sd_encp, handles, tmp_path):
+    from safetensors.numpy import save_file
+    p = tmp_path / "m.safetensors"
+    save_file({k: np.ascontiguousarray(v) for k, v in sd_encp.items()}, str(p))
+    d2 = gsv.Decoder.load_file(p, device=0, mode="fp32")
+    try:
+        assert d2.encp_info == handles["fp32"].encp_info
+        x = _x(1, 16, 15)
+        assert np.array_equal(d2.encp_ffn("encoder_text", 1, x), handles["fp32"].encp_ffn("encoder_text", 1, x))
+    finally:
+        d2.close()
