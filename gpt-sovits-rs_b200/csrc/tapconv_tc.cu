@@ -274,16 +274,20 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t sr
                : "memory");
 }
 
-template <int CK, int NT, int NBUF, int STG>
+template <int CK, int NT, int NBUF, int STG, int MT = 1>
 struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
+  // Taps per streamed weight stage: one barrier wait, fence and commit per
+  // stage, so narrow tiles (whose 4 MMAs per tap are short) load two taps at
+  // a time.
+  static constexpr int kTapsPerB = NT <= 64 ? 2 : 1;
   // TMA-store staging: per epilogue warp, 32 rows x 32 channels bf16 for each
   // of the STG staged outputs (raw and/or act).
   static constexpr uint32_t kStageOut = 32 * 32 * 2;
   static constexpr uint32_t kStageWarp = STG * kStageOut;
   static constexpr uint32_t kStageBytes = 4 * kStageWarp;
-  static constexpr int kCols = NBUF * NT;  // NBUF accumulators of NT fp32 columns
+  static constexpr int kCols = NBUF * MT * NT;  // NBUF accumulators of MT x NT fp32 columns
   static constexpr uint32_t kTmemCols =
       kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
   static_assert(kCols <= 512, "TMEM holds 512 columns");
@@ -332,20 +336,26 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
   return e / o.Cout >= o.len[b];
 }
 
-// SA: activation-window ring depth; SB: streamed weight ring depth (RES = false);
+// MT: 128-row windows per tile (2: every tap issues one MMA per window into
+// adjacent accumulator columns, so the per-tile hand-offs of all three roles
+// are paid once per 256 rows -- the narrow layers' MMAs are too short to hide them);
+// SA: activation-window ring depth (stages of MT windows); SB: streamed weight ring depth (RES = false);
 // NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
 // STG: 1 or 2 outputs leave through shared-memory staging and TMA tensor
 // stores (0: plain stores); GATE: the ops are gated-activation ops (kept out
 // of the other instantiations, whose register budget it would raise).
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE, int MT>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
-  using S = TcShape<CK, NT, NBUF, STG>;
+  using S = TcShape<CK, NT, NBUF, STG, MT>;
+  static_assert(MT == 1 || (MT == 2 && !GATE), "two-window tiles: plain and staged epilogues only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t a_stage = (uint32_t)P.a_stage_bytes;
+  const uint32_t a_win = (uint32_t)P.a_stage_bytes;  // one 128-row window (+ halo), 1024-aligned
+  const uint32_t a_stage = MT * a_win;
   uint8_t* sA = smem;
   uint8_t* sB = smem + SA * a_stage;
-  const int nbt = RES ? P.w_tiles : SB;
+  constexpr int TPB = RES ? 1 : S::kTapsPerB;
+  const int nbt = RES ? P.w_tiles : SB * TPB;
   uint8_t* sStage = sB + (size_t)nbt * S::kBPitch;  // 1024-byte aligned
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + S::kStageBytes);
   const uint32_t a_full = smem_u32(bars);
@@ -435,7 +445,9 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   int* err = P.grp.err;
-  const int row_tiles = P.row_tiles, n_tiles = P.n_tiles, total = P.total_tiles;
+  const int row_tiles = MT == 1 ? P.row_tiles : cdiv(P.row_tiles, MT), n_tiles = P.n_tiles;
+  const int total = P.total_tiles / P.row_tiles * row_tiles;
+  constexpr int kTileRows = kM * MT;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -460,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
         }
       uint32_t ia = 0, ib = 0;
       for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total && ok; w.next()) {
-        const int oi = w.oi, n0 = w.nt * NT, b = w.b, q0 = w.qt * kM;
+        const int oi = w.oi, n0 = w.nt * NT, b = w.b, q0 = w.qt * kTileRows;
         if (tile_masked(ops[oi], b, q0)) continue;
         const int nseg = ops[oi].nseg, N = ops[oi].N;
         for (int s = 0; s < nseg && ok; ++s) {
@@ -473,21 +485,25 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
               ok = false;
               break;
             }
-            mbar_expect_tx(a_full + 8 * st, wbytes);
-            tma_load_3d(smem_u32(sA + st * a_stage), &P.mapA[d.flat], a_full + 8 * st, c0,
-                        q0 + d.minoff, b);
+            mbar_expect_tx(a_full + 8 * st, MT * wbytes);
+#pragma unroll
+            for (int m = 0; m < MT; ++m)
+              tma_load_3d(smem_u32(sA + st * a_stage + m * a_win), &P.mapA[d.flat], a_full + 8 * st, c0,
+                          q0 + m * kM + d.minoff, b);
             ++ia;
             if (!RES) {
-              for (int j = 0; j < d.ntaps; ++j) {
+              for (int j = 0; j < d.ntaps; j += TPB) {
+                const int nt = min(TPB, d.ntaps - j);
                 const uint32_t sb = ib % SB;
                 if (!mbar_wait(b_empty + 8 * sb, ((ib / SB) & 1u) ^ 1u, abort)) {
                   raise_err(err, abort, 2);
                   ok = false;
                   break;
                 }
-                mbar_expect_tx(b_full + 8 * sb, S::kBBytes);
-                tma_load_2d(smem_u32(sB + sb * S::kBPitch), &P.mapB[d.flat], b_full + 8 * sb, c0,
-                            j * N + n0);
+                mbar_expect_tx(b_full + 8 * sb, (uint32_t)nt * S::kBBytes);
+                for (int t = 0; t < nt; ++t)
+                  tma_load_2d(smem_u32(sB + (sb * TPB + t) * S::kBPitch), &P.mapB[d.flat], b_full + 8 * sb,
+                              c0, (j + t) * N + n0);
                 ++ib;
               }
             }
@@ -506,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       }
       uint32_t ia = 0, ib = 0, i = 0;
       for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total && ok; w.next(), ++i) {
-        const int oi = w.oi, b = w.b, q0 = w.qt * kM;
+        const int oi = w.oi, b = w.b, q0 = w.qt * kTileRows;
         const bool masked = tile_masked(ops[oi], b, q0);
         const int nseg = ops[oi].nseg;
         const uint32_t buf = i % NBUF;
@@ -519,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           mbar_arrive(acc_full + 8 * buf);
           continue;
         }
-        const uint32_t d = tmem + buf * NT;
+        const uint32_t d = tmem + buf * (MT * NT);
         uint32_t accumulate = 0;
         for (int s = 0; s < nseg && ok; ++s) {
           const SmSeg sg = ops[oi].seg[s];  // register copy
@@ -534,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
             const uint32_t a_base = smem_u32(sA + st * a_stage) +
                                     (uint32_t)(sg.off0 - sg.minoff) * (CK * 2);
             const int row_step = sg.offstep * (CK * 2);
-            for (int j = 0; j < sg.ntaps; ++j) {
+            for (int j = 0; j < sg.ntaps; j += TPB) {
               uint32_t b_base;
               uint32_t sb = 0;
               if (RES) {
@@ -547,14 +563,20 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
                   break;
                 }
                 tc_fence_after();
-                b_base = smem_u32(sB + sb * S::kBPitch);
+                b_base = smem_u32(sB + sb * TPB * S::kBPitch);
               }
-              const uint32_t a_tap = a_base + (uint32_t)(j * row_step);
+              const int nt = min(TPB, sg.ntaps - j);
+              for (int t = 0; t < nt; ++t) {
+                const uint32_t a_tap = a_base + (uint32_t)((j + t) * row_step);
+                const uint32_t b_tap = b_base + (uint32_t)t * S::kBPitch;
 #pragma unroll
-              for (int kk = 0; kk < CK / 16; ++kk) {
-                mma_bf16(d, sdesc<CK>(a_tap + kk * 32), sdesc<CK>(b_base + kk * 32), idesc,
-                         accumulate);
-                accumulate = 1;
+                for (int kk = 0; kk < CK / 16; ++kk) {
+#pragma unroll
+                  for (int m = 0; m < MT; ++m)
+                    mma_bf16(d + m * NT, sdesc<CK>(a_tap + m * a_win + kk * 32), sdesc<CK>(b_tap + kk * 32),
+                             idesc, accumulate);
+                  accumulate = 1;
+                }
               }
               if (!RES) {
                 mma_commit(b_empty + 8 * sb);
@@ -578,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     bool pending = false;  // a TMA store of this warp may still be reading its staging
     uint32_t i = 0;
     for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total; w.next(), ++i) {
-      const int oi = w.oi, n0 = w.nt * NT, b = w.b, q0 = w.qt * kM;
+      const int oi = w.oi, n0 = w.nt * NT, b = w.b;
       const SmOp& o = ops[oi];
       const uint32_t buf = i % NBUF;
       const bool ok = mbar_wait_fast(acc_full + 8 * buf, (i / NBUF) & 1u, abort);
@@ -587,107 +609,109 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
         break;
       }
       tc_fence_after();
-      const bool masked = tile_masked(o, b, q0);
-      const int q = q0 + row;
-      const bool live = q < o.Q;
       const EpiArgs ea = epi_args(o, sbias, b);
       const int mode = STG > 0 ? o.out_mode : kOutPlain, scw = STG > 0 ? o.scw : 16;
-      if (GATE) {
-        // Gated activation: 32-column runs (a | b) -> 16 outputs of channel
-        // block (n0 + c0) / 2 (WN, src/models/sovits_flow.rs:171-184).
-        const int H = o.Cout / 2;
-        const bool dead = q >= ea.lim || q >= o.Q;
 #pragma unroll 1
-        for (int c0 = 0; c0 < NT; c0 += 32) {
-          float va[16], vb[16];
-          if (!masked) {
-            tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, va);
-            tmem_ld16(lane_addr + buf * NT + (uint32_t)(c0 + 16), vb);
-          }
-          if (!live) continue;
-          const int n = n0 + c0;
-          float y[16];
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            float a = va[k] + ea.bias[n + k], sg = vb[k] + ea.bias[n + 16 + k];
-            if (ea.bias_bc) {
-              a = a + __ldg(ea.bias_bc + n + k);
-              sg = sg + __ldg(ea.bias_bc + n + 16 + k);
+      for (int m = 0; m < MT; ++m) {
+        const int q0 = w.qt * kTileRows + m * kM;
+        const uint32_t acc = lane_addr + buf * (MT * NT) + m * NT;  // this window's accumulator
+        const bool masked = tile_masked(o, b, q0);
+        const int q = q0 + row;
+        const bool live = q < o.Q;
+        if (GATE) {
+          // Gated activation: 32-column runs (a | b) -> 16 outputs of channel
+          // block (n0 + c0) / 2 (WN, src/models/sovits_flow.rs:171-184).
+          const int H = o.Cout / 2;
+          const bool dead = q >= ea.lim || q >= o.Q;
+#pragma unroll 1
+          for (int c0 = 0; c0 < NT; c0 += 32) {
+            float va[16], vb[16];
+            if (!masked) {
+              tmem_ld16(acc + (uint32_t)c0, va);
+              tmem_ld16(acc + (uint32_t)(c0 + 16), vb);
             }
-            y[k] = (masked || dead) ? 0.0f : tanhf(a) * (1.0f / (1.0f + expf(-sg)));
-          }
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(o.out_raw) + ((size_t)b * o.Lout + q) * H + n / 2;
-          store8(dst, y);
-          store8(dst + 8, y + 8);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
-        continue;
-      }
-#pragma unroll 1
-      for (int cc = 0; cc < NT; cc += scw) {
-        // Destination of this warp's chunk: rows q0 + 32 * quarter .. + 31,
-        // GEMM columns n0 + cc .. + scw - 1.
-        bool tma = mode != kOutPlain;
-        int oc = n0 + cc, ov = 0, ou = q0 + quarter * 32;
-        if (mode == kOutConvT) {
-          const int p = oc / o.Cout;  // phase: output row t = s * q - pad + p
-          oc -= p * o.Cout;
-          const int vv = p - o.pad;
-          const int du = vv >= 0 ? vv / o.stride : -((o.stride - 1 - vv) / o.stride);
-          ov = vv - du * o.stride;
-          ou += du;
-          tma = ou >= 0;  // a store never starts at a negative row: plain stores there
-        }
-        if (tma && pending) {
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          __syncwarp();
-          pending = false;
-        }
-#pragma unroll 1
-        for (int c0 = cc; c0 < cc + scw; c0 += 16) {
-          float v[16];
-          if (!masked) {
-            tmem_ld16(lane_addr + buf * NT + (uint32_t)c0, v);
-          } else {
+            if (!live) continue;
+            const int n = n0 + c0;
+            float y[16];
 #pragma unroll
-            for (int k = 0; k < 16; ++k) v[k] = 0.0f;
+            for (int k = 0; k < 16; ++k) {
+              float a = va[k] + ea.bias[n + k], sg = vb[k] + ea.bias[n + 16 + k];
+              if (ea.bias_bc) {
+                a = a + __ldg(ea.bias_bc + n + k);
+                sg = sg + __ldg(ea.bias_bc + n + 16 + k);
+              }
+              y[k] = (masked || dead) ? 0.0f : tanhf(a) * (1.0f / (1.0f + expf(-sg)));
+            }
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(o.out_raw) + ((size_t)b * o.Lout + q) * H + n / 2;
+            store8(dst, y);
+            store8(dst + 8, y + 8);
           }
-          if (!tma) {
-            if (live) epi16(ea, q, n0 + c0, v);
-            continue;
-          }
-          // Rows outside the output are clipped by the tensor map.
-          epi16_values(ea, q, n0 + c0, v);
-          const int h = (c0 - cc) / 8;
-          const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
-          if (ea.raw) {
-            sts128(stage_addr(stg_raw, lane, h, scw), u0);
-            sts128(stage_addr(stg_raw, lane, h + 1, scw), u1);
-          }
-          if (ea.act) {
-            const __nv_bfloat162 s2 = __float2bfloat162_rn(ea.slope);
-            sts128(stage_addr(stg_act, lane, h, scw), lrelu_bf16x8(u0, s2));
-            sts128(stage_addr(stg_act, lane, h + 1, scw), lrelu_bf16x8(u1, s2));
-          }
+          continue;
         }
-        if (tma) {
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (mode == kOutConv) {
-              if (ea.raw) tma_store_3d(&P.mapOut[2 * oi], stg_raw, oc, ou, b);
-              if (ea.act) tma_store_3d(&P.mapOut[2 * oi + 1], stg_act, oc, ou, b);
+#pragma unroll 1
+        for (int cc = 0; cc < NT; cc += scw) {
+          // Destination of this warp's chunk: rows q0 + 32 * quarter .. + 31,
+          // GEMM columns n0 + cc .. + scw - 1.
+          bool tma = mode != kOutPlain;
+          int oc = n0 + cc, ov = 0, ou = q0 + quarter * 32;
+          if (mode == kOutConvT) {
+            const int p = oc / o.Cout;  // phase: output row t = s * q - pad + p
+            oc -= p * o.Cout;
+            const int vv = p - o.pad;
+            const int du = vv >= 0 ? vv / o.stride : -((o.stride - 1 - vv) / o.stride);
+            ov = vv - du * o.stride;
+            ou += du;
+            tma = ou >= 0;  // a store never starts at a negative row: plain stores there
+          }
+          if (tma && pending) {
+            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+            __syncwarp();
+            pending = false;
+          }
+#pragma unroll 1
+          for (int c0 = cc; c0 < cc + scw; c0 += 16) {
+            float v[16];
+            if (!masked) {
+              tmem_ld16(acc + (uint32_t)c0, v);
             } else {
-              if (ea.raw) tma_store_4d(&P.mapOut[2 * oi], stg_raw, oc, ov, ou, b);
-              if (ea.act) tma_store_4d(&P.mapOut[2 * oi + 1], stg_act, oc, ov, ou, b);
+#pragma unroll
+              for (int k = 0; k < 16; ++k) v[k] = 0.0f;
             }
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            if (!tma) {
+              if (live) epi16(ea, q, n0 + c0, v);
+              continue;
+            }
+            // Rows outside the output are clipped by the tensor map.
+            epi16_values(ea, q, n0 + c0, v);
+            const int h = (c0 - cc) / 8;
+            const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
+            if (ea.raw) {
+              sts128(stage_addr(stg_raw, lane, h, scw), u0);
+              sts128(stage_addr(stg_raw, lane, h + 1, scw), u1);
+            }
+            if (ea.act) {
+              const __nv_bfloat162 s2 = __float2bfloat162_rn(ea.slope);
+              sts128(stage_addr(stg_act, lane, h, scw), lrelu_bf16x8(u0, s2));
+              sts128(stage_addr(stg_act, lane, h + 1, scw), lrelu_bf16x8(u1, s2));
+            }
           }
-          pending = true;
+          if (tma) {
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (mode == kOutConv) {
+                if (ea.raw) tma_store_3d(&P.mapOut[2 * oi], stg_raw, oc, ou, b);
+                if (ea.act) tma_store_3d(&P.mapOut[2 * oi + 1], stg_act, oc, ou, b);
+              } else {
+                if (ea.raw) tma_store_4d(&P.mapOut[2 * oi], stg_raw, oc, ov, ou, b);
+                if (ea.act) tma_store_4d(&P.mapOut[2 * oi + 1], stg_act, oc, ov, ou, b);
+              }
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            }
+            pending = true;
+          }
         }
-      }
+      }  // windows of the tile
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
@@ -727,28 +751,28 @@ bool encode_out(CUtensorMap* m, void* y, int mode, int B, int Lout, int Cout, in
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, int MT = 1>
 size_t cfg_smem(const TcParams& P) {
-  using S = TcShape<CK, NT, NBUF, STG>;
-  const int nbt = RES ? P.w_tiles : SB;
-  return 1024 + (size_t)SA * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
+  using S = TcShape<CK, NT, NBUF, STG, MT>;
+  const int nbt = RES ? P.w_tiles : SB * S::kTapsPerB;
+  return 1024 + (size_t)SA * MT * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
          8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
          sizeof(float) * (size_t)P.bias_floats +
          (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
 }
 
 // True when `per_sm` CTAs of this configuration fit one SM's shared memory.
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, int MT = 1>
 bool cfg_fits(const TcParams& P, int per_sm) {
-  return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P) + 1024) <= (size_t)smem_per_sm();
+  return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, STG, MT>(P) + 1024) <= (size_t)smem_per_sm();
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE = false>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE = false, int MT = 1>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
-  using S = TcShape<CK, NT, NBUF, STG>;
-  const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, STG>(P);
+  using S = TcShape<CK, NT, NBUF, STG, MT>;
+  const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, STG, MT>(P);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG, GATE>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG, GATE, MT>;
   // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
   // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
   int nregs = 0;
@@ -759,17 +783,19 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   int per_sm = std::min({smem_sm / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
                          2048 / kThreads, (int)(512 / S::kTmemCols)});
   per_sm = std::max(1, per_sm);
-  const int grid = std::min(P.total_tiles, sm_count() * per_sm);
+  const int tiles = P.total_tiles / P.row_tiles * cdiv(P.row_tiles, MT);
+  const int grid = std::min(tiles, sm_count() * per_sm);
   if (grid <= 0) return cudaSuccess;
   kern<<<grid, kThreads, smem, st>>>(P);
   return cudaGetLastError();
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int SA2, int SB2, int NBUF>
+template <int CK, int NT, bool RES, int SA, int SB, int SA2, int SB2, int NBUF, int MT = 1>
 cudaError_t launch_staged(TcParams& P, int stg, int per_sm, cudaStream_t st) {
-  if (stg == 0) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 0>(P, st);
-  if (cfg_fits<CK, NT, RES, SA, SB, NBUF, 2>(P, per_sm)) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 2>(P, st);
-  return launch_cfg<CK, NT, RES, SA2, SB2, NBUF, 2>(P, st);
+  if (stg == 0) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 0, false, MT>(P, st);
+  if (cfg_fits<CK, NT, RES, SA, SB, NBUF, 2, MT>(P, per_sm))
+    return launch_cfg<CK, NT, RES, SA, SB, NBUF, 2, false, MT>(P, st);
+  return launch_cfg<CK, NT, RES, SA2, SB2, NBUF, 2, false, MT>(P, st);
 }
 
 }  // namespace
@@ -876,11 +902,21 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   }
   // With staging the deeper rings (SA, SB) are kept when `per_sm` CTAs still
   // fit next to the 16 KB of staging, else they shrink to (SA2, SB2).
-  if (ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st);
-  if (ck == 32 && nt == 32 && P.n_tiles == 1) return launch_staged<32, 32, true, 4, 1, 3, 1, 4>(P, stg, 2, st);
+  // Narrow layers: two-window tiles halve the per-tile hand-offs.  At 16
+  // channels a multi-segment op (the branch sum) is bound by its epilogue
+  // instead and keeps one window per tile with more CTAs per SM; at 32
+  // channels both kinds gain (measured per op kind on B200).
+  bool multi_seg = false;
+  for (int i = 0; i < g.n; ++i) multi_seg = multi_seg || g.op[i].nseg > 1;
+  if (ck == 16 && nt == 16 && P.n_tiles == 1)
+    return multi_seg ? launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st)
+                     : launch_cfg<16, 16, true, 6, 1, 4, 0, false, 2>(P, st);
+  if (ck == 32 && nt == 32 && P.n_tiles == 1)
+    return multi_seg ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
+                     : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
   if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 2, 4, 2, 3, 2>(P, stg, 1, st);
   if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
-  if (ck == 64 && nt == 64) return launch_staged<64, 64, false, 3, 4, 2, 4, 4>(P, stg, 2, st);
+  if (ck == 64 && nt == 64) return launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
   return cudaErrorInvalidValue;
 }
 
