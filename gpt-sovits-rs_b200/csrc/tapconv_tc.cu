@@ -894,6 +894,10 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
       stg = std::max(stg, (g.op[i].out_raw != nullptr) + (g.op[i].out_act != nullptr));
     gate = gate || g.op[i].gate;
   }
+  // The three-branch sum (one GEMM over the branches' last convs, plus their
+  // residuals as identity segments at >= 32 channels) has >= 3 segments.
+  bool branch_sum = false;
+  for (int i = 0; i < g.n; ++i) branch_sum = branch_sum || g.op[i].nseg >= 3;
   if (gate) {
     for (int i = 0; i < g.n; ++i)
       if (!g.op[i].gate) return cudaErrorInvalidValue;  // a group is all gated or none
@@ -902,21 +906,22 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   }
   // With staging the deeper rings (SA, SB) are kept when `per_sm` CTAs still
   // fit next to the 16 KB of staging, else they shrink to (SA2, SB2).
-  // Narrow layers: two-window tiles halve the per-tile hand-offs.  At 16
-  // channels a multi-segment op (the branch sum) is bound by its epilogue
-  // instead and keeps one window per tile with more CTAs per SM; at 32
-  // channels both kinds gain (measured per op kind on B200).
-  bool multi_seg = false;
-  for (int i = 0; i < g.n; ++i) multi_seg = multi_seg || g.op[i].nseg > 1;
+  // Two-window tiles (MT = 2) halve the per-tile hand-offs where those bound
+  // the launch (measured per op kind on B200): every narrow op except the
+  // 16-channel branch sum, which is bound by its epilogue and keeps one
+  // window with more CTAs per SM; at 64 channels only the branch sum, whose
+  // long MMA chains outweigh the lost second CTA per SM.
   if (ck == 16 && nt == 16 && P.n_tiles == 1)
-    return multi_seg ? launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st)
-                     : launch_cfg<16, 16, true, 6, 1, 4, 0, false, 2>(P, st);
+    return branch_sum ? launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st)
+                      : launch_cfg<16, 16, true, 6, 1, 4, 0, false, 2>(P, st);
   if (ck == 32 && nt == 32 && P.n_tiles == 1)
-    return multi_seg ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
-                     : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
+    return branch_sum ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
+                      : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
   if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 2, 4, 2, 3, 2>(P, stg, 1, st);
   if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
-  if (ck == 64 && nt == 64) return launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
+  if (ck == 64 && nt == 64)
+    return branch_sum ? launch_staged<64, 64, false, 2, 2, 2, 2, 2, 2>(P, stg, 1, st)
+                      : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
   return cudaErrorInvalidValue;
 }
 
