@@ -1011,6 +1011,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
         }
         const cudaError_t e = launch_rbstep(rg, st);
         if (e != cudaSuccess) return set_err(GSV_E_CUDA, "fused resblock step launch failed: %s", cudaGetErrorString(e));
+        h->launches += rg.n - 1;  // one kernel per branch
         GSV_TRY(after_launch(h, st, "rb" + std::to_string(i) + ".step" + std::to_string(j) + ".fused", 0,
                              wk.nconv, wk.flops, wk.bytes, wk.cf, wk.cb));
       }

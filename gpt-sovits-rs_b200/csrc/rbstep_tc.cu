@@ -29,7 +29,6 @@ namespace gsv {
 namespace {
 
 constexpr int kRbThreads = 192;
-constexpr int kRbWindowStages = 3;  // windows in flight: hides the HBM latency of the next loads
 
 struct RbOpDev {
   const __nv_bfloat16* x;
@@ -91,8 +90,11 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
-template <int C>
+// WS: raw windows in flight (hides the HBM latency of the next loads); 2 where
+// that lets one more CTA share the SM.
+template <int C, int WS>
 __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_constant__ RbParams P) {
+  constexpr int kRbWindowStages = WS;
   using S = RbShape<C>;
   // ---- which branch this CTA serves
   int oi = 0;
@@ -336,16 +338,20 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
 }
 
 template <int C>
-cudaError_t launch_c(RbParams& P, cudaStream_t st) {
+size_t rb_smem(const RbParams& P, int ws) {
   using S = RbShape<C>;
   int kmax = 0;
   for (int i = 0; i < P.nops; ++i) kmax = std::max(kmax, P.op[i].k);
-  const size_t smem = 1024 + (size_t)(2 * kmax + 1) * S::kWPitch +
-                      (size_t)(kRbWindowStages + 1) * P.a_stage + P.t_bytes +
-                      8 * (8 + 2 * kRbWindowStages) + 16 + 2 * C * sizeof(float) +
-                      (P.len_smem ? sizeof(int) * (size_t)P.B : 0);
+  return 1024 + (size_t)(2 * kmax + 1) * S::kWPitch + (size_t)(ws + 1) * P.a_stage + P.t_bytes +
+         8 * (8 + 2 * ws) + 16 + 2 * C * sizeof(float) + (P.len_smem ? sizeof(int) * (size_t)P.B : 0);
+}
+
+template <int C, int WS>
+cudaError_t launch_c(RbParams& P, cudaStream_t st) {
+  using S = RbShape<C>;
+  const size_t smem = rb_smem<C>(P, WS);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = rbstep_kernel<C>;
+  auto kern = rbstep_kernel<C, WS>;
   int nregs = 0;
   cudaError_t e = kernel_setup(kern, smem, &nregs);
   if (e != cudaSuccess) return e;
@@ -410,8 +416,29 @@ cudaError_t launch_rbstep(const RbStepGroup& g, cudaStream_t st) {
   P.a_stage = (max_win * g.C * 2 + 1023) / 1024 * 1024;
   P.t_bytes = ((kM + 16) * g.C * 2 + 1023) / 1024 * 1024;
   if (g.B <= 0 || g.L <= 0) return cudaSuccess;
-  if (g.C == 16) return launch_c<16>(P, st);
-  return launch_c<32>(P, st);
+  // Each branch is its own launch, with shared memory sized for its own kernel
+  // width (the k = 11 branch's weights would otherwise set every CTA's size),
+  // and two window stages where that fits one more CTA per SM.
+  for (int i = 0; i < g.n; ++i) {
+    RbParams Q = P;
+    Q.nops = 1;
+    Q.op[0] = P.op[i];
+    Q.mapX[0] = P.mapX[i];
+    Q.mapW1[0] = P.mapW1[i];
+    Q.mapW2[0] = P.mapW2[i];
+    Q.a_stage = ((kM + Q.op[0].d * (Q.op[0].k - 1)) * g.C * 2 + 1023) / 1024 * 1024;
+    const int sm = smem_per_sm();
+    cudaError_t e;
+    if (g.C == 16) {
+      const bool two = sm / (int)(rb_smem<16>(Q, 2) + 1024) > sm / (int)(rb_smem<16>(Q, 3) + 1024);
+      e = two ? launch_c<16, 2>(Q, st) : launch_c<16, 3>(Q, st);
+    } else {
+      const bool two = sm / (int)(rb_smem<32>(Q, 2) + 1024) > sm / (int)(rb_smem<32>(Q, 3) + 1024);
+      e = two ? launch_c<32, 2>(Q, st) : launch_c<32, 3>(Q, st);
+    }
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace gsv
