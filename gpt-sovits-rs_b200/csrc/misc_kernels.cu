@@ -145,6 +145,14 @@ constexpr int kPostThreads = 256;
 template <typename T>
 constexpr int post_per() { return sizeof(T) == 2 ? 4 : 2; }
 
+// conv_post with the weights as a kernel parameter, in two passes over a block
+// of kPostOut samples: (1) every input row of the block's window is read once
+// (16-byte loads, a warp reads 1 KB contiguous) and turned into its K per-tap
+// partial dots d_j(r) = sum_c w[j][c] x[r][c], stored as sd[j][r]; (2) sample t
+// sums d_j(t + j) over j, reading K consecutive floats per tap across the warp.
+// Each row is fetched from HBM once and read from shared memory as 4 K bytes
+// instead of K times 32; the sums run in the same order as a direct
+// per-sample loop (over c within a tap, then over taps, from the bias).
 template <typename T, int K>
 __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __restrict__ x, int L,
                                                                  const __grid_constant__ PostWeights P,
@@ -156,14 +164,44 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
   constexpr int U = C * (int)sizeof(T) / 16;  // 16-byte units per input row
   constexpr int kPostPer = post_per<T>(), kPostOut = kPostThreads * kPostPer;
   constexpr int kRows = kPostOut + K - 1;
-  __shared__ uint4 srow[kRows * U];
+  __shared__ float sd[K][kRows];
   const int b = blockIdx.y;
   const int t_base = blockIdx.x * kPostOut;
   const int r0 = t_base - pad;
   const uint4* xb = reinterpret_cast<const uint4*>(x + (size_t)b * L * C);
-  for (int i = threadIdx.x; i < kRows * U; i += kPostThreads) {
-    const int row = r0 + i / U;
-    srow[i] = (row >= 0 && row < L) ? __ldg(xb + (size_t)row * U + i % U) : make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < kRows; i += kPostThreads) {
+    const int row = r0 + i;
+    float v[C];
+    if (row >= 0 && row < L) {
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const uint4 u = __ldg(xb + (size_t)row * U + k);
+        if constexpr (sizeof(T) == 2) {
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            v[8 * k + 2 * e] = f.x;
+            v[8 * k + 2 * e + 1] = f.y;
+          }
+        } else {
+          v[4 * k] = __uint_as_float(u.x);
+          v[4 * k + 1] = __uint_as_float(u.y);
+          v[4 * k + 2] = __uint_as_float(u.z);
+          v[4 * k + 3] = __uint_as_float(u.w);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) v[c] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float s = 0.0f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) s = fmaf(v[c], P.w[j * C + c], s);
+      sd[j][i] = s;
+    }
   }
   __syncthreads();
   const int lim = len ? min(len[b], L) : L;
@@ -174,36 +212,7 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
     if (t >= L) break;
     float acc = bias;
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      float v[C];
-      const uint4* rp = srow + (tl + j) * U;
-      if constexpr (sizeof(T) == 2) {
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-          const uint4 u = rp[k];
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __bfloat1622float2(h[e]);
-            v[8 * k + 2 * e] = f.x;
-            v[8 * k + 2 * e + 1] = f.y;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-          const uint4 u = rp[k];
-          v[4 * k] = __uint_as_float(u.x);
-          v[4 * k + 1] = __uint_as_float(u.y);
-          v[4 * k + 2] = __uint_as_float(u.z);
-          v[4 * k + 3] = __uint_as_float(u.w);
-        }
-      }
-      float s = 0.0f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) s = fmaf(v[c], P.w[j * C + c], s);
-      acc += s;
-    }
+    for (int j = 0; j < K; ++j) acc += sd[j][tl + j];
     const bool dead = t >= lim;
     if (pre) pre[(size_t)b * L + t] = dead ? 0.0f : acc;
     wav[(size_t)b * L + t] = dead ? 0.0f : tanhf(acc);
