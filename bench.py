@@ -452,6 +452,59 @@ def run_encp(args):
     dec.close()
 
 
+def run_load(args):
+    """Checkpoint load through gsvdec_create_from_file (the C++ safetensors
+    reader: mmap, dtype conversion, weight-norm fold, packing, upload) on a
+    seeded v2 checkpoint written to a temporary file: the dec.* Generator, the
+    flow and the enc_p tensors the chains use, fp32 as the converter writes
+    them.  The CPU baseline restates the reference's load path for the same
+    file (src/utils/weights.rs:116-162 read + the per-conv weight-norm fold of
+    :589-614) with the oracle's fold."""
+    import tempfile
+    import torch
+    from safetensors.numpy import load_file, save_file
+    gsv = load_pkg()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    sd.update(gsv.synth.make_flow_state_dict(init="n001"))
+    sd.update(gsv.synth.make_encp_state_dict())
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "sovits_v2_seeded.safetensors")
+        save_file({k: np.ascontiguousarray(v, dtype=np.float32) for k, v in sd.items()}, path)
+        size = os.path.getsize(path)
+        for _ in range(args.warmup):
+            gsv.Decoder.load_file(path, device=0, mode=args.mode).close()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            d = gsv.Decoder.load_file(path, device=0, mode=args.mode)
+            torch.cuda.synchronize()
+            times.append(time.perf_counter() - t0)
+            d.close()
+        ms = 1e3 * float(np.median(times))
+        cpu = None
+        if not args.no_cpu_baseline:
+            import oracle
+            t0 = time.perf_counter()
+            tens = load_file(path)
+            n_wn = 0
+            for k in [k for k in tens if k.endswith(".weight_v")]:
+                pfx = k[: -len(".weight_v")]
+                oracle.weight_norm(tens[k], tens[pfx + ".weight_g"])
+                n_wn += 1
+            dt = time.perf_counter() - t0
+            cpu = {"value": size / dt / 1e6, "unit": "MB/s", "cores": oracle.num_threads(), "kind": "port",
+                   "sample": f"the same {size / 1e6:.0f} MB file: safetensors read + {n_wn} weight-norm folds"}
+    print(json.dumps({
+        "metric": f"checkpoint load MB/s ({args.mode})", "value": size / (ms / 1e3) / 1e6, "unit": "MB/s",
+        "ms_per_load": ms, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": args.mode, "data": "synthetic: seeded v2 dec + flow + enc_p tensors, fp32 safetensors",
+        "config": {"workload": f"gsvdec_create_from_file of a {size / 1e6:.0f} MB checkpoint "
+                               "(mmap, fold, pack, upload; host wall clock incl. device sync)",
+                   "file_bytes": size, "tensors": len(sd)},
+        "cpu_baseline": cpu}), flush=True)
+
+
 def run_sharded(args, ws, rank, local):
     """Strong-scaling workloads over torch.distributed (NCCL): every rank gets the
     same inputs, decodes its share and the finished waveform pieces are gathered
@@ -576,12 +629,13 @@ def main():
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", action="store_true", help="print the per-launch table to stderr")
-    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60", "flow", "encp"), default="batch16",
+    ap.add_argument("--workload", choices=("batch16", "varlen256", "long60", "flow", "encp", "load"), default="batch16",
                     help="batch16: 16 x 10 s per GPU (weak scaling, the headline); varlen256: "
                          "256 utterances of 2-20 s sharded by utterance (strong scaling); long60: "
                          "one 60 s utterance split in halo time chunks (strong scaling); flow: the "
                          "flow inverse before the decoder (and flow + decoder), one GPU; encp: the "
-                         "EncP fused chains (12 encoder layers' norms + FFN, projection + prior), one GPU")
+                         "EncP fused chains (12 encoder layers' norms + FFN, projection + prior), one GPU; "
+                         "load: safetensors checkpoint load (gsvdec_create_from_file)")
     ap.add_argument("--sweep", action="store_true",
                     help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
                          "x --frames, in --mode; prints one JSON line per mode")
@@ -602,6 +656,9 @@ def main():
         return
     if args.workload == "encp":
         run_encp(args)
+        return
+    if args.workload == "load":
+        run_load(args)
         return
     if args.workload != "batch16":
         run_sharded(args, ws, rank, local)
