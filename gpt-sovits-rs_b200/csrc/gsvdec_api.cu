@@ -16,6 +16,8 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
+#include <atomic>
 #include <vector>
 
 #include "../../include/gsvdec.h"
@@ -61,6 +63,11 @@ struct HostConv {
   std::vector<float> b;  // bias or empty
   int d0 = 0, d1 = 0, K = 0;
   int pad = 0, dil = 1, stride = 1;
+  // Where w comes from: the plain weight, or (src_g set) the weight-norm pair
+  // v = src_w, g = src_g.  Validated at load; converted and folded by
+  // materialize(), in parallel over all convs.
+  const gsvdec_tensor* src_w = nullptr;
+  const gsvdec_tensor* src_g = nullptr;
 };
 
 struct HostModel {
@@ -95,27 +102,59 @@ int64_t numel(const gsvdec_tensor* t) {
   return n;
 }
 
-int to_f32(const gsvdec_tensor* t, std::vector<float>& out) {
+int check_data(const gsvdec_tensor* t) {
+  if (!t->data && numel(t)) return set_err(GSV_E_INVALID_ARG, "tensor %s has no data", t->name);
+  if (t->dtype != GSV_DTYPE_F32 && t->dtype != GSV_DTYPE_F16 && t->dtype != GSV_DTYPE_BF16)
+    return set_err(GSV_E_DTYPE, "tensor %s: unsupported dtype %d", t->name, t->dtype);
+  return GSV_OK;
+}
+
+// Converts a checked tensor to fp32 (cannot fail: check_data ran first).
+void convert_f32(const gsvdec_tensor* t, float* out) {
   const int64_t n = numel(t);
-  out.resize((size_t)n);
-  if (!t->data && n) return set_err(GSV_E_INVALID_ARG, "tensor %s has no data", t->name);
   switch (t->dtype) {
     case GSV_DTYPE_F32:
-      memcpy(out.data(), t->data, sizeof(float) * (size_t)n);
-      return GSV_OK;
+      memcpy(out, t->data, sizeof(float) * (size_t)n);
+      return;
     case GSV_DTYPE_F16: {
       const uint16_t* p = static_cast<const uint16_t*>(t->data);
       for (int64_t i = 0; i < n; ++i) out[i] = half_to_float(p[i]);
-      return GSV_OK;
+      return;
     }
-    case GSV_DTYPE_BF16: {
+    default: {
       const uint16_t* p = static_cast<const uint16_t*>(t->data);
       for (int64_t i = 0; i < n; ++i) out[i] = bf16_to_float(p[i]);
-      return GSV_OK;
+      return;
     }
-    default:
-      return set_err(GSV_E_DTYPE, "tensor %s: unsupported dtype %d", t->name, t->dtype);
   }
+}
+
+int to_f32(const gsvdec_tensor* t, std::vector<float>& out) {
+  GSV_TRY(check_data(t));
+  out.resize((size_t)numel(t));
+  convert_f32(t, out.data());
+  return GSV_OK;
+}
+
+// Runs f(0) .. f(n - 1) on up to hardware_concurrency host threads (the
+// calling thread included).  f must not fail or touch the thread-local error.
+template <typename F>
+void parallel_for(size_t n, F&& f) {
+  const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  const size_t nt = std::min<size_t>(std::min<size_t>(hw, 32), n);
+  if (nt <= 1) {
+    for (size_t i = 0; i < n; ++i) f(i);
+    return;
+  }
+  std::atomic<size_t> next{0};
+  auto work = [&] {
+    for (size_t i; (i = next.fetch_add(1, std::memory_order_relaxed)) < n;) f(i);
+  };
+  std::vector<std::thread> pool;
+  pool.reserve(nt - 1);
+  for (size_t t = 1; t < nt; ++t) pool.emplace_back(work);
+  work();
+  for (auto& th : pool) th.join();
 }
 
 // Plain conv: "<pfx>.weight" [O, I, K], optional "<pfx>.bias"; pad (K-1)/2
@@ -125,7 +164,9 @@ int load_plain(const TensorMap& tm, const std::string& pfx, HostConv& c) {
   const gsvdec_tensor* w = tm.get(pfx + ".weight");
   if (!w) return set_err(GSV_E_MISSING_KEY, "Key '%s.weight' not found in state dict", pfx.c_str());
   if (w->ndim != 3) return set_err(GSV_E_SHAPE, "%s.weight must be 3-d", pfx.c_str());
-  GSV_TRY(to_f32(w, c.w));
+  GSV_TRY(check_data(w));
+  c.src_w = w;
+  c.src_g = nullptr;
   c.d0 = (int)w->shape[0];
   c.d1 = (int)w->shape[1];
   c.K = (int)w->shape[2];
@@ -151,20 +192,39 @@ int load_wn(const TensorMap& tm, const std::string& pfx, HostConv& c) {
   c.K = (int)v->shape[2];
   if (numel(g) != c.d0)
     return set_err(GSV_E_SHAPE, "%s.weight_g must hold %d values (one per dim-0 slice)", pfx.c_str(), c.d0);
-  std::vector<float> vv, gg;
-  GSV_TRY(to_f32(v, vv));
-  GSV_TRY(to_f32(g, gg));
-  const size_t per = (size_t)c.d1 * c.K;
-  c.w.resize(vv.size());
-  for (int o = 0; o < c.d0; ++o) {
-    double ss = 0.0;
-    for (size_t j = 0; j < per; ++j) ss += (double)vv[o * per + j] * vv[o * per + j];
-    const float norm = (float)std::sqrt(ss);
-    for (size_t j = 0; j < per; ++j) c.w[o * per + j] = (vv[o * per + j] / norm) * gg[o];
-  }
+  GSV_TRY(check_data(v));
+  GSV_TRY(check_data(g));
+  c.src_w = v;
+  c.src_g = g;
   if (const gsvdec_tensor* b = tm.get(pfx + ".bias")) GSV_TRY(to_f32(b, c.b));
   c.pad = (c.K - 1) / 2;
   return GSV_OK;
+}
+
+// The fp32 weight of a loaded conv: the plain weight converted, or the
+// weight-norm fold w = g * v / ||v||, the norm over dims (1, 2) of each dim-0
+// slice accumulated in double (src/utils/weights.rs:589-614).
+void materialize(HostConv& c) {
+  if (!c.src_w) return;
+  c.w.resize((size_t)numel(c.src_w));
+  convert_f32(c.src_w, c.w.data());
+  if (c.src_g) {
+    std::vector<float> gg((size_t)numel(c.src_g));
+    convert_f32(c.src_g, gg.data());
+    const size_t per = (size_t)c.d1 * c.K;
+    for (int o = 0; o < c.d0; ++o) {
+      float* row = c.w.data() + (size_t)o * per;
+      double ss = 0.0;
+      for (size_t j = 0; j < per; ++j) ss += (double)row[j] * row[j];
+      const float norm = (float)std::sqrt(ss);
+      for (size_t j = 0; j < per; ++j) row[j] = (row[j] / norm) * gg[o];
+    }
+  }
+  c.src_w = c.src_g = nullptr;
+}
+
+void materialize_all(const std::vector<HostConv*>& cs) {
+  parallel_for(cs.size(), [&](size_t i) { materialize(*cs[i]); });
 }
 
 int load_model(const gsvdec_tensor* ts, int n, HostModel& m) {
@@ -368,53 +428,85 @@ struct GemmConv {
   int Q(int Lin) const { return transposed ? (Lout(Lin) + pad - 1) / stride + 1 : Lout(Lin); }
 };
 
+// Builds the weight arena.  conv()/convT()/identity() only reserve the bytes
+// and record fill jobs; finish() allocates the arena once and runs the jobs in
+// parallel.  The HostConv weights a job reads must stay alive (and unmoved)
+// until finish(): the loaded model's convs live for the whole create call, and
+// temporaries are handed over with conv(HostConv&&).
 struct Packer {
   Dt dt;
-  std::vector<uint8_t> wbytes;
+  size_t size = 0;                      // bytes reserved so far
+  std::unique_ptr<uint8_t[]> arena;     // size bytes after finish()
   std::vector<float> biases;
 
-  size_t align(size_t a) {
-    size_t r = (wbytes.size() + a - 1) / a * a;
-    wbytes.resize(r);
+  enum Kind { kConv, kConvT, kIdentity };
+  struct Job {
+    Kind kind;
+    const float* w;  // HostConv layout: conv [N][Cin][K], convT [Cin][Cout][K]
+    const int* rows; // conv: packed column n reads weight row rows[n] (NULL: n)
+    int Cin, Cout, N, K, stride;
+    size_t base;
+    int j, n0, n1;   // tap j, packed columns [n0, n1)
+  };
+  std::vector<Job> jobs;
+  std::vector<std::pair<size_t, size_t>> gaps;  // alignment padding to zero
+  std::vector<std::unique_ptr<std::vector<float>>> owned;
+  std::vector<std::unique_ptr<std::vector<int>>> owned_rows;
+
+  size_t esize() const { return dt == Dt::F32 ? 4 : 2; }
+  size_t reserve(size_t bytes) {
+    const size_t r = (size + 1023) / 1024 * 1024;
+    if (r > size) gaps.emplace_back(size, r - size);
+    size = r + bytes;
     return r;
   }
-  // Element (tap j, column n, channel c) of the packed weight.
-  void put(size_t base, int ntaps, int N, int Cin, int j, int n, int c, float v) {
-    size_t idx = dt == Dt::F32 ? ((size_t)j * Cin + c) * N + n   // [tap][Cin][N]
-                               : ((size_t)j * N + n) * Cin + c;  // [tap][N][Cin] (K-major)
-    (void)ntaps;
-    if (dt == Dt::F32) {
-      memcpy(&wbytes[base + idx * 4], &v, 4);
-    } else {
-      __nv_bfloat16 h = __float2bfloat16_rn(v);
-      memcpy(&wbytes[base + idx * 2], &h, 2);
-    }
+  // One job per tap and block of about 64k packed elements.
+  void add_jobs(Kind kind, const float* w, const GemmConv& g, int Cin, int K, int stride,
+                const int* rows = nullptr) {
+    const int cols = std::max(1, 65536 / std::max(Cin, 1));
+    for (int j = 0; j < g.ntaps; ++j)
+      for (int n0 = 0; n0 < g.N; n0 += cols)
+        jobs.push_back(Job{kind, w, rows, Cin, g.Cout, g.N, K, stride, g.w_off, j, n0, std::min(g.N, n0 + cols)});
   }
-  size_t esize() const { return dt == Dt::F32 ? 4 : 2; }
 
-  GemmConv conv(const HostConv& c) {
+  GemmConv conv(const HostConv& c) { return conv_from(c, c.w.data()); }
+  GemmConv conv(HostConv&& c) {
+    owned.push_back(std::make_unique<std::vector<float>>(std::move(c.w)));
+    return conv_from(c, owned.back()->data());
+  }
+  // The conv c with its output rows reordered (packed column n = row rows[n])
+  // or truncated to the first d0 rows (d0 below c.d0), reading c's weights in
+  // place.
+  GemmConv conv_rows(const HostConv& c, std::vector<int> rows, int d0) {
+    HostConv view;
+    view.d0 = d0; view.d1 = c.d1; view.K = c.K; view.pad = c.pad; view.dil = c.dil;
+    if (!c.b.empty())
+      for (int n = 0; n < d0; ++n) view.b.push_back(c.b[rows.empty() ? n : rows[n]]);
+    const int* map = nullptr;
+    if (!rows.empty()) {
+      owned_rows.push_back(std::make_unique<std::vector<int>>(std::move(rows)));
+      map = owned_rows.back()->data();
+    }
+    return conv_from(view, c.w.data(), map);
+  }
+  GemmConv conv_from(const HostConv& c, const float* w, const int* rows = nullptr) {
     GemmConv g;
     g.Cin = c.d1; g.Cout = c.d0; g.N = c.d0; g.ntaps = c.K;
     g.off0 = -c.pad; g.offstep = c.dil; g.pad = c.pad; g.K = c.K;
-    g.w_off = align(1024);
-    wbytes.resize(g.w_off + (size_t)g.ntaps * g.N * g.Cin * esize());
-    for (int n = 0; n < g.N; ++n)
-      for (int ci = 0; ci < g.Cin; ++ci)
-        for (int j = 0; j < c.K; ++j)
-          put(g.w_off, g.ntaps, g.N, g.Cin, j, n, ci, c.w[((size_t)n * g.Cin + ci) * c.K + j]);
+    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * esize());
+    add_jobs(kConv, w, g, g.Cin, c.K, 1, rows);
     g.b_off = biases.size();
     for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
     return g;
   }
   // Identity [1][C][C]: a ResBlock residual fed through the MMA (bf16 mode).
   size_t identity(int C) {
-    const size_t off = align(1024);
-    wbytes.resize(off + (size_t)C * C * esize());
-    for (int n = 0; n < C; ++n)
-      for (int c = 0; c < C; ++c) put(off, 1, C, C, 0, n, c, n == c ? 1.0f : 0.0f);
-    return off;
+    GemmConv g;
+    g.Cin = C; g.Cout = C; g.N = C; g.ntaps = 1;
+    g.w_off = reserve((size_t)C * C * esize());
+    add_jobs(kIdentity, nullptr, g, C, 1, 1);
+    return g.w_off;
   }
-
   // Polyphase ConvTranspose1d: tap m, column n = phi*Cout + o, channel c holds
   // w[c][o][phi + m*s] (zero past the kernel).
   GemmConv convT(const HostConv& c) {
@@ -423,19 +515,66 @@ struct Packer {
     g.Cin = c.d0; g.Cout = c.d1; g.stride = c.stride; g.pad = c.pad; g.K = c.K;
     g.ntaps = (c.K + c.stride - 1) / c.stride;
     g.N = c.stride * g.Cout; g.off0 = 0; g.offstep = -1;
-    g.w_off = align(1024);
-    wbytes.resize(g.w_off + (size_t)g.ntaps * g.N * g.Cin * esize());
-    for (int m = 0; m < g.ntaps; ++m)
-      for (int phi = 0; phi < c.stride; ++phi)
-        for (int o = 0; o < g.Cout; ++o)
-          for (int ci = 0; ci < g.Cin; ++ci) {
-            const int kk = phi + m * c.stride;
-            const float v = kk < c.K ? c.w[((size_t)ci * g.Cout + o) * c.K + kk] : 0.0f;
-            put(g.w_off, g.ntaps, g.N, g.Cin, m, phi * g.Cout + o, ci, v);
-          }
+    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * esize());
+    add_jobs(kConvT, c.w.data(), g, g.Cin, c.K, c.stride);
     g.b_off = biases.size();
     for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
     return g;
+  }
+
+  // BF16 arena: [tap][N][Cin] (K-major B operand); FP32: [tap][Cin][N].
+  // src(n, ci) is the value of packed element (tap b.j, column n, channel ci).
+  // Geometry is read into locals first: the stores could otherwise alias it.
+  template <typename F>
+  void fill(const Job& b, F src) {
+    const int Cin = b.Cin, N = b.N, j = b.j, n0 = b.n0, n1 = b.n1;
+    uint8_t* base = arena.get() + b.base;
+    if (dt == Dt::BF16) {
+      uint16_t* out = reinterpret_cast<uint16_t*>(base);
+      for (int n = n0; n < n1; ++n) {
+        uint16_t* row = out + ((size_t)j * N + n) * Cin;
+        for (int ci = 0; ci < Cin; ++ci) row[ci] = __bfloat16_as_ushort(__float2bfloat16_rn(src(n, ci)));
+      }
+    } else {
+      // A transpose: 32-channel blocks keep both the reads (along ci) and the
+      // writes (along n) in a few cache lines each.
+      float* out = reinterpret_cast<float*>(base) + (size_t)j * Cin * N;
+      for (int c0 = 0; c0 < Cin; c0 += 32) {
+        const int c1 = std::min(Cin, c0 + 32);
+        for (int n = n0; n < n1; ++n)
+          for (int ci = c0; ci < c1; ++ci) out[(size_t)ci * N + n] = src(n, ci);
+      }
+    }
+  }
+  void run(const Job& b) {
+    const int Cin = b.Cin, Cout = b.Cout, K = b.K, stride = b.stride, j = b.j;
+    const float* w = b.w;
+    switch (b.kind) {
+      case kConv:
+        if (b.rows) {
+          const int* rows = b.rows;
+          fill(b, [=](int n, int ci) { return w[((size_t)rows[n] * Cin + ci) * K + j]; });
+        } else {
+          fill(b, [=](int n, int ci) { return w[((size_t)n * Cin + ci) * K + j]; });
+        }
+        break;
+      case kConvT:
+        fill(b, [=](int n, int ci) {
+          const int phi = n / Cout, o = n - phi * Cout, kk = phi + j * stride;
+          return kk < K ? w[((size_t)ci * Cout + o) * K + kk] : 0.0f;
+        });
+        break;
+      default:
+        fill(b, [](int n, int ci) { return n == ci ? 1.0f : 0.0f; });
+    }
+  }
+  void finish() {
+    arena.reset(new uint8_t[std::max<size_t>(size, 1)]);
+    for (const auto& gp : gaps) memset(arena.get() + gp.first, 0, gp.second);
+    parallel_for(jobs.size(), [&](size_t i) { run(jobs[i]); });
+    jobs.clear();
+    owned.clear();
+    owned_rows.clear();
   }
 };
 
@@ -596,7 +735,7 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
     for (int o = 0; o < hid; ++o)
       for (int j = 0; j < half; ++j) pre.w[(size_t)o * C + pi[j]] = c.pre.w[(size_t)o * half + j];
     pre.b = c.pre.b;
-    F.pre = pk.conv(pre);
+    F.pre = pk.conv(std::move(pre));
     for (int j = 0; j < nl; ++j) {
       if (!h->flow_gate_fused) {
         F.in.push_back(pk.conv(c.in[j]));
@@ -604,40 +743,33 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
       }
       // Columns interleaved in 16-channel (tanh half, sigmoid half) pairs, so
       // one 32-column epilogue run holds both halves of 16 outputs.
-      HostConv a = c.in[j];
-      const size_t per = (size_t)a.d1 * a.K;
-      for (int col = 0; col < 2 * hid; ++col) {
-        const int src = gate_src(col, hid);
-        std::copy(c.in[j].w.begin() + (size_t)src * per, c.in[j].w.begin() + (size_t)(src + 1) * per,
-                  a.w.begin() + (size_t)col * per);
-        if (!a.b.empty()) a.b[col] = c.in[j].b[src];
-      }
-      F.in.push_back(pk.conv(a));
+      std::vector<int> rows(2 * hid);
+      for (int col = 0; col < 2 * hid; ++col) rows[col] = gate_src(col, hid);
+      F.in.push_back(pk.conv_rows(c.in[j], std::move(rows), 2 * hid));
     }
     for (int j = 0; j + 1 < nl; ++j) {
-      HostConv r;
-      r.name = c.rs[j].name; r.d0 = hid; r.d1 = hid; r.K = 1; r.pad = 0;
-      r.w.assign(c.rs[j].w.begin(), c.rs[j].w.begin() + (size_t)hid * hid);
-      if (!c.rs[j].b.empty()) r.b.assign(c.rs[j].b.begin(), c.rs[j].b.begin() + hid);
-      F.res.push_back(pk.conv(r));
+      // The residual half: the first hid rows of res_skip j (1x1, pad 0).
+      F.res.push_back(pk.conv_rows(c.rs[j], {}, hid));
     }
     // Coupling update weights and bias (double precision fold).
     std::vector<double> cb(half, 0.0);
     for (int i = 0; i < half; ++i) cb[i] = c.post.b.empty() ? 0.0 : c.post.b[i];
     std::vector<std::vector<double>> wp(nl, std::vector<double>((size_t)half * hid, 0.0));
-    for (int j = 0; j < nl; ++j) {
-      const HostConv& rs = c.rs[j];
-      const int r0 = j < nl - 1 ? hid : 0;  // skip rows of res_skip j
-      for (int i = 0; i < half; ++i) {
+    // Rows i are independent (each sums over j, then k, in that order).
+    parallel_for((size_t)half, [&](size_t ii) {
+      const int i = (int)ii;
+      for (int j = 0; j < nl; ++j) {
+        const HostConv& rs = c.rs[j];
+        const int r0 = j < nl - 1 ? hid : 0;  // skip rows of res_skip j
+        double* dst = &wp[j][(size_t)i * hid];
         for (int k = 0; k < hid; ++k) {
           const double wpk = c.post.w[(size_t)i * hid + k];
           if (!rs.b.empty()) cb[i] += wpk * rs.b[r0 + k];
           const float* srow = &rs.w[(size_t)(r0 + k) * hid];
-          double* dst = &wp[j][(size_t)i * hid];
           for (int m = 0; m < hid; ++m) dst[m] += wpk * srow[m];
         }
       }
-    }
+    });
     for (int j = 0; j < nl; ++j) {
       HostConv u;
       u.name = c.post.name; u.d0 = C; u.d1 = hid; u.K = 1; u.pad = 0;
@@ -648,7 +780,7 @@ int pack_flow(gsvdec* h, Packer& pk, const HostFlow& hf, std::vector<std::vector
         for (int m = 0; m < hid; ++m) u.w[(size_t)row * hid + m] = (float)-wp[j][(size_t)i * hid + m];
         if (j == 0) u.b[row] = (float)-cb[i];
       }
-      F.post.push_back(pk.conv(u));
+      F.post.push_back(pk.conv(std::move(u)));
     }
     if (c.has_cond) {
       F.has_cond = true;
@@ -955,11 +1087,21 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
     L = sg.up.Lout(Lin);
     const int C = sg.up.Cout;
     const int* len = stage_len(i + 1);
+    // Narrow stages in BF16 mode: ResBlock steps 0 and 1 run as fused
+    // conv1 -> conv2 kernels (rbstep_tc.cu); the intermediate stays on chip.
+    bool fuse = h->dt == Dt::BF16 && nb == 3 && rbstep_supported(C, 1, 1) && h->ident_off.count(C);
+    for (int r = 0; r < nb && fuse; ++r) {
+      fuse = sg.c1[r].size() == 3;
+      for (int j = 0; j < 2 && fuse; ++j)
+        fuse = rbstep_supported(C, sg.c1[r][j].ntaps, sg.c1[r][j].offstep) && sg.c1[r][j].off0 == -sg.c1[r][j].pad;
+    }
     {
       TapConv op = make_op(h, sg.up, B, OUT, Lin);
       op.len = len;
       op.out_raw = X;
-      op.out_act = nb > 0 ? AX : nullptr;
+      // The fused step applies the LeakyReLU to its own input window, so the
+      // upsample's activated copy is only needed by the unfused step 0.
+      op.out_act = nb > 0 && !fuse ? AX : nullptr;
       if (nb == 0) { op.out_act = AX; op.slope = next_slope; }
       Work wk;
       wk.add(sg.up, B, Lin, 0, eb);
@@ -971,14 +1113,6 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
       std::swap(OUT, AX);
       mark(h, st);
       continue;
-    }
-    // Narrow stages in BF16 mode: ResBlock steps 0 and 1 run as fused
-    // conv1 -> conv2 kernels (rbstep_tc.cu); the intermediate stays on chip.
-    bool fuse = h->dt == Dt::BF16 && nb == 3 && rbstep_supported(C, 1, 1) && h->ident_off.count(C);
-    for (int r = 0; r < nb && fuse; ++r) {
-      fuse = sg.c1[r].size() == 3;
-      for (int j = 0; j < 2 && fuse; ++j)
-        fuse = rbstep_supported(C, sg.c1[r][j].ntaps, sg.c1[r][j].offstep) && sg.c1[r][j].off0 == -sg.c1[r][j].pad;
     }
     int first_step = 0;
     if (fuse) {
@@ -1302,8 +1436,35 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   *out = nullptr;
   if (!ts || n <= 0) return set_err(GSV_E_INVALID_ARG, "no tensors given");
   if (mode != GSV_MODE_FP32 && mode != GSV_MODE_BF16) return set_err(GSV_E_INVALID_ARG, "bad mode %d", mode);
+  // Validate every tensor first (cheap), then convert and fold all weights in
+  // parallel, then pack (the packing jobs also run in parallel, in finish()).
   HostModel m;
   GSV_TRY(load_model(ts, n, m));
+  HostFlow hf;
+  GSV_TRY(load_flow(ts, n, "flow.flows", hf));
+  HostEncp he;
+  GSV_TRY(load_encp(ts, n, he));
+  {
+    std::vector<HostConv*> all{&m.pre, &m.post};
+    if (m.has_cond) all.push_back(&m.cond);
+    for (auto& u : m.ups) all.push_back(&u);
+    for (auto& rb : m.rbs) {
+      for (auto& c : rb.c1) all.push_back(&c);
+      for (auto& c : rb.c2) all.push_back(&c);
+    }
+    for (auto& c : hf.layers) {
+      for (HostConv* x : {&c.pre, &c.post, &c.cond}) all.push_back(x);
+      for (auto& x : c.in) all.push_back(&x);
+      for (auto& x : c.rs) all.push_back(&x);
+    }
+    for (auto& st : he.stacks)
+      for (auto& L : st) {
+        all.push_back(&L.c1);
+        all.push_back(&L.c2);
+      }
+    if (he.has_proj) all.push_back(&he.proj);
+    materialize_all(all);
+  }
   GSV_TRY(check_device(device));
   CUDA_TRY(cudaSetDevice(device));
   std::unique_ptr<gsvdec> h(new gsvdec());
@@ -1372,8 +1533,6 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the bf16 tcgen05 kernel");
   }
   // The flow (optional), packed into the same weight arena.
-  HostFlow hf;
-  GSV_TRY(load_flow(ts, n, "flow.flows", hf));
   std::vector<std::vector<float>> flow_cond_w, flow_cond_b;
   if (!hf.layers.empty()) {
     GSV_TRY(pack_flow(h.get(), pk, hf, flow_cond_w, flow_cond_b));
@@ -1395,8 +1554,6 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
     }
   }
   // The EncP chains (optional), packed into the same weight arena.
-  HostEncp he;
-  GSV_TRY(load_encp(ts, n, he));
   std::vector<float> encp_norm;
   for (int s = 0; s < 3; ++s)
     for (const HostEncpLayer& L : he.stacks[s]) {
@@ -1437,10 +1594,11 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   std::vector<float> post_w((size_t)h->post_K * h->post_C);  // [K][C]
   for (int c = 0; c < h->post_C; ++c)
     for (int j = 0; j < h->post_K; ++j) post_w[(size_t)j * h->post_C + c] = m.post.w[(size_t)c * h->post_K + j];
-  // Upload.
-  h->w_bytes = pk.wbytes.size();
+  // Fill the arena, then upload.
+  pk.finish();
+  h->w_bytes = pk.size;
   CUDA_TRY(cudaMalloc(&h->d_w, std::max<size_t>(h->w_bytes, 256)));
-  CUDA_TRY(cudaMemcpy(h->d_w, pk.wbytes.data(), h->w_bytes, cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(h->d_w, pk.arena.get(), h->w_bytes, cudaMemcpyHostToDevice));
   CUDA_TRY(cudaMalloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
   CUDA_TRY(cudaMemcpy(h->d_bias, pk.biases.data(), sizeof(float) * pk.biases.size(), cudaMemcpyHostToDevice));
   if (post_w.size() <= sizeof(h->post_wh.w) / sizeof(float)) {
