@@ -704,7 +704,6 @@ def main():
         dec.forward_device(zt, gt, out=out)
     torch.cuda.synchronize()
     launches_per_step = dec.launch_count()
-    dec.set_stage_timing(2)
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
@@ -719,10 +718,18 @@ def main():
     barrier()
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
-    stats = dec.launch_stats()
-    dec.set_stage_timing(0)
     value = ws * secs_per_step * args.steps / (ms / 1e3)
     assert torch.isfinite(out).all().item()
+    # Per-launch profile (roofline) from the same K steps run again with an
+    # event pair around every launch; kept out of the timed loop above, which
+    # runs the launches exactly as a caller does (no event records between
+    # them, so each kernel may start during the tail of the one before).
+    dec.set_stage_timing(2)
+    for _ in range(args.steps):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    stats = dec.launch_stats()
+    dec.set_stage_timing(0)
 
     # ---- end to end through the public call with host buffers (e2e) --------
     zh = torch.from_numpy(z).pin_memory()

@@ -25,6 +25,7 @@
 #include <algorithm>
 
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 
 namespace gsv {
 namespace {
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(kWarps * 32) add_ln_ncl_kernel(const float* __
                                                                   const float* __restrict__ beta, int C,
                                                                   int T, float eps, const int* __restrict__ len,
                                                                   To* __restrict__ out) {
+  pdl_wait();
   extern __shared__ float s[];
   const int b = blockIdx.y, t0 = blockIdx.x * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(kWarps * 32) ln_tm_ncl_kernel(const Tv* __rest
                                                                  const float* __restrict__ beta, float eps,
                                                                  const int* __restrict__ len,
                                                                  float* __restrict__ out) {
+  pdl_wait();
   extern __shared__ float s[];
   const int b = blockIdx.y, t0 = blockIdx.x * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -158,6 +161,7 @@ __global__ void __launch_bounds__(kWarps * 32) ln_tm_ncl_kernel(const Tv* __rest
 // blend, each step rounded in f32 as written there (no contraction).
 __global__ void interp_kernel(const float* __restrict__ x, int T, int Tout, float scale, long long rows,
                               float* __restrict__ out) {
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= Tout) return;
   float src = __fsub_rn(__fmul_rn(__fadd_rn((float)i, 0.5f), scale), 0.5f);
@@ -180,6 +184,7 @@ __global__ void __launch_bounds__(kWarps * 32) prior_kernel(const Tv* __restrict
                                                             const float* __restrict__ noise, float scale,
                                                             float* __restrict__ m, float* __restrict__ logs,
                                                             float* __restrict__ zp) {
+  pdl_wait();
   __shared__ float sm[kTile][kTile + 1], sl[kTile][kTile + 1];
   const int b = blockIdx.z, t0 = blockIdx.x * kTile, c0 = blockIdx.y * kTile;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -224,8 +229,11 @@ cudaError_t launch_add_layernorm_ncl(const float* x, const float* y, const float
   const size_t smem = sizeof(float) * (size_t)C * (kTile + 1);
   cudaError_t e = set_smem((const void*)add_ln_ncl_kernel<float, false>, smem);
   if (e != cudaSuccess) return e;
-  add_ln_ncl_kernel<float, false><<<dim3(cdiv(T, kTile), B), kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T,
-                                                                                      eps, len, out);
+  {
+    const cudaError_t e_ = launch_k(add_ln_ncl_kernel<float, false>, dim3(cdiv(T, kTile), B), kWarps * 32, smem,
+                                    st, x, y, gamma, beta, C, T, eps, len, out);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -239,13 +247,19 @@ cudaError_t launch_add_layernorm_ncl_tm(const float* x, const float* y, const fl
   if (dt == Dt::F32) {
     e = set_smem((const void*)add_ln_ncl_kernel<float, true>, smem);
     if (e != cudaSuccess) return e;
-    add_ln_ncl_kernel<float, true><<<grid, kWarps * 32, smem, st>>>(x, y, gamma, beta, C, T, eps, len,
-                                                                    static_cast<float*>(out));
+    {
+      const cudaError_t e_ = launch_k(add_ln_ncl_kernel<float, true>, grid, kWarps * 32, smem, st, x, y, gamma,
+                                      beta, C, T, eps, len, static_cast<float*>(out));
+      if (e_ != cudaSuccess) return e_;
+    }
   } else {
     e = set_smem((const void*)add_ln_ncl_kernel<__nv_bfloat16, true>, smem);
     if (e != cudaSuccess) return e;
-    add_ln_ncl_kernel<__nv_bfloat16, true><<<grid, kWarps * 32, smem, st>>>(
-        x, y, gamma, beta, C, T, eps, len, static_cast<__nv_bfloat16*>(out));
+    {
+      const cudaError_t e_ = launch_k(add_ln_ncl_kernel<__nv_bfloat16, true>, grid, kWarps * 32, smem, st, x, y,
+                                      gamma, beta, C, T, eps, len, static_cast<__nv_bfloat16*>(out));
+      if (e_ != cudaSuccess) return e_;
+    }
   }
   return cudaGetLastError();
 }
@@ -260,13 +274,19 @@ cudaError_t launch_layernorm_tm_ncl(const void* v, Dt dt, int B, int T, int C, c
   if (dt == Dt::F32) {
     e = set_smem((const void*)ln_tm_ncl_kernel<float>, smem);
     if (e != cudaSuccess) return e;
-    ln_tm_ncl_kernel<float><<<grid, kWarps * 32, smem, st>>>(static_cast<const float*>(v), C, T, gamma, beta,
-                                                             eps, len, out);
+    {
+      const cudaError_t e_ = launch_k(ln_tm_ncl_kernel<float>, grid, kWarps * 32, smem, st,
+                                      static_cast<const float*>(v), C, T, gamma, beta, eps, len, out);
+      if (e_ != cudaSuccess) return e_;
+    }
   } else {
     e = set_smem((const void*)ln_tm_ncl_kernel<__nv_bfloat16>, smem);
     if (e != cudaSuccess) return e;
-    ln_tm_ncl_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, st>>>(
-        static_cast<const __nv_bfloat16*>(v), C, T, gamma, beta, eps, len, out);
+    {
+      const cudaError_t e_ = launch_k(ln_tm_ncl_kernel<__nv_bfloat16>, grid, kWarps * 32, smem, st,
+                                      static_cast<const __nv_bfloat16*>(v), C, T, gamma, beta, eps, len, out);
+      if (e_ != cudaSuccess) return e_;
+    }
   }
   return cudaGetLastError();
 }
@@ -276,7 +296,10 @@ cudaError_t launch_interpolate(const float* x, long long rows, int T, int Tout, 
   const float scale = (float)T / (float)Tout;
   const int threads = 128;
   const dim3 grid(cdiv(Tout, threads), (unsigned)std::min<long long>(rows, 65535));
-  interp_kernel<<<grid, threads, 0, st>>>(x, T, Tout, scale, rows, out);
+  {
+    const cudaError_t e_ = launch_k(interp_kernel, grid, threads, 0, st, x, T, Tout, scale, rows, out);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -287,11 +310,19 @@ cudaError_t launch_prior_sample(const void* stats, Dt dt, int B, int T, int Co, 
   if (zp && !noise) return cudaErrorInvalidValue;
   const dim3 grid(cdiv(T, kTile), cdiv(Co, kTile), B);
   if (dt == Dt::F32)
-    prior_kernel<float><<<grid, kWarps * 32, 0, st>>>(static_cast<const float*>(stats), Co, T, len, noise,
-                                                      noise_scale, m, logs, zp);
+    {
+      const cudaError_t e_ = launch_k(prior_kernel<float>, grid, kWarps * 32, 0, st,
+                                      static_cast<const float*>(stats), Co, T, len, noise, noise_scale, m, logs,
+                                      zp);
+      if (e_ != cudaSuccess) return e_;
+    }
   else
-    prior_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(stats), Co,
-                                                              T, len, noise, noise_scale, m, logs, zp);
+    {
+      const cudaError_t e_ = launch_k(prior_kernel<__nv_bfloat16>, grid, kWarps * 32, 0, st,
+                                      static_cast<const __nv_bfloat16*>(stats), Co, T, len, noise, noise_scale,
+                                      m, logs, zp);
+      if (e_ != cudaSuccess) return e_;
+    }
   return cudaGetLastError();
 }
 

@@ -22,6 +22,7 @@
 
 #include "../../include/gsvdec.h"
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 #include "safetensors.h"
 
 namespace gsv {
@@ -1302,6 +1303,8 @@ void begin_run(gsvdec* h, cudaStream_t st) {
 // null, lens_in [B] or null, z_dev [B][C][T0] fp32.
 int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_in, int B, int T0,
                 float* z_dev, FlowWs& w, cudaStream_t st) {
+  // Programmatic dependent launch for the flow's chain of short launches.
+  PdlScope pdl(true);
   begin_run(h, st);
   const double eb = (double)act_bytes(h);
   const int C = h->flow_C, hid = h->flow_hid, nl = h->flow_nwn;

@@ -8,6 +8,7 @@
 
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 
 namespace gsv {
 
@@ -18,6 +19,7 @@ namespace {
 template <typename T>
 __global__ void transpose_in_kernel(const float* __restrict__ z, int Cin, int Tsrc, int t_off,
                                     int Tn, const int* __restrict__ len, T* __restrict__ out) {
+  pdl_wait();
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -39,6 +41,7 @@ __global__ void transpose_in_kernel(const float* __restrict__ z, int Cin, int Ts
 __global__ void cond_kernel(const float* __restrict__ g, const float* __restrict__ wc,
                             const float* __restrict__ bc, int B, int gin, int C,
                             float* __restrict__ out) {
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
   if (warp >= B * C) return;
@@ -56,6 +59,7 @@ struct StageLen {
 
 __global__ void lengths_kernel(const int* __restrict__ len_in, int B, int T0, StageLen sl,
                                int nstage, int* __restrict__ lens) {
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int l = len_in ? len_in[b] : T0;
@@ -98,6 +102,7 @@ __global__ void __launch_bounds__(256) post_kernel(const T* __restrict__ x, int 
                                                    const float* __restrict__ w, int K, int pad,
                                                    float bias, const int* __restrict__ len,
                                                    float* __restrict__ wav, float* __restrict__ pre) {
+  pdl_wait();
   constexpr int kPer = 4;
   __shared__ float sw[64 * C];  // [K][C]
   for (int i = threadIdx.x; i < K * C; i += blockDim.x) sw[i] = w[i];
@@ -160,6 +165,7 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
                                                                  const int* __restrict__ len,
                                                                  float* __restrict__ wav,
                                                                  float* __restrict__ pre) {
+  pdl_wait();
   constexpr int C = 16;
   constexpr int U = C * (int)sizeof(T) / 16;  // 16-byte units per input row
   constexpr int kPostPer = post_per<T>(), kPostOut = kPostThreads * kPostPer;
@@ -222,6 +228,7 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
 template <typename T>
 __global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __restrict__ y,
                               const int* __restrict__ perm) {
+  pdl_wait();
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
@@ -250,6 +257,7 @@ template <typename T>
 __global__ void gate_kernel(const T* __restrict__ xin, const float* __restrict__ cond, int cond_ld,
                             int cond_off, int B, int L, int H, const int* __restrict__ len,
                             T* __restrict__ out) {
+  pdl_wait();
   const int groups = H / 8;
   const long long total = (long long)B * L * groups;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -282,18 +290,28 @@ cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_
                                 const int* len, void* zt, Dt dt, cudaStream_t st) {
   dim3 grid(cdiv(T, 32), cdiv(Cin, 32), B), block(32, 8);
   if (dt == Dt::F32)
-    transpose_in_kernel<float><<<grid, block, 0, st>>>(z, Cin, Tsrc, t_off, T, len,
-                                                       static_cast<float*>(zt));
+    {
+      const cudaError_t e_ = launch_k(transpose_in_kernel<float>, grid, block, 0, st, z, Cin, Tsrc, t_off, T,
+                                      len, static_cast<float*>(zt));
+      if (e_ != cudaSuccess) return e_;
+    }
   else
-    transpose_in_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(
-        z, Cin, Tsrc, t_off, T, len, static_cast<__nv_bfloat16*>(zt));
+    {
+      const cudaError_t e_ = launch_k(transpose_in_kernel<__nv_bfloat16>, grid, block, 0, st, z, Cin, Tsrc,
+                                      t_off, T, len, static_cast<__nv_bfloat16*>(zt));
+      if (e_ != cudaSuccess) return e_;
+    }
   return cudaGetLastError();
 }
 
 cudaError_t launch_cond(const float* g, const float* wc, const float* bc, int B, int gin, int C,
                         float* bias_bc, cudaStream_t st) {
   const int warps = B * C;
-  cond_kernel<<<cdiv(warps * 32, 256), 256, 0, st>>>(g, wc, bc, B, gin, C, bias_bc);
+  {
+    const cudaError_t e_ = launch_k(cond_kernel, cdiv(warps * 32, 256), 256, 0, st, g, wc, bc, B, gin, C,
+                                    bias_bc);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -302,7 +320,10 @@ cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, con
   if (nstage > 15) return cudaErrorInvalidValue;
   StageLen sl{};
   for (int s = 0; s < nstage; ++s) { sl.mul[s] = mul[s]; sl.add[s] = add[s]; }
-  lengths_kernel<<<cdiv(B, 128), 128, 0, st>>>(len_in, B, T0, sl, nstage, lens);
+  {
+    const cudaError_t e_ = launch_k(lengths_kernel, cdiv(B, 128), 128, 0, st, len_in, B, T0, sl, nstage, lens);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 
@@ -311,21 +332,35 @@ cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* 
   if (K > 64 || C != 16) return cudaErrorInvalidValue;
   if (wh != nullptr && K == 7) {
     if (dt == Dt::F32)
-      post_fast_kernel<float, 7><<<dim3(cdiv(L, kPostThreads * post_per<float>()), B), kPostThreads, 0, st>>>(
-          static_cast<const float*>(x), L, *wh, pad, bias, len, wav, pre);
+      {
+        const cudaError_t e_ = launch_k(post_fast_kernel<float, 7>,
+                                        dim3(cdiv(L, kPostThreads * post_per<float>()), B), kPostThreads, 0, st,
+                                        static_cast<const float*>(x), L, *wh, pad, bias, len, wav, pre);
+        if (e_ != cudaSuccess) return e_;
+      }
     else
-      post_fast_kernel<__nv_bfloat16, 7>
-          <<<dim3(cdiv(L, kPostThreads * post_per<__nv_bfloat16>()), B), kPostThreads, 0, st>>>(
-              static_cast<const __nv_bfloat16*>(x), L, *wh, pad, bias, len, wav, pre);
+      {
+        const cudaError_t e_ = launch_k(post_fast_kernel<__nv_bfloat16, 7>,
+                                        dim3(cdiv(L, kPostThreads * post_per<__nv_bfloat16>()), B),
+                                        kPostThreads, 0, st, static_cast<const __nv_bfloat16*>(x), L, *wh, pad,
+                                        bias, len, wav, pre);
+        if (e_ != cudaSuccess) return e_;
+      }
     return cudaGetLastError();
   }
   dim3 grid(cdiv(L, 256 * 4), B);
   if (dt == Dt::F32)
-    post_kernel<float, 16><<<grid, 256, 0, st>>>(static_cast<const float*>(x), L, w, K, pad, bias,
-                                                 len, wav, pre);
+    {
+      const cudaError_t e_ = launch_k(post_kernel<float, 16>, grid, 256, 0, st, static_cast<const float*>(x), L,
+                                      w, K, pad, bias, len, wav, pre);
+      if (e_ != cudaSuccess) return e_;
+    }
   else
-    post_kernel<__nv_bfloat16, 16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), L,
-                                                         w, K, pad, bias, len, wav, pre);
+    {
+      const cudaError_t e_ = launch_k(post_kernel<__nv_bfloat16, 16>, grid, 256, 0, st,
+                                      static_cast<const __nv_bfloat16*>(x), L, w, K, pad, bias, len, wav, pre);
+      if (e_ != cudaSuccess) return e_;
+    }
   return cudaGetLastError();
 }
 
@@ -333,10 +368,17 @@ cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, c
                           const int* perm) {
   dim3 grid(cdiv(L, 32), cdiv(C, 32), B), block(32, 8);
   if (dt == Dt::F32)
-    to_ncl_kernel<float><<<grid, block, 0, st>>>(static_cast<const float*>(x), L, C, y, perm);
+    {
+      const cudaError_t e_ = launch_k(to_ncl_kernel<float>, grid, block, 0, st, static_cast<const float*>(x), L,
+                                      C, y, perm);
+      if (e_ != cudaSuccess) return e_;
+    }
   else
-    to_ncl_kernel<__nv_bfloat16><<<grid, block, 0, st>>>(static_cast<const __nv_bfloat16*>(x), L,
-                                                         C, y, perm);
+    {
+      const cudaError_t e_ = launch_k(to_ncl_kernel<__nv_bfloat16>, grid, block, 0, st,
+                                      static_cast<const __nv_bfloat16*>(x), L, C, y, perm);
+      if (e_ != cudaSuccess) return e_;
+    }
   return cudaGetLastError();
 }
 
@@ -346,12 +388,18 @@ cudaError_t launch_gate(const void* xin, const float* cond, int cond_ld, int con
   const long long total = (long long)B * L * (H / 8);
   const int grid = (int)std::min<long long>((total + 255) / 256, 148LL * 16);
   if (dt == Dt::F32)
-    gate_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(xin), cond, cond_ld, cond_off, B, L,
-                                             H, len, static_cast<float*>(out));
+    {
+      const cudaError_t e_ = launch_k(gate_kernel<float>, grid, 256, 0, st, static_cast<const float*>(xin),
+                                      cond, cond_ld, cond_off, B, L, H, len, static_cast<float*>(out));
+      if (e_ != cudaSuccess) return e_;
+    }
   else
-    gate_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(xin), cond, cond_ld,
-                                                     cond_off, B, L, H, len,
-                                                     static_cast<__nv_bfloat16*>(out));
+    {
+      const cudaError_t e_ = launch_k(gate_kernel<__nv_bfloat16>, grid, 256, 0, st,
+                                      static_cast<const __nv_bfloat16*>(xin), cond, cond_ld, cond_off, B, L, H,
+                                      len, static_cast<__nv_bfloat16*>(out));
+      if (e_ != cudaSuccess) return e_;
+    }
   return cudaGetLastError();
 }
 

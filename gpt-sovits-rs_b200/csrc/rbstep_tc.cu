@@ -22,6 +22,7 @@
 // transform so the MMA warp always has work.  All waits are bounded.
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 #include "tc_common.cuh"
 
 namespace gsv {
@@ -131,8 +132,6 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   for (int c = threadIdx.x; c < 2 * C; c += kRbThreads) sb[c] = c < C ? op.b1[c] : op.b2[c - C];
-  if (P.len_smem)
-    for (int b = threadIdx.x; b < P.B; b += kRbThreads) slen[b] = P.len ? P.len[b] : P.L;
   if (threadIdx.x == 0) {
     mbar_init(w_full, 1);
     for (int s = 0; s < kRbWindowStages; ++s) {
@@ -152,6 +151,13 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Everything above touched only this CTA's resources, the kernel parameters
+  // and the static biases; the input window and lengths come from earlier kernels.
+  pdl_wait();
+  if (P.len_smem) {
+    for (int b = threadIdx.x; b < P.B; b += kRbThreads) slen[b] = P.len ? P.len[b] : P.L;
+    __syncthreads();
+  }
   const uint32_t tmem = *tmem_slot;
   int* err = P.err;
   const int ntiles = op.tiles;
@@ -329,6 +335,8 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
     }
     if (!ok && lane == 0) raise_err(err, abort, 15);
   }
+  // This CTA's work is done: the next kernel's CTAs may be scheduled.
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -369,7 +377,13 @@ cudaError_t launch_c(RbParams& P, cudaStream_t st) {
     n = std::min(n, P.op[i].tiles);
     P.cta_base[i + 1] = P.cta_base[i] + n;
   }
-  kern<<<P.cta_base[P.nops], kRbThreads, smem, st>>>(P);
+  {
+    const size_t smem_launch = pad_smem_to_occupancy(smem, per_sm, smem_sm);
+    e = kernel_setup(kern, smem_launch, &nregs);
+    if (e != cudaSuccess) return e;
+    const cudaError_t e_ = launch_k(kern, P.cta_base[P.nops], kRbThreads, smem_launch, st, P);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 

@@ -12,6 +12,7 @@
 
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 
 namespace gsv {
 
@@ -31,6 +32,7 @@ struct Cfg {
 
 template <int TN>
 __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_constant__ TapConvGroup grp) {
+  pdl_wait();
   using C = Cfg<TN>;
   const TapConv& op = grp.op[blockIdx.z];
   const int b = blockIdx.x / op.row_tiles;
@@ -119,7 +121,10 @@ cudaError_t launch_tn(TapConvGroup g, cudaStream_t st) {
     gy = max(gy, cdiv(op.N, TN));
   }
   if (gx == 0 || gy == 0) return cudaSuccess;
-  tapconv_f32_kernel<TN><<<dim3(gx, gy, g.n), kThreads, 0, st>>>(g);
+  {
+    const cudaError_t e_ = launch_k(tapconv_f32_kernel<TN>, dim3(gx, gy, g.n), kThreads, 0, st, g);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 

@@ -26,6 +26,7 @@
 // the group's error word, stops the CTA's loops and frees its TMEM.
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
+#include "gsv_pdl.cuh"
 #include "tc_common.cuh"
 
 namespace gsv {
@@ -418,10 +419,6 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   for (int o = 0; o < nops; ++o)
     for (int c = threadIdx.x; c < P.grp.op[o].Cout; c += kThreads)
       sbias[P.bias_off[o] + c] = P.grp.op[o].bias[c];
-  if (P.len_smem)
-    for (int o = 0; o < nops; ++o)
-      if (P.grp.op[o].len)
-        for (int b = threadIdx.x; b < P.grp.op[o].B; b += kThreads) slen[o * P.grp.op[o].B + b] = P.grp.op[o].len[b];
   if (threadIdx.x == 0) {
     for (int s = 0; s < SA; ++s) {
       mbar_init(a_full + 8 * s, 1);
@@ -443,6 +440,15 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Everything above touched only this CTA's resources, the kernel parameters
+  // and the static biases; activations and lengths come from earlier kernels.
+  pdl_wait();
+  if (P.len_smem) {
+    for (int o = 0; o < nops; ++o)
+      if (P.grp.op[o].len)
+        for (int b = threadIdx.x; b < P.grp.op[o].B; b += kThreads) slen[o * P.grp.op[o].B + b] = P.grp.op[o].len[b];
+    __syncthreads();
+  }
   const uint32_t tmem = *tmem_slot;
   int* err = P.grp.err;
   const int row_tiles = MT == 1 ? P.row_tiles : cdiv(P.row_tiles, MT), n_tiles = P.n_tiles;
@@ -719,6 +725,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     // Every TMA store of this warp has finished before the CTA exits.
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
+  // This CTA's work is done: the next kernel's CTAs may be scheduled.
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -786,7 +794,13 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   const int tiles = P.total_tiles / P.row_tiles * cdiv(P.row_tiles, MT);
   const int grid = std::min(tiles, sm_count() * per_sm);
   if (grid <= 0) return cudaSuccess;
-  kern<<<grid, kThreads, smem, st>>>(P);
+  const size_t smem_launch = pad_smem_to_occupancy(smem, per_sm, smem_sm);
+  e = kernel_setup(kern, smem_launch, &nregs);
+  if (e != cudaSuccess) return e;
+  {
+    const cudaError_t e_ = launch_k(kern, grid, kThreads, smem_launch, st, P);
+    if (e_ != cudaSuccess) return e_;
+  }
   return cudaGetLastError();
 }
 

@@ -312,6 +312,24 @@ int smem_per_sm() {
 // launch: the shared-memory carveout, the register count, and the dynamic
 // shared-memory limit (raised only when a launch needs more).  Short launches
 // (the flow's) were bound by these host calls.
+// Dynamic shared memory for a launch meant to hold per_sm CTAs per SM: smem,
+// padded where needed so that per_sm + 1 CTAs (1 KB reserved each) do not fit
+// the SM's shared memory.  A persistent grid of sm_count x per_sm CTAs then
+// lands exactly per_sm CTAs on every SM even when its CTAs are placed while
+// the previous kernel still holds some SMs (programmatic dependent launch);
+// otherwise an early-free SM can take extra CTAs (TMEM or registers permitting
+// only later) while another SM gets fewer, and the launch ends late.
+size_t pad_smem_to_occupancy(size_t smem, int per_sm, int smem_sm) {
+  const size_t floor_excl = (size_t)(smem_sm / (per_sm + 1)) + 16;  // (per_sm + 1) x this > smem_sm
+  const size_t pad = floor_excl > 1024 ? floor_excl - 1024 : 0;
+  const size_t out = std::max(smem, pad);
+  return out <= 227 * 1024 ? out : smem;
+}
+
+// Slots per device and kernel signature: every instantiation of a kernel
+// template shares one signature, and the tap GEMM has a few dozen.
+constexpr int kSetupSlots = 64;
+
 template <typename K>
 cudaError_t kernel_setup(K kern, size_t smem, int* regs) {
   struct Entry {
@@ -319,14 +337,14 @@ cudaError_t kernel_setup(K kern, size_t smem, int* regs) {
     bool ready = false;
   };
   static std::mutex mu;
-  static Entry table[64][8];
-  static const void* keys[64][8] = {};
+  static Entry table[64][kSetupSlots];
+  static const void* keys[64][kSetupSlots] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> lock(mu);
   Entry* en = nullptr;
-  for (int i = 0; i < 8 && !en; ++i) {
+  for (int i = 0; i < kSetupSlots && !en; ++i) {
     if (keys[dev][i] == (const void*)kern) en = &table[dev][i];
     else if (!keys[dev][i]) {
       keys[dev][i] = (const void*)kern;
@@ -334,7 +352,7 @@ cudaError_t kernel_setup(K kern, size_t smem, int* regs) {
     }
   }
   Entry scratch;
-  if (!en) en = &scratch;  // more than 8 instantiations on one device: no caching
+  if (!en) en = &scratch;  // more instantiations than slots on one device: no caching
   if (!en->ready) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                                          cudaSharedmemCarveoutMaxShared);
