@@ -1692,9 +1692,13 @@ int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengt
   const int* ld = lengths;
   float* wd = wav;
   if (mem_kind == GSV_MEM_HOST) {
-    // Copy only the requested frames of each channel row.
-    CUDA_TRY(cudaMemcpy2DAsync(w.zstage, sizeof(float) * T0, z + t_off, sizeof(float) * Tsrc,
-                               sizeof(float) * T0, (size_t)B * h->in_ch, cudaMemcpyHostToDevice, st));
+    // Copy only the requested frames of each channel row: one flat copy when
+    // that is all of them, else a pitched copy.
+    if (Tsrc == T0 && t_off == 0)
+      CUDA_TRY(cudaMemcpyAsync(w.zstage, z, sizeof(float) * (size_t)B * h->in_ch * T0, cudaMemcpyHostToDevice, st));
+    else
+      CUDA_TRY(cudaMemcpy2DAsync(w.zstage, sizeof(float) * T0, z + t_off, sizeof(float) * Tsrc,
+                                 sizeof(float) * T0, (size_t)B * h->in_ch, cudaMemcpyHostToDevice, st));
     zd = w.zstage;
     Tsrc = T0;
     t_off = 0;

@@ -354,9 +354,23 @@ size_t rb_smem(const RbParams& P, int ws) {
          8 * (8 + 2 * ws) + 16 + 2 * C * sizeof(float) + (P.len_smem ? sizeof(int) * (size_t)P.B : 0);
 }
 
+// CTAs of rbstep_kernel<C, WS> per SM for these parameters, bounded by
+// shared memory (1 KB reserved per CTA), registers, threads and TMEM; 0 when
+// the kernel cannot be set up.
+template <int C, int WS>
+int rb_per_sm(const RbParams& P) {
+  using S = RbShape<C>;
+  const size_t smem = rb_smem<C>(P, WS);
+  if (smem > 227 * 1024) return 0;
+  int nregs = 0;
+  if (kernel_setup(rbstep_kernel<C, WS>, smem, &nregs) != cudaSuccess) return 0;
+  const int regs_cta = ((nregs * 32 + 255) / 256 * 256) * (kRbThreads / 32);
+  return std::max(1, std::min({smem_per_sm() / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
+                               2048 / kRbThreads, (int)(512 / S::kTmemCols)}));
+}
+
 template <int C, int WS>
 cudaError_t launch_c(RbParams& P, cudaStream_t st) {
-  using S = RbShape<C>;
   const size_t smem = rb_smem<C>(P, WS);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   auto kern = rbstep_kernel<C, WS>;
@@ -364,9 +378,8 @@ cudaError_t launch_c(RbParams& P, cudaStream_t st) {
   cudaError_t e = kernel_setup(kern, smem, &nregs);
   if (e != cudaSuccess) return e;
   const int smem_sm = smem_per_sm();
-  const int regs_cta = ((nregs * 32 + 255) / 256 * 256) * (kRbThreads / 32);
-  const int per_sm = std::max(1, std::min({smem_sm / (int)(smem + 1024), 65536 / std::max(regs_cta, 1),
-                                           2048 / kRbThreads, (int)(512 / S::kTmemCols)}));
+  const int per_sm = rb_per_sm<C, WS>(P);
+  if (per_sm < 1) return cudaErrorInvalidValue;
   // Split the persistent CTAs over the branches in proportion to their tiles.
   long long total = 0;
   for (int i = 0; i < P.nops; ++i) total += P.op[i].tiles;
@@ -441,13 +454,15 @@ cudaError_t launch_rbstep(const RbStepGroup& g, cudaStream_t st) {
     Q.mapW1[0] = P.mapW1[i];
     Q.mapW2[0] = P.mapW2[i];
     Q.a_stage = ((kM + Q.op[0].d * (Q.op[0].k - 1)) * g.C * 2 + 1023) / 1024 * 1024;
-    const int sm = smem_per_sm();
+    // The 2-deep ring only where it buys a CTA per SM once registers, threads
+    // and TMEM are counted too (shared memory alone would pick it for every
+    // 16-channel branch, whose registers allow no extra CTA).
     cudaError_t e;
     if (g.C == 16) {
-      const bool two = sm / (int)(rb_smem<16>(Q, 2) + 1024) > sm / (int)(rb_smem<16>(Q, 3) + 1024);
+      const bool two = rb_per_sm<16, 2>(Q) > rb_per_sm<16, 3>(Q);
       e = two ? launch_c<16, 2>(Q, st) : launch_c<16, 3>(Q, st);
     } else {
-      const bool two = sm / (int)(rb_smem<32>(Q, 2) + 1024) > sm / (int)(rb_smem<32>(Q, 3) + 1024);
+      const bool two = rb_per_sm<32, 2>(Q) > rb_per_sm<32, 3>(Q);
       e = two ? launch_c<32, 2>(Q, st) : launch_c<32, 3>(Q, st);
     }
     if (e != cudaSuccess) return e;
