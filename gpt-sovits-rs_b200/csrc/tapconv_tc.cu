@@ -933,9 +933,16 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
                       : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
   if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 2, 4, 2, 3, 2>(P, stg, 1, st);
   if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
-  if (ck == 64 && nt == 64)
-    return branch_sum ? launch_staged<64, 64, false, 2, 2, 2, 2, 2, 2>(P, stg, 1, st)
-                      : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
+  if (ck == 64 && nt == 64) {
+    if (branch_sum) return launch_staged<64, 64, false, 2, 2, 2, 2, 2, 2>(P, stg, 1, st);
+    // Four weight stages (eight taps in flight) where that still fits two
+    // CTAs per SM: the 64-column MMAs are short, and with two stages the MMA
+    // warp waited on weight loads (measured: 64-channel conv1 / conv2 launches
+    // 4-8 % faster).  The dilation-5 windows leave no room for it.
+    const bool deep = stg == 0 ? cfg_fits<64, 64, false, 2, 4, 4, 0>(P, 2) : cfg_fits<64, 64, false, 2, 3, 4, 2>(P, 2);
+    return deep ? launch_staged<64, 64, false, 2, 4, 2, 3, 4>(P, stg, 2, st)
+                : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
+  }
   return cudaErrorInvalidValue;
 }
 
