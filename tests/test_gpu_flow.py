@@ -98,6 +98,44 @@ def test_flow_device_pointers(handles, sd_flow):
     assert np.array_equal(wav.cpu().numpy(), h.flow_decode(zp, g, [64, 40]))
 
 
+_NO_PDL_CHILD = r"""
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from __graft_entry__ import load_package
+gsv = load_package()
+sd = gsv.synth.make_state_dict(0, init="unit", bias="rand")
+sd.update(gsv.synth.make_flow_state_dict(init="unit"))
+d = np.load(sys.argv[2])
+outs = {}
+for mode in ("fp32", "bf16"):
+    h = gsv.Decoder.load(sd, device=0, mode=mode)
+    outs[mode] = h.flow_inverse(d["zp"], d["g"], [96, 51])
+    h.close()
+np.savez(sys.argv[3], **outs)
+"""
+
+
+def test_flow_same_with_and_without_dependent_launch(handles, tmp_path):
+    """The flow inverse launches with programmatic dependent launch: each
+    kernel may be scheduled before the previous one ends and waits on the
+    device for it.  A child process with GSVDEC_NO_PDL=1 (strict stream
+    order) must produce bit-identical outputs in both modes."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    zp, g = _inputs(2, 96, seed=13)
+    np.savez(tmp_path / "in.npz", zp=zp, g=g)
+    env = dict(os.environ, GSVDEC_NO_PDL="1")
+    r = subprocess.run([sys.executable, "-c", _NO_PDL_CHILD, str(ROOT), str(tmp_path / "in.npz"),
+                        str(tmp_path / "out.npz")], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    ref = np.load(tmp_path / "out.npz")
+    for mode in ("fp32", "bf16"):
+        assert np.array_equal(handles[mode].flow_inverse(zp, g, [96, 51]), ref[mode]), mode
+
+
 def test_handle_without_flow_reports_it(gsv):
     d = gsv.Decoder.load(gsv.synth.make_state_dict(0), device=0, mode="bf16")
     try:
