@@ -5,9 +5,10 @@
 // reference's own F32 arithmetic (src/config/mod.rs:52-58), each output an
 // fp32 dot product accumulated in the fixed order (segment, Cin chunk, tap,
 // channel).  One CTA computes a TQ x TN tile of the GEMM for one utterance:
-// the haloed input window [TQ + span rows x 16 channels] is staged once per
-// channel chunk in shared memory and reused by every tap (a tap is a row
-// shift inside the window), each thread accumulating a 4x4 register tile.
+// the haloed input window [TQ + span rows x 16 channels] and the chunk's
+// weights for every tap are staged once per channel chunk in shared memory;
+// every tap reads the window as a row shift, each thread accumulating an
+// RQ x RN register tile.
 #include <cuda_runtime.h>
 
 #include "gsv_epilogue.cuh"
@@ -22,36 +23,50 @@ constexpr int kThreads = 256;
 constexpr int kCK = 16;       // input channels per shared-memory chunk
 constexpr int kMaxSpan = 64;  // largest (ntaps - 1) * |offstep| supported
 
+// A CTA computes TQ x TN outputs; each thread an RQ x RN register tile (RQ
+// consecutive rows, RN consecutive columns).  Four columns per thread keep the
+// epilogue's per-element stores and residual loads 16-byte apart across a
+// warp (eight measured slower); eight rows per thread at 32/64 columns give
+// each thread more independent FMAs per weight load (fp32 forward 279 -> 271 ms
+// on B200 against four rows with per-tap weight staging).
 template <int TN>
 struct Cfg {
-  static constexpr int TX = TN / 4;        // threads along n
-  static constexpr int TY = kThreads / TX; // threads along q
-  static constexpr int TQ = TY * 4;        // rows per tile
+  static constexpr int RN = 4;
+  static constexpr int RQ = TN >= 32 ? 8 : 4;
+  static constexpr int TX = TN / RN;        // threads along n
+  static constexpr int TY = kThreads / TX;  // threads along q
+  static constexpr int TQ = TY * RQ;        // rows per tile
   static constexpr int W = TQ + kMaxSpan + 1;
 };
+
+// Dynamic shared memory: the window [kCK][W] and every tap's weights of one
+// channel chunk [ntaps][kCK][TN].
+template <int TN>
+size_t f32_smem(int max_taps) {
+  return sizeof(float) * ((size_t)kCK * Cfg<TN>::W + (size_t)max_taps * kCK * TN);
+}
 
 template <int TN>
 __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_constant__ TapConvGroup grp) {
   pdl_wait();
   using C = Cfg<TN>;
+  constexpr int RQ = C::RQ, RN = C::RN;
   const TapConv& op = grp.op[blockIdx.z];
   const int b = blockIdx.x / op.row_tiles;
   if (b >= op.B) return;
   const int q0 = (blockIdx.x % op.row_tiles) * C::TQ;
   const int n0 = blockIdx.y * TN;
   if (n0 >= op.N) return;
-
-  __shared__ float xs[kCK][C::W];
-  __shared__ __align__(16) float ws[kCK][TN];
-
+  extern __shared__ __align__(16) float f32_smem_raw[];
+  float* xs = f32_smem_raw;               // [kCK][W]
+  float* ws = f32_smem_raw + kCK * C::W;  // [tap][kCK][TN]
   const int tid = threadIdx.x;
   const int tx = tid % C::TX, ty = tid / C::TX;
-  float acc[4][4];
+  float acc[RQ][RN];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < RQ; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-
+    for (int j = 0; j < RN; ++j) acc[i][j] = 0.0f;
   const bool masked = op.len != nullptr && first_out_row(op, q0) >= op.len[b];
   if (!masked) {
     for (int s = 0; s < op.nseg; ++s) {
@@ -68,29 +83,35 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
           const int gr = q0 + minoff + r;
           float v = 0.0f;
           if (gr >= 0 && gr < sg.Lin && c0 + c < sg.Cin) v = x[(size_t)gr * sg.Cin + c0 + c];
-          xs[c][r] = v;
+          xs[c * C::W + r] = v;
         }
+        for (int idx = tid; idx < sg.ntaps * kCK * TN; idx += kThreads) {
+          const int j = idx / (kCK * TN), c = (idx / TN) % kCK, n = idx % TN;
+          float v = 0.0f;
+          if (c0 + c < sg.Cin && n0 + n < op.N) v = w[((size_t)j * sg.Cin + c0 + c) * op.N + n0 + n];
+          ws[idx] = v;
+        }
+        __syncthreads();
+        // Per output: taps in order, channels in order within a tap.
         for (int j = 0; j < sg.ntaps; ++j) {
-          __syncthreads();
-          for (int idx = tid; idx < kCK * TN; idx += kThreads) {
-            const int c = idx / TN, n = idx % TN;
-            float v = 0.0f;
-            if (c0 + c < sg.Cin && n0 + n < op.N)
-              v = w[((size_t)j * sg.Cin + c0 + c) * op.N + n0 + n];
-            ws[c][n] = v;
-          }
-          __syncthreads();
-          const int d = sg.off0 + j * sg.offstep - minoff + ty * 4;
+          const float* xr = xs + (sg.off0 + j * sg.offstep - minoff + ty * RQ);
+          const float* wr = ws + (size_t)j * kCK * TN + tx * RN;
 #pragma unroll
           for (int c = 0; c < kCK; ++c) {
-            const float4 wv = *reinterpret_cast<const float4*>(&ws[c][tx * 4]);
+            float wv[RN];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float xv = xs[c][d + i];
-              acc[i][0] = fmaf(xv, wv.x, acc[i][0]);
-              acc[i][1] = fmaf(xv, wv.y, acc[i][1]);
-              acc[i][2] = fmaf(xv, wv.z, acc[i][2]);
-              acc[i][3] = fmaf(xv, wv.w, acc[i][3]);
+            for (int k = 0; k < RN; k += 4) {
+              const float4 t = *reinterpret_cast<const float4*>(wr + c * TN + k);
+              wv[k] = t.x;
+              wv[k + 1] = t.y;
+              wv[k + 2] = t.z;
+              wv[k + 3] = t.w;
+            }
+#pragma unroll
+            for (int i = 0; i < RQ; ++i) {
+              const float xv = xr[c * C::W + i];
+#pragma unroll
+              for (int k = 0; k < RN; ++k) acc[i][k] = fmaf(xv, wv[k], acc[i][k]);
             }
           }
         }
@@ -98,12 +119,12 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int q = q0 + ty * 4 + i;
+  for (int i = 0; i < RQ; ++i) {
+    const int q = q0 + ty * RQ + i;
     if (q >= op.Q) continue;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
+    for (int j = 0; j < RN; ++j) {
+      const int n = n0 + tx * RN + j;
       if (n < op.N) epi_element<float>(op, b, q, n, acc[i][j]);
     }
   }
@@ -111,20 +132,27 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
 
 template <int TN>
 cudaError_t launch_tn(TapConvGroup g, cudaStream_t st) {
-  int gx = 0, gy = 0;
+  int gx = 0, gy = 0, max_taps = 1;
   for (int i = 0; i < g.n; ++i) {
     TapConv& op = g.op[i];
-    for (int s = 0; s < op.nseg; ++s)
+    for (int s = 0; s < op.nseg; ++s) {
       if ((op.seg[s].ntaps - 1) * abs(op.seg[s].offstep) > kMaxSpan) return cudaErrorInvalidValue;
+      max_taps = max(max_taps, op.seg[s].ntaps);
+    }
     op.row_tiles = cdiv(op.Q, Cfg<TN>::TQ);
     gx = max(gx, op.B * op.row_tiles);
     gy = max(gy, cdiv(op.N, TN));
   }
   if (gx == 0 || gy == 0) return cudaSuccess;
-  {
-    const cudaError_t e_ = launch_k(tapconv_f32_kernel<TN>, dim3(gx, gy, g.n), kThreads, 0, st, g);
-    if (e_ != cudaSuccess) return e_;
+  const size_t smem = f32_smem<TN>(max_taps);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(tapconv_f32_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+    if (e != cudaSuccess) return e;
   }
+  const cudaError_t e_ = launch_k(tapconv_f32_kernel<TN>, dim3(gx, gy, g.n), kThreads, smem, st, g);
+  if (e_ != cudaSuccess) return e_;
   return cudaGetLastError();
 }
 

@@ -931,7 +931,9 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   if (ck == 32 && nt == 32 && P.n_tiles == 1)
     return branch_sum ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
                       : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
-  if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 2, 4, 2, 3, 2>(P, stg, 1, st);
+  // 256 columns (one CTA per SM): three window stages when nothing is staged
+  // (rb0 conv2 / branch sum 2-6 % faster than two).
+  if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 3, 4, 2, 3, 2>(P, stg, 1, st);
   if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
   if (ck == 64 && nt == 64) {
     if (branch_sum) return launch_staged<64, 64, false, 2, 2, 2, 2, 2, 2>(P, stg, 1, st);
