@@ -50,6 +50,29 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+# Where the one JSON result line goes: stdout, or (under torchrun) a saved copy
+# of it while file descriptor 1 itself points at stderr, so that banners that
+# native libraries print to stdout (NCCL's version line) stay out of it.
+_JSON_FD = None
+
+
+def emit(obj):
+    line = json.dumps(obj) + "\n"
+    if _JSON_FD is None:
+        sys.stdout.write(line)
+        sys.stdout.flush()
+    else:
+        os.write(_JSON_FD, line.encode())
+
+
+def keep_stdout_for_json():
+    global _JSON_FD
+    if _JSON_FD is None:
+        sys.stdout.flush()
+        _JSON_FD = os.dup(1)
+        os.dup2(2, 1)
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -164,7 +187,7 @@ def run_reference(args, ws, rank):
     secs = audio_seconds(1, args.frames, 640) * args.steps
     value = secs / el
     sample = f"1 utterance x {args.frames / 50:g} s (z [1,192,{args.frames}]) per step"
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -175,7 +198,7 @@ def run_reference(args, ws, rank):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 def load_pkg():
@@ -262,9 +285,9 @@ def run_sweep(args):
         torch.cuda.empty_cache()
     tot_roof = sum(r["roof_ms"] for r in rows)
     tot = sum(r["ms"] for r in rows)
-    print(json.dumps({"workload": f"per-layer sweep, B={B} x {T0 / 50:g} s, {args.mode}",
-                      "peaks": pk_kind, "layers": rows, "sum_ms": tot, "sum_roof_ms": tot_roof,
-                      "frac": tot_roof / tot}), flush=True)
+    emit({"workload": f"per-layer sweep, B={B} x {T0 / 50:g} s, {args.mode}",
+          "peaks": pk_kind, "layers": rows, "sum_ms": tot, "sum_roof_ms": tot_roof,
+          "frac": tot_roof / tot})
     dec.close()
 
 
@@ -324,7 +347,7 @@ def run_flow(args):
         cpu = {"value": audio_seconds(1, T0, dec.hop) / dt, "unit": UNIT, "cores": oracle.num_threads(),
                "kind": "port", "sample": f"1 utterance of {T0 / 50:g} s (z_p [1,192,{T0}]), C restatement "
                                          "of the reference flow, float accumulation"}
-    print(json.dumps({
+    emit({
         "metric": f"flow inverse audio-sec/sec at B={B}x{T0 / 50:g} s {args.mode}",
         "value": secs / (ms_flow / 1e3), "unit": UNIT, "ms_per_step": ms_flow, "steps": args.steps,
         "warmup": args.warmup, "dtype": args.mode, "data": "synthetic: seeded N(0,1) z_p/g, N(0,0.01) "
@@ -335,7 +358,7 @@ def run_flow(args):
         "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
                            "sum_meas_ms": 1e3 * meas_s, "conv_tflops": flops / meas_s / 1e12 if meas_s else None,
                            "peaks": pk_kind},
-        "launches": len(stats), "cpu_baseline": cpu}), flush=True)
+        "launches": len(stats), "cpu_baseline": cpu})
     dec.close()
 
 
@@ -434,7 +457,7 @@ def run_encp(args):
         cpu = {"value": (T / 50.0) / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
                "sample": f"1 utterance of {T / 50:g} s (x [1,192,{T}]), C restatement of the chains, "
                          "float accumulation"}
-    print(json.dumps({
+    emit({
         "metric": f"EncP chains audio-sec/sec at B={B}x{T / 50:g} s {args.mode}",
         "value": secs / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": args.steps,
         "warmup": args.warmup, "dtype": args.mode, "timing": "CUDA graph replay of one step",
@@ -448,7 +471,7 @@ def run_encp(args):
                            "sum_meas_ms": 1e3 * meas_s, "peaks": pk_kind},
         "ffn_gemm": {"ms": gemm_ms, "tflops": gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else None,
                      "launches": len(gemm)},
-        "launches": len(stats), "cpu_baseline": cpu}), flush=True)
+        "launches": len(stats), "cpu_baseline": cpu})
     dec.close()
 
 
@@ -495,14 +518,14 @@ def run_load(args):
             dt = time.perf_counter() - t0
             cpu = {"value": size / dt / 1e6, "unit": "MB/s", "cores": oracle.num_threads(), "kind": "port",
                    "sample": f"the same {size / 1e6:.0f} MB file: safetensors read + {n_wn} weight-norm folds"}
-    print(json.dumps({
+    emit({
         "metric": f"checkpoint load MB/s ({args.mode})", "value": size / (ms / 1e3) / 1e6, "unit": "MB/s",
         "ms_per_load": ms, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "dtype": args.mode, "data": "synthetic: seeded v2 dec + flow + enc_p tensors, fp32 safetensors",
         "config": {"workload": f"gsvdec_create_from_file of a {size / 1e6:.0f} MB checkpoint "
                                "(mmap, fold, pack, upload; host wall clock incl. device sync)",
                    "file_bytes": size, "tensors": len(sd)},
-        "cpu_baseline": cpu}), flush=True)
+        "cpu_baseline": cpu})
 
 
 def run_sharded(args, ws, rank, local):
@@ -599,7 +622,7 @@ def run_sharded(args, ws, rank, local):
             whole = dec.forward(z, g)
             parity = {"max_rel_err": float(np.abs(res - whole).max() / max(np.abs(whole).max(), 1e-30)),
                       "bit_exact": bool(np.array_equal(res, whole))}
-        print(json.dumps({
+        emit({
             "metric": METRIC, "value": total_s * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -612,7 +635,7 @@ def run_sharded(args, ws, rank, local):
                     "ms_per_step": ms_host / args.steps,
                     "note": "host-memory API end to end (z/g from host, waveform back to host)"},
             "parity": parity,
-        }), flush=True)
+        })
     dec.close()
     if ws > 1:
         dist.destroy_process_group()
@@ -644,6 +667,8 @@ def main():
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     ws, rank, local = dist_setup()
+    if ws > 1:
+        keep_stdout_for_json()
 
     if args.impl == "reference":
         run_reference(args, ws, rank)
@@ -796,7 +821,7 @@ def main():
                          "workload, C restatement of the reference decoder, float accumulation"}
 
     if rank == 0:
-        print(json.dumps({
+        emit({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if args.mode == "bf16" else "f32",
@@ -809,7 +834,7 @@ def main():
                        "parallelism": f"utterance-sharded x{ws} (independent per-GPU batches)"},
             "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
             "layer_roofline": layer, "cpu_baseline": cpu, "clocks": clk,
-        }), flush=True)
+        })
     dec.close()
     if ws > 1:
         dist.destroy_process_group()
