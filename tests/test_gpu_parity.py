@@ -161,6 +161,25 @@ def test_load_file_matches_in_memory(gsv, sd_unit, dec_fp32, tmp_path):
     d2.close()
 
 
+def test_half_precision_weights_match_oracle(gsv, sd_unit):
+    """F16 / BF16 checkpoint tensors are upcast to fp32 at load (src/utils/
+    weights.rs:140-151) before the weight-norm fold and packing: the fp32
+    decoder on half-precision weights must match the oracle run on the same
+    values held in fp32 (the upcast is exact)."""
+    import torch
+    half = {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in sd_unit.items()}
+    half["dec.conv_pre.weight"] = torch.from_numpy(sd_unit["dec.conv_pre.weight"]).to(torch.float16)
+    up = {k: t.to(torch.float32).numpy() for k, t in half.items()}
+    z, g = gsv.synth.make_inputs(2, 5)
+    ref = oracle.decoder_forward(up, z, g)
+    dec = gsv.Decoder.load(half, device=0, mode="fp32")
+    try:
+        wav = dec.forward(z, g)
+    finally:
+        dec.close()
+    assert rel_max(wav, ref) <= FP32_REL
+
+
 # ----------------------------------------------------------------- BF16 mode
 
 
