@@ -18,7 +18,9 @@ roofline  the tap-GEMM conv launches: achieved = algorithmic FLOPs / average
           launch time (CUDA events around every launch on the forward's
           stream, over the timed region); layer_roofline adds the
           layer-weighted fraction sum(t_roof) / sum(t_measured), t_roof =
-          max(FLOPs / tensor peak, bytes / HBM peak) per conv.
+          max(FLOPs / tensor peak, bytes / HBM peak) per conv; roofline_by_bound
+          splits the same launches into compute-bound (TF/s against the tensor
+          peak) and HBM-bound (GB/s against the HBM peak).
 """
 from __future__ import annotations
 
@@ -229,6 +231,37 @@ def layer_roofline(stats, mode, pk):
                      "frac": round(t_roof / t_meas, 3) if t_meas > 0 else None,
                      "bound": "hbm" if s["bytes"] / bw >= comp else "compute"})
     return roof, meas, rows
+
+
+def roofline_by_bound(stats, mode, pk):
+    """The tap-GEMM launches split by what bounds each one (algorithmic FLOPs
+    against the compute peak vs algorithmic bytes against HBM): compute-bound
+    launches report achieved TF/s against the compute peak, HBM-bound ones
+    achieved GB/s against the HBM peak."""
+    p_comp = (pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) if mode == "bf16" else FP32_CORE_TFLOPS) * 1e12
+    bw = pk["hbm_gbs"] * 1e9
+    acc = {"compute": [0, 0.0, 0.0, 0.0], "hbm": [0, 0.0, 0.0, 0.0]}  # launches, flops, bytes, seconds
+    for s in stats:
+        if s["kind"] != 0 or s["ms"] <= 0:
+            continue
+        a = acc["hbm" if s["bytes"] / bw >= s["flops"] / p_comp else "compute"]
+        a[0] += 1
+        a[1] += s["flops"]
+        a[2] += s["bytes"]
+        a[3] += s["ms"] / 1e3
+    out = {}
+    n, f, _, t = acc["compute"]
+    if t > 0:
+        out["compute"] = {"launches": n, "achieved": f / t / 1e12, "peak": p_comp / 1e12, "unit": "TFLOP/s",
+                          "frac": f / t / p_comp, "share_of_time": None}
+    n, _, b, t2 = acc["hbm"]
+    if t2 > 0:
+        out["hbm"] = {"launches": n, "achieved": b / t2 / 1e9, "peak": bw / 1e9, "unit": "GB/s",
+                      "frac": b / t2 / bw, "share_of_time": None}
+    tot = acc["compute"][3] + acc["hbm"][3]
+    for k, v in out.items():
+        v["share_of_time"] = acc[k][3] / tot
+    return out
 
 
 def run_sweep(args):
@@ -803,6 +836,7 @@ def main():
                           "all 97 convs except conv_post)",
                 "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
                                                  else "nominal fp32 CUDA-core")}
+    by_bound = roofline_by_bound(stats, args.mode, pk)
     layer = {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
              "sum_meas_ms": 1e3 * meas_s, "hbm_gbs": pk["hbm_gbs"],
              "compute_tflops": peak, "peaks": pk_kind}
@@ -833,7 +867,7 @@ def main():
                              "buffers of 164 MB each (> 126 MB L2)",
                        "parallelism": f"utterance-sharded x{ws} (independent per-GPU batches)"},
             "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
-            "layer_roofline": layer, "cpu_baseline": cpu, "clocks": clk,
+            "layer_roofline": layer, "roofline_by_bound": by_bound, "cpu_baseline": cpu, "clocks": clk,
         })
     dec.close()
     if ws > 1:
