@@ -561,49 +561,63 @@ def run_load(args):
         "cpu_baseline": cpu})
 
 
-def run_sharded(args, ws, rank, local):
-    """Strong-scaling workloads over torch.distributed (NCCL): every rank gets the
-    same inputs, decodes its share and the finished waveform pieces are gathered
-    to rank 0 inside the timed region; rank 0 then checks the result against a
-    single-GPU decode of the same inputs."""
+class _Solo:
+    """torch.distributed's calls for a single process (no process group)."""
+
+    @staticmethod
+    def get_rank(group=None):
+        return 0
+
+    @staticmethod
+    def get_world_size(group=None):
+        return 1
+
+    @staticmethod
+    def all_gather(out, t, group=None):
+        out[0].copy_(t)
+
+    @staticmethod
+    def gather(t, gather_list=None, dst=0, group=None):
+        gather_list[0].copy_(t)
+
+
+def sharded_result(workload, dec, ws, rank, steps, warmup, mode):
+    """One strong-scaling workload over torch.distributed (NCCL): every rank gets
+    the same inputs, decodes its share, and the finished waveform pieces are
+    gathered to rank 0 inside the timed region; rank 0 then checks the result
+    against single-GPU decodes of the same inputs.  Returns the result dict on
+    rank 0 (None elsewhere).
+
+    varlen256: 256 utterances with frame counts ~ U[100, 1000] (2-20 s),
+    right-padded and length-masked, split by utterance (LPT) with up to 8
+    length buckets per rank.  long60: one 60 s utterance (3000 frames) split
+    into one contiguous frame range per rank, decoded with a 16-frame halo.
+    value: inputs resident in HBM, device-side batching and NCCL gather; e2e:
+    host arrays in (one pinned H2D per rank) and the whole waveform back on
+    rank 0's host (one D2H), through the same public calls."""
     import torch
     import torch.distributed as dist
-    if ws > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
     gsv = load_pkg()
-    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
-    dec = gsv.Decoder.load(sd, device=local, mode=args.mode)
     hop = dec.hop
     group = dist.group.WORLD if ws > 1 else None
-
-    class _Solo:  # the same calls on a single process
-        @staticmethod
-        def get_rank(group=None): return 0
-        @staticmethod
-        def get_world_size(group=None): return 1
-        @staticmethod
-        def all_gather(out, t, group=None): out[0].copy_(t)
-        @staticmethod
-        def gather(t, gather_list=None, dst=0, group=None): gather_list[0].copy_(t)
     dd = dist if ws > 1 else _Solo
-    if args.workload == "varlen256":
+    if workload == "varlen256":
         Bn, lo, hi = 256, 100, 1000
         lens = gsv.synth.make_lengths(Bn, lo, hi)
         z, g = gsv.synth.make_inputs(Bn, hi)
         total_s = float(lens.sum()) * hop / SAMPLE_RATE
         zd, gd = torch.from_numpy(z).cuda(), torch.from_numpy(g).cuda()
+        dev_decode = lambda zb, gb, lb: dec.forward_device(zb, gb, lb)  # noqa: E731
 
         def step_dev():  # inputs resident in HBM, device pieces gathered over NCCL
-            return gsv.shard.decode_batch_sharded(lambda zb, gb, lb: dec.forward_device(zb, gb, lb),
-                                                  zd, gd, lens, hop, dd, group, device="cuda")
+            return gsv.shard.decode_batch_sharded(dev_decode, zd, gd, lens, hop, dd, group, device="cuda")
 
-        def step_host():  # the host-memory API end to end
-            return gsv.shard.decode_batch_sharded(lambda zb, gb, lb: dec.forward(zb, gb, lengths=lb),
-                                                  z, g, lens, hop, dd, group, device="cuda")
-        workload = (f"{Bn} utterances, frames ~ U[{lo},{hi}] (2-20 s), sharded by utterance (LPT), "
-                    "up to 8 length buckets per rank")
+        def step_host():  # host arrays in, host waveform out on rank 0
+            return gsv.shard.decode_batch_sharded(dev_decode, z, g, lens, hop, dd, group, device="cuda")
+        desc = (f"{Bn} utterances, frames ~ U[{lo},{hi}] (2-20 s), right-padded to {hi}, length-masked, "
+                "sharded by utterance (LPT), up to 8 length buckets per rank")
+        h2d = int(z.nbytes + g.nbytes)
+        d2h = int(lens.sum()) * hop * 4
     else:
         T0, halo = 3000, 16
         z, g = gsv.synth.make_inputs(1, T0)
@@ -617,17 +631,19 @@ def run_sharded(args, ws, rank, local):
         def step_host():
             return gsv.shard.decode_long_chunked(
                 lambda b, e: dec.forward_chunk(z, g, b, e, halo=halo), T0, hop, dd, group, device="cuda")
-        workload = f"one 60 s utterance (z [1,192,{T0}]) in {ws} time chunks, halo {halo} frames"
+        desc = f"one 60 s utterance (z [1,192,{T0}]) in {ws} time chunks, halo {halo} frames"
+        h2d = int(z.nbytes + g.nbytes)
+        d2h = T0 * hop * 4
 
     def timed(step):
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             step()
         if ws > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             out = step()
         e1.record()
         torch.cuda.synchronize()
@@ -640,38 +656,107 @@ def run_sharded(args, ws, rank, local):
 
     ms, res = timed(step_dev)
     ms_host, _ = timed(step_host)
+    if rank != 0:
+        return None
+    res = [r.cpu().numpy() for r in res] if isinstance(res, list) else res.cpu().numpy()
+    if workload == "varlen256":
+        idx = [0, int(np.argmax(lens)), int(np.argmin(lens))]
+        errs, exact = [], True
+        for i in idx:
+            alone = dec.forward(z[i:i + 1, :, :lens[i]], g[i:i + 1])
+            errs.append(float(np.abs(res[i] - alone).max() / max(np.abs(alone).max(), 1e-30)))
+            exact = exact and bool(np.array_equal(res[i], alone))
+        parity = {"checked_utterances": idx, "max_rel_err": max(errs), "bit_exact": exact,
+                  "against": "single-GPU decode of each utterance alone"}
+    else:
+        whole = dec.forward(z, g)
+        parity = {"max_rel_err": float(np.abs(res - whole).max() / max(np.abs(whole).max(), 1e-30)),
+                  "bit_exact": bool(np.array_equal(res, whole)), "against": "single-GPU whole-utterance decode"}
+    return {
+        "value": total_s * steps / (ms / 1e3), "unit": UNIT, "n_gpus": ws, "steps": steps, "warmup": warmup,
+        "ms_per_step": ms / steps, "scaling": "strong", "dtype": "bf16" if mode == "bf16" else "f32",
+        "workload": desc, "audio_seconds_per_step": total_s,
+        "gather": "waveform pieces to rank 0 inside the timed region (NCCL gather)",
+        "e2e": {"value": total_s * steps / (ms_host / 1e3), "unit": UNIT, "ms_per_step": ms_host / steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "note": "host arrays in (one pinned H2D of each rank's share), waveform to rank 0's host "
+                        "(one D2H)"},
+        "parity": parity,
+    }
+
+
+def run_sharded(args, ws, rank, local):
+    """--workload varlen256 | long60 alone: one JSON line with that workload."""
+    import torch
+    import torch.distributed as dist
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    gsv = load_pkg()
+    sd = gsv.synth.make_state_dict(0, init="n001", bias="zero")
+    dec = gsv.Decoder.load(sd, device=local, mode=args.mode)
+    r = sharded_result(args.workload, dec, ws, rank, args.steps, args.warmup, args.mode)
     if rank == 0:
-        res = [r.cpu().numpy() for r in res] if isinstance(res, list) else res.cpu().numpy()
-    parity = None
-    if rank == 0:
-        if args.workload == "varlen256":
-            idx = [0, int(np.argmax(lens)), int(np.argmin(lens))]
-            errs = []
-            for i in idx:
-                alone = dec.forward(z[i:i + 1, :, :lens[i]], g[i:i + 1])
-                errs.append(float(np.abs(res[i] - alone).max() / max(np.abs(alone).max(), 1e-30)))
-            parity = {"checked_utterances": idx, "max_rel_err": max(errs)}
-        else:
-            whole = dec.forward(z, g)
-            parity = {"max_rel_err": float(np.abs(res - whole).max() / max(np.abs(whole).max(), 1e-30)),
-                      "bit_exact": bool(np.array_equal(res, whole))}
         emit({
-            "metric": METRIC, "value": total_s * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16" if args.mode == "bf16" else "f32",
+            "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": r["dtype"],
             "data": "synthetic: seeded N(0,1) z/g, N(0,0.01) random-init weights, zero bias",
-            "config": {"workload": workload, "audio_seconds_per_step": total_s, "mode": args.mode,
-                       "gather": "waveform pieces to rank 0 inside the timed region (dist.gather)",
+            "config": {"workload": r["workload"], "audio_seconds_per_step": r["audio_seconds_per_step"],
+                       "mode": args.mode, "gather": r["gather"],
                        "value_path": "inputs resident in HBM, device-side batching and gather"},
-            "e2e": {"value": total_s * args.steps / (ms_host / 1e3), "unit": UNIT,
-                    "ms_per_step": ms_host / args.steps,
-                    "note": "host-memory API end to end (z/g from host, waveform back to host)"},
-            "parity": parity,
+            "e2e": r["e2e"], "parity": r["parity"],
         })
     dec.close()
     if ws > 1:
         dist.destroy_process_group()
+
+
+def fp32_cfg1_result(sd, local, steps, warmup, pk):
+    """The fp32 CUDA-core mode on its own config: batch 1 x 5 s (z [1,192,250]),
+    device-resident inputs, CUDA events around K steps; the layer-weighted
+    roofline and the tap-GEMM launches' achieved TF/s against the nominal FP32
+    CUDA-core peak (148 SMs x 128 lanes x 2 FLOP x 1.965 GHz)."""
+    import torch
+    gsv = load_pkg()
+    dec = gsv.Decoder.load(sd, device=local, mode="fp32")
+    z, g = gsv.synth.make_inputs(1, 250)
+    zt, gt = torch.from_numpy(z).cuda(), torch.from_numpy(g).cuda()
+    out = torch.empty(250 * dec.hop, device="cuda")
+    for _ in range(warmup):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec.forward_device(zt, gt, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    dec.set_stage_timing(2)
+    for _ in range(steps):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    stats = dec.launch_stats()
+    dec.set_stage_timing(0)
+    dec.close()
+    roof_s, meas_s, _ = layer_roofline(stats, "fp32", pk)
+    conv = [s_ for s_ in stats if s_["kind"] == 0]
+    f_conv = sum(s_["flops"] for s_ in conv)
+    t_conv = sum(s_["ms"] for s_ in conv) / 1e3
+    achieved = f_conv / t_conv / 1e12 if t_conv > 0 else None
+    return {
+        "value": 5.0 / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+        "dtype": "f32", "workload": "fp32 CUDA-core mode, B=1 x 5 s (z [1,192,250] -> 160 000 samples)",
+        "roofline": {"bound": "fp32-core", "achieved": achieved, "peak": FP32_CORE_TFLOPS, "unit": "TFLOP/s",
+                     "frac": achieved / FP32_CORE_TFLOPS if achieved else None,
+                     "kernel": "tapconv_f32 launches of one forward (all 97 convs except conv_post)",
+                     "peak_source": "nominal FP32 CUDA-core peak (not in MEASURED_PEAKS.json)"},
+        "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
+                           "sum_meas_ms": 1e3 * meas_s},
+        "gpu_launches": len(stats) * steps,
+    }
 
 
 def main():
@@ -695,6 +780,8 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="per-layer sweep: every distinct conv shape at --batch (64 by default) "
                          "x --frames, in --mode; prints one JSON line per mode")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the extra keys (varlen256, long60 strong scaling; fp32 batch-1 5 s)")
     ap.add_argument("--once", action="store_true",
                     help="one untimed forward, then exit (a short, fixed launch list for ncu)")
     args = ap.parse_args()
@@ -758,8 +845,32 @@ def main():
         log(f"one forward: {dec.launch_count()} launches, finite={bool(torch.isfinite(out).all())}")
         dec.close()
         return
-    for _ in range(args.warmup):
-        dec.forward_device(zt, gt, out=out)
+    # With N > 1 every step's waveform is gathered to rank 0 over NCCL inside
+    # the timed region (the north star's one collective).  The gather of step
+    # i runs on a second stream while step i + 1 decodes into the other of two
+    # output buffers; a buffer is overwritten only after its gather has read it.
+    outs = [out, torch.empty_like(out)]
+    comm = torch.cuda.Stream() if ws > 1 else None
+    ev_done = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_sent = [torch.cuda.Event(), torch.cuda.Event()]
+    gathered = [[torch.empty_like(out) for _ in range(ws)] for _ in range(2)] if (ws > 1 and rank == 0) else None
+
+    def step(i):
+        k = i % 2
+        if comm is not None:
+            stream.wait_event(ev_sent[k])
+        dec.forward_device(zt, gt, out=outs[k])
+        if comm is not None:
+            ev_done[k].record(stream)
+            with torch.cuda.stream(comm):
+                comm.wait_event(ev_done[k])
+                dist.gather(outs[k], gather_list=gathered[k] if rank == 0 else None, dst=0)
+                ev_sent[k].record(comm)
+
+    for i in range(args.warmup):
+        step(i)
+    if comm is not None:
+        stream.wait_stream(comm)
     torch.cuda.synchronize()
     launches_per_step = dec.launch_count()
     clocks = ClockSampler(local)
@@ -769,8 +880,10 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        dec.forward_device(zt, gt, out=out)
+    for i in range(args.steps):
+        step(i)
+    if comm is not None:
+        stream.wait_stream(comm)  # every gather has landed before the clock stops
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -778,6 +891,14 @@ def main():
     ms = max_over_ranks(e0.elapsed_time(e1))
     value = ws * secs_per_step * args.steps / (ms / 1e3)
     assert torch.isfinite(out).all().item()
+    gather_check = None
+    if gathered is not None:
+        # rank r's last waveform arrived intact: rank 0 decodes rank r's inputs itself
+        last = gathered[(args.steps - 1) % 2]
+        zr, gr = gsv.synth.make_inputs(B, T0, seed_z=1 + 1000 * (ws - 1), seed_g=2 + 1000 * (ws - 1))
+        mine = dec.forward_device(torch.from_numpy(zr).cuda(), torch.from_numpy(gr).cuda())
+        torch.cuda.synchronize()
+        gather_check = {"rank_checked": ws - 1, "bit_exact": bool(torch.equal(last[ws - 1], mine))}
     # Per-launch profile (roofline) from the same K steps run again with an
     # event pair around every launch; kept out of the timed loop above, which
     # runs the launches exactly as a caller does (no event records between
@@ -854,6 +975,18 @@ def main():
                "sample": f"{reps} x 1 utterance of {T0 / 50:g} s (z [1,192,{T0}]) of the same "
                          "workload, C restatement of the reference decoder, float accumulation"}
 
+    # ---- the other configs of the same job, as extra keys of the line -------
+    extra = {}
+    if not args.no_extra:
+        xs, xw = max(1, min(args.steps, 5)), 3
+        for wl in ("varlen256", "long60"):
+            r = sharded_result(wl, dec, ws, rank, xs, xw, args.mode)
+            if rank == 0:
+                extra[wl] = r
+        if rank == 0:
+            extra["fp32_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk)
+        barrier()
+
     if rank == 0:
         emit({
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
@@ -865,9 +998,12 @@ def main():
                        "batch": B, "frames": T0, "mode": args.mode,
                        "l2": "no flush: one step moves several GB of activations through "
                              "buffers of 164 MB each (> 126 MB L2)",
-                       "parallelism": f"utterance-sharded x{ws} (independent per-GPU batches)"},
+                       "parallelism": f"utterance-sharded x{ws}" + (
+                           ", every step's waveform gathered to rank 0 over NCCL inside the timed region "
+                           "(overlapped with the next step's decode)" if ws > 1 else "")},
             "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "roofline": roofline,
             "layer_roofline": layer, "roofline_by_bound": by_bound, "cpu_baseline": cpu, "clocks": clk,
+            "gather_check": gather_check, **extra,
         })
     dec.close()
     if ws > 1:

@@ -41,6 +41,8 @@ EXPORTS = (
     "gsvdec_layer_names", "gsvdec_last_error", "gsvdec_flow_info", "gsvdec_flow_inverse",
     "gsvdec_flow_decode", "gsvdec_encp_info", "gsvdec_encp_add_norm", "gsvdec_encp_ffn", "gsvdec_encp_layer",
     "gsvdec_encp_speed_len", "gsvdec_encp_interpolate", "gsvdec_encp_project",
+    "gsvdec_forward_multi", "gsvdec_plan_multi", "gsvdec_sync_status", "gsvdec_selftest_wait",
+    "gsvdec_set_alloc_fail_after", "gsvdec_workspace_bytes",
 )
 
 # EncP encoder stacks (GSV_ENCP_SSL / _TEXT / _2), by their enc_p.* names.
@@ -117,6 +119,12 @@ def library(path: Optional[Path] = None) -> ctypes.CDLL:
     lib.gsvdec_encp_speed_len.argtypes = [i, ctypes.c_float, ctypes.POINTER(i)]
     lib.gsvdec_encp_interpolate.argtypes = [vp, vp, i, i, i, i, vp, i, vp]
     lib.gsvdec_encp_project.argtypes = [vp, vp, vp, i, i, vp, ctypes.c_float, vp, vp, vp, i, vp]
+    lib.gsvdec_forward_multi.argtypes = [ctypes.POINTER(vp), i, vp, vp, vp, i, i, vp, i, vp]
+    lib.gsvdec_plan_multi.argtypes = [vp, i, i, i, vp, vp]
+    lib.gsvdec_sync_status.argtypes = [vp, vp]
+    lib.gsvdec_selftest_wait.argtypes = [vp, ctypes.c_int64, vp]
+    lib.gsvdec_set_alloc_fail_after.argtypes = [i]
+    lib.gsvdec_workspace_bytes.argtypes = [vp, ctypes.POINTER(ctypes.c_int64)]
     _lib = lib
     return lib
 
@@ -277,6 +285,30 @@ class Decoder:
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
             B, T0, ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(st)))
         return out
+
+    # -- status of stream-async calls, failure hooks --------------------------
+    def sync_status(self, stream=None) -> None:
+        """Wait for ``stream`` (default: torch's current stream on this device)
+        and raise GsvDecError(GSV_E_TIMEOUT) if a device wait of a
+        stream-async call on this handle gave up (gsvdec_sync_status)."""
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(self.info["device"]).cuda_stream
+        _check(library().gsvdec_sync_status(self._h, ctypes.c_void_p(stream)))
+
+    def selftest_wait(self, limit_ns: int = 1_000_000, stream=None) -> None:
+        """Queue the give-up self-test (gsvdec_selftest_wait): one bounded wait
+        that nothing completes, reported like a decode kernel's give-up."""
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(self.info["device"]).cuda_stream
+        _check(library().gsvdec_selftest_wait(self._h, int(limit_ns), ctypes.c_void_p(stream)))
+
+    def workspace_bytes(self) -> int:
+        """Device bytes held for per-call workspaces (not the weights)."""
+        n = ctypes.c_int64()
+        _check(library().gsvdec_workspace_bytes(self._h, ctypes.byref(n)))
+        return n.value
 
     # -- ResidualCouplingBlock::forward(reverse = true) ----------------------
     @property
@@ -618,3 +650,69 @@ class Decoder:
         n = ctypes.c_int()
         _check(library().gsvdec_launch_count(self._h, 0, 0, ctypes.byref(n)))
         return n.value
+
+
+# -- several devices ------------------------------------------------------------
+
+def set_alloc_fail_after(n: int) -> None:
+    """Allocation-failure hook: the next ``n`` device allocations of the library
+    succeed and later ones fail with GSV_E_OOM; ``n < 0`` turns it off."""
+    _check(library().gsvdec_set_alloc_fail_after(int(n)))
+
+
+def plan_multi(lengths, n_workers: int, T0: Optional[int] = None):
+    """The utterance plan of gsvdec_forward_multi: (worker, bucket) per utterance
+    (-1 for empty utterances)."""
+    ln = np.ascontiguousarray(np.asarray(lengths, np.int32))
+    B = ln.size
+    T = int(ln.max()) if T0 is None else int(T0)
+    worker = np.empty(B, np.int32)
+    bucket = np.empty(B, np.int32)
+    _check(library().gsvdec_plan_multi(_ptr(ln), B, max(T, 1), n_workers, _ptr(worker), _ptr(bucket)))
+    return worker, bucket
+
+
+def _handles(decoders):
+    arr = (ctypes.c_void_p * len(decoders))()
+    for i, d in enumerate(decoders):
+        arr[i] = d._h
+    return arr
+
+
+def forward_multi(decoders: Sequence["Decoder"], x, g=None, lengths: Optional[Sequence[int]] = None,
+                  out=None) -> np.ndarray:
+    """Decoder::forward over several handles (one per device) on host arrays:
+    utterances split over the handles, or one utterance (B = 1) split in time
+    with a recomputed halo; the flattened waveform, as forward returns it."""
+    z = _host_f32(x)
+    if z.ndim != 3:
+        raise ValueError("x must be [B, C, T]")
+    B, _, T0 = z.shape
+    gg = _host_f32(g)
+    ln = None if lengths is None else np.ascontiguousarray(np.asarray(lengths, np.int32))
+    if ln is not None and ln.shape != (B,):
+        raise ValueError("lengths must hold one value per utterance")
+    hop = decoders[0].hop
+    if out is None:
+        out = np.empty(B * hop * T0, np.float32)
+    elif out.dtype != np.float32 or out.size != B * hop * T0 or not out.flags.c_contiguous:
+        raise ValueError("out must be a contiguous float32 array of B*hop*T0 samples")
+    _check(library().gsvdec_forward_multi(_handles(decoders), len(decoders), _ptr(z), _ptr(gg), _ptr(ln), B, T0,
+                                          _ptr(out), MEM_HOST, None))
+    return out
+
+
+def forward_multi_device(decoders: Sequence["Decoder"], z, g=None, lengths=None, out=None, stream=None):
+    """forward_multi on CUDA tensors of decoders[0]'s device (stream-async in
+    that device's stream order)."""
+    import torch
+    B, _, T0 = z.shape
+    assert z.is_cuda and z.dtype == torch.float32 and z.is_contiguous()
+    hop = decoders[0].hop
+    if out is None:
+        out = torch.empty(B * hop * T0, device=z.device, dtype=torch.float32)
+    st = stream if stream is not None else torch.cuda.current_stream(z.device).cuda_stream
+    p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    _check(library().gsvdec_forward_multi(_handles(decoders), len(decoders), p(z), p(g), p(lengths), B, T0,
+                                          p(out), MEM_DEVICE, ctypes.c_void_p(st)))
+    return out

@@ -41,6 +41,10 @@ struct RbStepGroup {
 bool rbstep_supported(int C, int k, int d);
 cudaError_t launch_rbstep(const RbStepGroup& g, cudaStream_t st);
 
+// One CTA whose bounded hand-off wait runs out after limit_ns and sets *err
+// (selftest.cu; gsvdec_selftest_wait).
+cudaError_t launch_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st);
+
 // z [B][Cin][Tsrc] fp32 (NCL, the reference layout) -> zt [B][T][Cin] (time-major)
 // reading frames [t_off, t_off + T); frames t >= len[b] are written as 0.
 cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_off, int T,
@@ -51,6 +55,9 @@ cudaError_t launch_cond(const float* g, const float* wc, const float* bc, int B,
 // Per-stage valid lengths: lens[s*B + b] for s in [0, nstage], stage 0 = frames.
 cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, const int* add,
                            int nstage, int* lens, cudaStream_t st);
+// wav [B][hop * T0]: samples past hop * len[b] of each utterance set to 0
+// (len device-resident, clamped to [0, T0]).
+cudaError_t launch_zero_tails(float* wav, const int* len, int B, int T0, int hop, cudaStream_t st);
 // conv_post weights [K][16] by value (K <= 16), for the kernel-parameter path.
 struct PostWeights {
   float w[16 * 16];

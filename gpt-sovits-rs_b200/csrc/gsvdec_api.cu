@@ -12,6 +12,7 @@
 #include <cstring>
 #include <initializer_list>
 #include <algorithm>
+#include <array>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -54,6 +55,35 @@ int set_err(int code, const char* fmt, ...) {
     int rc_ = (expr);          \
     if (rc_ != GSV_OK) return rc_; \
   } while (0)
+
+// Allocation-failure hook (gsvdec_set_alloc_fail_after): while the budget is
+// >= 0, each device allocation of the library consumes one unit and fails
+// with cudaErrorMemoryAllocation (reported as GSV_E_OOM) once none is left.
+// -1 (the default) injects nothing.
+std::atomic<int> g_alloc_budget{-1};
+
+cudaError_t dev_malloc_raw(void** p, size_t bytes) {
+  *p = nullptr;
+  int b = g_alloc_budget.load();
+  while (b >= 0) {
+    if (b == 0) return cudaErrorMemoryAllocation;
+    if (g_alloc_budget.compare_exchange_weak(b, b - 1)) break;
+  }
+  const cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // not sticky: keep it out of later launch checks
+    *p = nullptr;
+  }
+  return e;
+}
+
+template <typename T>
+cudaError_t dev_malloc(T** p, size_t bytes) {
+  void* v = nullptr;
+  const cudaError_t e = dev_malloc_raw(&v, bytes);
+  *p = static_cast<T*>(v);
+  return e;
+}
 
 // ---------------------------------------------------------------------------
 // Host-side model, following Decoder::load (src/models/sovits_decoder.rs:231-293).
@@ -608,7 +638,11 @@ struct gsvdec {
   float* d_post_w = nullptr;
   PostWeights post_wh{};  // the same [K][C] weights by value (K <= 16)
   bool post_wh_ok = false;
-  int* d_err = nullptr;  // error word of the bounded device waits
+  // Error word of the bounded device waits: pinned, mapped host memory, so
+  // the host can read what a stream-async call's kernels reported without a
+  // copy or a sync (h_err), while the kernels write it through d_err.
+  int* h_err = nullptr;
+  int* d_err = nullptr;
   std::map<int, size_t> ident_off;  // bf16: identity weights per channel width
   std::map<std::string, GemmConv> layers;  // every tap-GEMM conv by its dec.* prefix
   std::string layer_names;                 // newline-separated, in forward order
@@ -668,6 +702,10 @@ struct gsvdec {
   float* d_encp_norm = nullptr;
   void* ews = nullptr;
   size_t ews_bytes = 0;
+  // Multi-device decode (gsvdec_forward_multi): this handle's worker stream
+  // and events, created on first use on the handle's device.
+  cudaStream_t mstream = nullptr;
+  cudaEvent_t mev_in = nullptr, mev_done = nullptr;
 };
 
 namespace gsv {
@@ -855,7 +893,7 @@ int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w) {
     if (h->ws) CUDA_TRY(cudaFree(h->ws));
     h->ws = nullptr;
     h->ws_bytes = 0;
-    CUDA_TRY(cudaMalloc(&h->ws, need));
+    CUDA_TRY(dev_malloc(&h->ws, need));
     h->ws_bytes = need;
   }
   char* p = static_cast<char*>(h->ws);
@@ -1262,7 +1300,7 @@ int ensure_flow_ws(gsvdec* h, int B, int T0, FlowWs& w) {
     if (h->fws) CUDA_TRY(cudaFree(h->fws));
     h->fws = nullptr;
     h->fws_bytes = 0;
-    CUDA_TRY(cudaMalloc(&h->fws, need));
+    CUDA_TRY(dev_malloc(&h->fws, need));
     h->fws_bytes = need;
   }
   char* p = static_cast<char*>(h->fws);
@@ -1392,12 +1430,33 @@ int flow_device(gsvdec* h, const float* zp, const float* gdev, const int* lens_i
 }
 
 // A kernel whose bounded wait gave up leaves a non-zero word in d_err.
+// Called after the stream of the call has been synchronised: every kernel of
+// this call (and of earlier stream-async calls on the same handle) has
+// finished, so the word holds everything they reported.
 int check_device_error(gsvdec* h) {
-  int v = 0;
-  CUDA_TRY(cudaMemcpy(&v, h->d_err, sizeof v, cudaMemcpyDeviceToHost));
+  volatile int* w = h->h_err;
+  const int v = *w;
   if (v != 0) {
-    CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
-    return set_err(GSV_E_TIMEOUT, "a device wait gave up (code %d); results are invalid", v);
+    *w = 0;
+    return set_err(GSV_E_TIMEOUT,
+                   "a device wait of this call or of an earlier stream-async call on this handle gave up "
+                   "(code %d); its results are invalid", v);
+  }
+  return GSV_OK;
+}
+
+// Entry check of every call: a stream-async call returns before its kernels
+// run, so a wait that gave up in one of them is reported here, by the next
+// call on the handle, which then does nothing else (the word is cleared, so
+// the call after it proceeds).  Reads host memory only: no sync.
+int take_async_error(gsvdec* h) {
+  volatile int* w = h->h_err;
+  const int v = *w;
+  if (v != 0) {
+    *w = 0;
+    return set_err(GSV_E_TIMEOUT,
+                   "a device wait of an earlier stream-async call on this handle gave up (code %d); "
+                   "that call's results are invalid (this call did not run)", v);
   }
   return GSV_OK;
 }
@@ -1433,6 +1492,12 @@ int check_device(int device) {
     return set_err(GSV_E_UNSUPPORTED, "device %d is sm_%d%d; libgsvdec is built for sm_100a (B200)", device, p.major, p.minor);
   return GSV_OK;
 }
+
+void destroy_impl(gsvdec* h);
+// Frees everything a partly built handle holds when creation fails.
+struct HandleDeleter {
+  void operator()(gsvdec* h) const { destroy_impl(h); }
+};
 
 int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t** out) {
   if (!out) return set_err(GSV_E_INVALID_ARG, "out is NULL");
@@ -1470,7 +1535,7 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   }
   GSV_TRY(check_device(device));
   CUDA_TRY(cudaSetDevice(device));
-  std::unique_ptr<gsvdec> h(new gsvdec());
+  std::unique_ptr<gsvdec, HandleDeleter> h(new gsvdec());
   h->mode = mode;
   h->device = device;
   h->dt = mode == GSV_MODE_FP32 ? Dt::F32 : Dt::BF16;
@@ -1600,22 +1665,22 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   // Fill the arena, then upload.
   pk.finish();
   h->w_bytes = pk.size;
-  CUDA_TRY(cudaMalloc(&h->d_w, std::max<size_t>(h->w_bytes, 256)));
+  CUDA_TRY(dev_malloc(&h->d_w, std::max<size_t>(h->w_bytes, 256)));
   CUDA_TRY(cudaMemcpy(h->d_w, pk.arena.get(), h->w_bytes, cudaMemcpyHostToDevice));
-  CUDA_TRY(cudaMalloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
+  CUDA_TRY(dev_malloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
   CUDA_TRY(cudaMemcpy(h->d_bias, pk.biases.data(), sizeof(float) * pk.biases.size(), cudaMemcpyHostToDevice));
   if (post_w.size() <= sizeof(h->post_wh.w) / sizeof(float)) {
     std::copy(post_w.begin(), post_w.end(), h->post_wh.w);
     h->post_wh_ok = true;
   }
-  CUDA_TRY(cudaMalloc(&h->d_post_w, sizeof(float) * post_w.size()));
+  CUDA_TRY(dev_malloc(&h->d_post_w, sizeof(float) * post_w.size()));
   CUDA_TRY(cudaMemcpy(h->d_post_w, post_w.data(), sizeof(float) * post_w.size(), cudaMemcpyHostToDevice));
   if (h->has_cond) {
-    CUDA_TRY(cudaMalloc(&h->d_cond_w, sizeof(float) * m.cond.w.size()));
+    CUDA_TRY(dev_malloc(&h->d_cond_w, sizeof(float) * m.cond.w.size()));
     CUDA_TRY(cudaMemcpy(h->d_cond_w, m.cond.w.data(), sizeof(float) * m.cond.w.size(), cudaMemcpyHostToDevice));
     std::vector<float> cb(h->C0, 0.0f);
     if (!m.cond.b.empty()) cb = m.cond.b;
-    CUDA_TRY(cudaMalloc(&h->d_cond_b, sizeof(float) * cb.size()));
+    CUDA_TRY(dev_malloc(&h->d_cond_b, sizeof(float) * cb.size()));
     CUDA_TRY(cudaMemcpy(h->d_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
   if (!h->flow.empty() && h->flow[0].has_cond) {
@@ -1624,23 +1689,24 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
       cw.insert(cw.end(), flow_cond_w[l].begin(), flow_cond_w[l].end());
       cb.insert(cb.end(), flow_cond_b[l].begin(), flow_cond_b[l].end());
     }
-    CUDA_TRY(cudaMalloc(&h->d_flow_cond_w, sizeof(float) * cw.size()));
+    CUDA_TRY(dev_malloc(&h->d_flow_cond_w, sizeof(float) * cw.size()));
     CUDA_TRY(cudaMemcpy(h->d_flow_cond_w, cw.data(), sizeof(float) * cw.size(), cudaMemcpyHostToDevice));
-    CUDA_TRY(cudaMalloc(&h->d_flow_cond_b, sizeof(float) * cb.size()));
+    CUDA_TRY(dev_malloc(&h->d_flow_cond_b, sizeof(float) * cb.size()));
     CUDA_TRY(cudaMemcpy(h->d_flow_cond_b, cb.data(), sizeof(float) * cb.size(), cudaMemcpyHostToDevice));
   }
   if (!h->flow.empty()) {
-    CUDA_TRY(cudaMalloc(&h->d_flow_perm, sizeof(int) * h->flow_perm_host.size()));
+    CUDA_TRY(dev_malloc(&h->d_flow_perm, sizeof(int) * h->flow_perm_host.size()));
     CUDA_TRY(cudaMemcpy(h->d_flow_perm, h->flow_perm_host.data(), sizeof(int) * h->flow_perm_host.size(),
                         cudaMemcpyHostToDevice));
   }
   if (!encp_norm.empty()) {
-    CUDA_TRY(cudaMalloc(&h->d_encp_norm, sizeof(float) * encp_norm.size()));
+    CUDA_TRY(dev_malloc(&h->d_encp_norm, sizeof(float) * encp_norm.size()));
     CUDA_TRY(cudaMemcpy(h->d_encp_norm, encp_norm.data(), sizeof(float) * encp_norm.size(),
                         cudaMemcpyHostToDevice));
   }
-  CUDA_TRY(cudaMalloc(&h->d_err, sizeof(int)));
-  CUDA_TRY(cudaMemset(h->d_err, 0, sizeof(int)));
+  CUDA_TRY(cudaHostAlloc(reinterpret_cast<void**>(&h->h_err), sizeof(int), cudaHostAllocMapped));
+  *reinterpret_cast<volatile int*>(h->h_err) = 0;
+  CUDA_TRY(cudaHostGetDevicePointer(reinterpret_cast<void**>(&h->d_err), h->h_err, 0));
   for (auto& e : h->ev) CUDA_TRY(cudaEventCreate(&e));
   *out = h.release();
   return GSV_OK;
@@ -1655,7 +1721,7 @@ void destroy_impl(gsvdec* h) {
   cudaFree(h->d_cond_w);
   cudaFree(h->d_cond_b);
   cudaFree(h->d_post_w);
-  cudaFree(h->d_err);
+  if (h->h_err) cudaFreeHost(h->h_err);
   cudaFree(h->ws);
   cudaFree(h->lws);
   cudaFree(h->fws);
@@ -1669,6 +1735,9 @@ void destroy_impl(gsvdec* h) {
   for (auto& run : h->runs)
     for (auto& e : run) cudaEventDestroy(e);
   for (auto& e : h->pool) cudaEventDestroy(e);
+  if (h->mstream) cudaStreamDestroy(h->mstream);
+  if (h->mev_in) cudaEventDestroy(h->mev_in);
+  if (h->mev_done) cudaEventDestroy(h->mev_done);
   cudaSetDevice(prev);
   delete h;
 }
@@ -1683,6 +1752,7 @@ int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengt
     return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
   if ((int64_t)B * max_act_elems(h, T0) > (int64_t)1 << 40)
     return set_err(GSV_E_INVALID_ARG, "request too large");
+  GSV_TRY(take_async_error(h));
   CUDA_TRY(cudaSetDevice(h->device));
   Workspace w;
   GSV_TRY(ensure_ws(h, B, T0, taps != nullptr, w));
@@ -1742,6 +1812,7 @@ int layer_impl(gsvdec* h, const char* name, const float* x, int B, int L, float*
   const int Cout = post ? 1 : it->second.Cout;
   const int Lout = post ? L : it->second.Lout(L);
   if (Lout <= 0) return set_err(GSV_E_INVALID_ARG, "output length %d <= 0", Lout);
+  GSV_TRY(take_async_error(h));
   CUDA_TRY(cudaSetDevice(h->device));
   const size_t eb = act_bytes(h);
   auto al = [](size_t v) { return (v + 255) / 256 * 256; };
@@ -1751,7 +1822,7 @@ int layer_impl(gsvdec* h, const char* name, const float* x, int B, int L, float*
     if (h->lws) CUDA_TRY(cudaFree(h->lws));
     h->lws = nullptr;
     h->lws_bytes = 0;
-    CUDA_TRY(cudaMalloc(&h->lws, need));
+    CUDA_TRY(dev_malloc(&h->lws, need));
     h->lws_bytes = need;
   }
   char* p = static_cast<char*>(h->lws);
@@ -1818,6 +1889,7 @@ int flow_impl(gsvdec* h, const float* zp, const float* g, const int32_t* lengths
     return set_err(GSV_E_SHAPE, "flow width %d != decoder input width %d", h->flow_C, h->in_ch);
   if ((int64_t)B * T0 * std::max(h->flow_C, 2 * h->flow_hid) > (int64_t)1 << 36)
     return set_err(GSV_E_INVALID_ARG, "request too large");
+  GSV_TRY(take_async_error(h));
   CUDA_TRY(cudaSetDevice(h->device));
   FlowWs fw;
   GSV_TRY(ensure_flow_ws(h, B, T0, fw));
@@ -1879,7 +1951,7 @@ int encp_scratch(gsvdec* h, std::initializer_list<size_t> sizes, std::vector<cha
     if (h->ews) CUDA_TRY(cudaFree(h->ews));
     h->ews = nullptr;
     h->ews_bytes = 0;
-    CUDA_TRY(cudaMalloc(&h->ews, need));
+    CUDA_TRY(dev_malloc(&h->ews, need));
     h->ews_bytes = need;
   }
   char* p = static_cast<char*>(h->ews);
@@ -1896,7 +1968,7 @@ int encp_common(gsvdec* h, int B, int T, int mem_kind) {
   if (B <= 0 || T <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T=%d must be positive", B, T);
   if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
     return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
-  return GSV_OK;
+  return take_async_error(h);
 }
 
 int encp_layer(gsvdec* h, int stack, int layer, const gsvdec::EncpLayer** L) {
@@ -2369,6 +2441,34 @@ int gsvdec_launch_count(gsvdec_t* h, int B, int T0, int* count) {
   return GSV_OK;
 }
 
+int gsvdec_sync_status(gsvdec_t* h, void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  return gsv::check_device_error(h);
+}
+
+int gsvdec_selftest_wait(gsvdec_t* h, int64_t limit_ns, void* stream) {
+  if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
+  if (limit_ns < 1000 || limit_ns > 10000000000ll)
+    return gsv::set_err(GSV_E_INVALID_ARG, "limit_ns %lld outside [1e3, 1e10]", (long long)limit_ns);
+  GSV_TRY(gsv::take_async_error(h));
+  CUDA_TRY(cudaSetDevice(h->device));
+  CUDA_TRY(gsv::launch_wait_selftest(h->d_err, (unsigned long long)limit_ns, static_cast<cudaStream_t>(stream)));
+  return GSV_OK;
+}
+
+int gsvdec_set_alloc_fail_after(int n) {
+  gsv::g_alloc_budget.store(n < 0 ? -1 : n);
+  return GSV_OK;
+}
+
+int gsvdec_workspace_bytes(const gsvdec_t* h, int64_t* bytes) {
+  if (!h || !bytes) return gsv::set_err(GSV_E_INVALID_ARG, "NULL argument");
+  *bytes = (int64_t)(h->ws_bytes + h->lws_bytes + h->fws_bytes + h->ews_bytes);
+  return GSV_OK;
+}
+
 }  // extern "C"
 
 // ---------------------------------------------------------------------------
@@ -2443,6 +2543,13 @@ extern "C" int gsvdec_forward_noalloc(gsvdec_t* h, const float* z, const float* 
   if (!h) return gsv::set_err(GSV_E_INVALID_ARG, "handle is NULL");
   if (!z || !wav) return gsv::set_err(GSV_E_INVALID_ARG, "z and wav must not be NULL");
   if (B <= 0 || T0 <= 0) return gsv::set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
+  // The same size bound as gsvdec_forward, before any byte count is formed:
+  // below it the scratch sizes cannot overflow.
+  if ((int64_t)B * gsv::max_act_elems(h, T0) > (int64_t)1 << 40)
+    return gsv::set_err(GSV_E_INVALID_ARG,
+                        "gsvdec_forward_noalloc: B=%d x T0=%d does not fit the static scratch (%zu bytes)", B, T0,
+                        gsv::kNoAllocScratchBytes);
+  GSV_TRY(gsv::take_async_error(h));
   {
     const cudaError_t e = cudaSetDevice(h->device);
     if (e != cudaSuccess) return gsv::set_err(GSV_E_CUDA, "cudaSetDevice: %s", cudaGetErrorString(e));
@@ -2452,8 +2559,428 @@ extern "C" int gsvdec_forward_noalloc(gsvdec_t* h, const float* z, const float* 
   gsv::Workspace w;
   GSV_TRY(gsv::carve_noalloc(h, B, T0, static_cast<char*>(scratch), gsv::kNoAllocScratchBytes, w));
   const float* gd = (h->has_cond && g) ? g : nullptr;
-  return gsv::forward_device(h, z, T0, 0, gd, lengths, B, T0, wav, w, nullptr,
-                             static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GSV_TRY(gsv::forward_device(h, z, T0, 0, gd, lengths, B, T0, wav, w, nullptr, st));
+  // Stage timers, when enabled, are read back exactly as gsvdec_forward does.
+  return gsv::collect_timing(h, st);
 }
 
 extern "C" int64_t gsvdec_noalloc_scratch_bytes(void) { return (int64_t)gsv::kNoAllocScratchBytes; }
+
+// ---------------------------------------------------------------------------
+// Several devices in one call (gsvdec_forward_multi).
+//
+// Utterances are independent and an output frame depends only on a bounded
+// window of input frames, so the decode shards with no exchange step.  A
+// batch is split by utterance (longest-processing-time balance of the frame
+// counts, then up to kMultiMaxBuckets length buckets per device so short
+// utterances are not padded to the longest); one long utterance (B = 1) is
+// split into contiguous frame ranges, each decoded with kMultiChunkHalo input
+// frames recomputed on both sides.  Every handle runs its share on its own
+// stream from its own host thread.  The only transfers are each device's
+// inputs in and its waveform pieces out, as copy-engine copies between
+// devices (NVLink); no kernel reads another device's memory.  The reference
+// decodes on one device (src/config/mod.rs:68-80): no counterpart there.
+
+namespace gsv {
+namespace {
+
+constexpr int kMultiMaxBuckets = 8;
+constexpr int kMultiBucketOverhead = 300;  // per-forward cost in frames (its launch chain)
+constexpr int kMultiChunkHalo = 16;
+constexpr int kMultiMaxHandles = 64;
+
+// Utterance indices per worker: longest first onto the least-loaded worker,
+// ties to the lower worker; each list ascending.
+std::vector<std::vector<int>> plan_utterances(const std::vector<int>& len, const std::vector<int>& ids, int n) {
+  std::vector<int> order(ids);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return len[a] != len[b] ? len[a] > len[b] : a < b; });
+  std::vector<long long> load(n, 0);
+  std::vector<std::vector<int>> out(n);
+  for (int i : order) {
+    int r = 0;
+    for (int k = 1; k < n; ++k)
+      if (load[k] < load[r]) r = k;
+    out[r].push_back(i);
+    load[r] += len[i];
+  }
+  for (auto& v : out) std::sort(v.begin(), v.end());
+  return out;
+}
+
+// Length buckets of one worker's utterances: the split of the length-sorted
+// order into at most kMultiMaxBuckets contiguous runs that minimises
+// sum(run size x its longest length + kMultiBucketOverhead) (dynamic
+// programming; equal-count runs beyond 4096 utterances).  Returns lists of
+// utterance ids, each ascending, the buckets by length.
+std::vector<std::vector<int>> plan_buckets(const std::vector<int>& len, const std::vector<int>& ids) {
+  const int n = (int)ids.size();
+  std::vector<std::vector<int>> out;
+  if (n == 0) return out;
+  std::vector<int> order(ids);
+  std::stable_sort(order.begin(), order.end(),
+                   [&](int a, int b) { return len[a] != len[b] ? len[a] < len[b] : a < b; });
+  const int K = std::max(1, std::min(kMultiMaxBuckets, n));
+  std::vector<int> cuts;  // run boundaries in sorted order: 0 = c0 < c1 < ... = n
+  if (n > 4096) {
+    for (int k = 0; k <= K; ++k) cuts.push_back((int)((long long)n * k / K));
+  } else {
+    const double INF = 1e300;
+    std::vector<std::vector<double>> best(K + 1, std::vector<double>(n + 1, INF));
+    std::vector<std::vector<int>> cut(K + 1, std::vector<int>(n + 1, 0));
+    best[0][0] = 0.0;
+    for (int k = 1; k <= K; ++k)
+      for (int j = 1; j <= n; ++j)
+        for (int i = k - 1; i < j; ++i) {
+          const double c = best[k - 1][i] + (double)(j - i) * len[order[j - 1]] + kMultiBucketOverhead;
+          if (c < best[k][j]) {
+            best[k][j] = c;
+            cut[k][j] = i;
+          }
+        }
+    int kb = 1;
+    for (int k = 2; k <= K; ++k)
+      if (best[k][n] < best[kb][n]) kb = k;
+    cuts.push_back(n);
+    for (int k = kb, j = n; k > 0; --k) {
+      j = cut[k][j];
+      cuts.push_back(j);
+    }
+    std::reverse(cuts.begin(), cuts.end());
+  }
+  for (size_t r = 0; r + 1 < cuts.size(); ++r) {
+    if (cuts[r + 1] <= cuts[r]) continue;
+    std::vector<int> b(order.begin() + cuts[r], order.begin() + cuts[r + 1]);
+    std::sort(b.begin(), b.end());
+    out.push_back(std::move(b));
+  }
+  return out;
+}
+
+// One forward of a worker: a masked batch of utterances, or one time chunk.
+struct MultiJob {
+  std::vector<int> idx;   // utterances (batch job)
+  int T = 0;              // frames of the batch: its longest utterance
+  int lo = 0, hi = 0;     // chunk job: input window [lo, hi) ...
+  int b = 0, e = 0;       // ... and the frames [b, e) it keeps
+};
+
+struct MultiCall {
+  const float* z;
+  const float* g;
+  const int32_t* len_user;  // the caller's lengths pointer (or null)
+  std::vector<int> len;     // host copy (all T0 without lengths)
+  int B, T0, in_ch, gin, hop, mem_kind, dev0;
+  float* wav;
+  cudaEvent_t ev_in;        // device mode: recorded on the caller's stream
+  bool chunked;
+};
+
+// Pitched copy of `height` rows of `width` bytes between (possibly) different
+// devices, by a copy engine.
+cudaError_t copy_rows(void* dst, int ddev, size_t dpitch, const void* src, int sdev, size_t spitch, size_t width,
+                      size_t height, cudaStream_t s) {
+  if (width == 0 || height == 0) return cudaSuccess;
+  const bool flat = height == 1 || (dpitch == width && spitch == width);
+  if (ddev == sdev)
+    return flat ? cudaMemcpyAsync(dst, src, width * height, cudaMemcpyDeviceToDevice, s)
+                : cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDeviceToDevice, s);
+  if (flat) return cudaMemcpyPeerAsync(dst, ddev, src, sdev, width * height, s);
+  cudaMemcpy3DPeerParms p = {};
+  p.srcPtr = make_cudaPitchedPtr(const_cast<void*>(src), spitch, width, height);
+  p.srcDevice = sdev;
+  p.dstPtr = make_cudaPitchedPtr(dst, dpitch, width, height);
+  p.dstDevice = ddev;
+  p.extent = make_cudaExtent(width, height, 1);
+  return cudaMemcpy3DPeerAsync(&p, s);
+}
+
+// Runs of consecutive utterance ids in a sorted list: (position, first id, count).
+std::vector<std::array<int, 3>> id_runs(const std::vector<int>& idx) {
+  std::vector<std::array<int, 3>> r;
+  for (int k = 0; k < (int)idx.size();) {
+    int m = 1;
+    while (k + m < (int)idx.size() && idx[k + m] == idx[k] + m) ++m;
+    r.push_back({k, idx[k], m});
+    k += m;
+  }
+  return r;
+}
+
+int multi_worker_device(gsvdec* h, const std::vector<MultiJob>& jobs, const MultiCall& c) {
+  CUDA_TRY(cudaSetDevice(h->device));
+  if (!h->mstream) CUDA_TRY(cudaStreamCreateWithFlags(&h->mstream, cudaStreamNonBlocking));
+  if (!h->mev_done) CUDA_TRY(cudaEventCreateWithFlags(&h->mev_done, cudaEventDisableTiming));
+  const cudaStream_t s = h->mstream;
+  CUDA_TRY(cudaStreamWaitEvent(s, c.ev_in, 0));
+  int maxB = 1, maxT = 1;
+  for (const MultiJob& j : jobs) {
+    maxB = std::max(maxB, c.chunked ? 1 : (int)j.idx.size());
+    maxT = std::max(maxT, c.chunked ? j.hi - j.lo : j.T);
+  }
+  Workspace w;
+  GSV_TRY(ensure_ws(h, maxB, maxT, false, w));  // allocate once for every job
+  const bool cond = c.g && h->has_cond;
+  const size_t C = c.in_ch;
+  for (const MultiJob& j : jobs) {
+    if (c.chunked) {
+      const int win = j.hi - j.lo;
+      GSV_TRY(ensure_ws(h, 1, win, false, w));
+      const float* zsrc = c.z;
+      int Tsrc = c.T0, toff = j.lo;
+      if (h->device != c.dev0) {  // the window [C][win] into this device
+        CUDA_TRY(copy_rows(w.zstage, h->device, (size_t)win * 4, c.z + j.lo, c.dev0, (size_t)c.T0 * 4,
+                           (size_t)win * 4, C, s));
+        zsrc = w.zstage;
+        Tsrc = win;
+        toff = 0;
+      }
+      const float* gd = cond ? c.g : nullptr;
+      if (cond && h->device != c.dev0) {
+        CUDA_TRY(copy_rows(w.gstage, h->device, 0, c.g, c.dev0, 0, (size_t)c.gin * 4, 1, s));
+        gd = w.gstage;
+      }
+      GSV_TRY(forward_device(h, zsrc, Tsrc, toff, gd, nullptr, 1, win, w.wav, w, nullptr, s));
+      CUDA_TRY(copy_rows(c.wav + (size_t)j.b * c.hop, c.dev0, 0, w.wav + (size_t)(j.b - j.lo) * c.hop, h->device, 0,
+                         (size_t)(j.e - j.b) * c.hop * 4, 1, s));
+      continue;
+    }
+    const int nb = (int)j.idx.size(), T = j.T;
+    GSV_TRY(ensure_ws(h, nb, T, false, w));
+    const auto runs = id_runs(j.idx);
+    for (const auto& r : runs)  // z[u][:, :T] of each utterance -> zstage[k]
+      CUDA_TRY(copy_rows(w.zstage + (size_t)r[0] * C * T, h->device, (size_t)T * 4, c.z + (size_t)r[1] * C * c.T0,
+                         c.dev0, (size_t)c.T0 * 4, (size_t)T * 4, C * r[2], s));
+    const float* gd = nullptr;
+    if (cond) {
+      for (const auto& r : runs)
+        CUDA_TRY(copy_rows(w.gstage + (size_t)r[0] * c.gin, h->device, 0, c.g + (size_t)r[1] * c.gin, c.dev0, 0,
+                           (size_t)c.gin * r[2] * 4, 1, s));
+      gd = w.gstage;
+    }
+    const int* ld = nullptr;
+    if (c.len_user) {
+      std::vector<int> lb(nb);
+      for (int k = 0; k < nb; ++k) lb[k] = c.len[j.idx[k]];
+      // pageable source: staged by the driver before the call returns
+      CUDA_TRY(cudaMemcpyAsync(w.lstage, lb.data(), sizeof(int) * nb, cudaMemcpyHostToDevice, s));
+      ld = w.lstage;
+    }
+    GSV_TRY(forward_device(h, w.zstage, T, 0, gd, ld, nb, T, w.wav, w, nullptr, s));
+    const size_t row = (size_t)c.hop * T;  // decoded samples per utterance (zero past its length)
+    for (const auto& r : runs)
+      CUDA_TRY(copy_rows(c.wav + (size_t)r[1] * c.hop * c.T0, c.dev0, (size_t)c.hop * c.T0 * 4,
+                         w.wav + (size_t)r[0] * row, h->device, row * 4, row * 4, r[2], s));
+  }
+  CUDA_TRY(cudaEventRecord(h->mev_done, s));
+  return GSV_OK;
+}
+
+int multi_worker_host(gsvdec* h, const std::vector<MultiJob>& jobs, const MultiCall& c) {
+  CUDA_TRY(cudaSetDevice(h->device));
+  if (!h->mstream) CUDA_TRY(cudaStreamCreateWithFlags(&h->mstream, cudaStreamNonBlocking));
+  const cudaStream_t s = h->mstream;
+  const bool cond = c.g && h->has_cond;
+  const size_t C = c.in_ch;
+  std::vector<float> zb, gb, ob;
+  for (const MultiJob& j : jobs) {
+    if (c.chunked) {
+      GSV_TRY(forward_impl(h, c.z, cond ? c.g : nullptr, nullptr, 1, c.T0, j.lo, j.hi - j.lo,
+                           c.wav + (size_t)j.b * c.hop, GSV_MEM_HOST, s, nullptr, (int64_t)(j.b - j.lo) * c.hop,
+                           (int64_t)(j.e - j.b) * c.hop));
+      continue;
+    }
+    const int nb = (int)j.idx.size(), T = j.T;
+    zb.resize((size_t)nb * C * T);
+    for (int k = 0; k < nb; ++k)
+      for (size_t ch = 0; ch < C; ++ch)
+        memcpy(&zb[((size_t)k * C + ch) * T], c.z + ((size_t)j.idx[k] * C + ch) * c.T0, sizeof(float) * T);
+    if (cond) {
+      gb.resize((size_t)nb * c.gin);
+      for (int k = 0; k < nb; ++k)
+        memcpy(&gb[(size_t)k * c.gin], c.g + (size_t)j.idx[k] * c.gin, sizeof(float) * c.gin);
+    }
+    std::vector<int32_t> lb(nb);
+    for (int k = 0; k < nb; ++k) lb[k] = c.len[j.idx[k]];
+    const size_t row = (size_t)c.hop * T;
+    ob.resize((size_t)nb * row);
+    GSV_TRY(forward_impl(h, zb.data(), cond ? gb.data() : nullptr, c.len_user ? lb.data() : nullptr, nb, T, 0, T,
+                         ob.data(), GSV_MEM_HOST, s, nullptr, 0, (int64_t)nb * row));
+    for (int k = 0; k < nb; ++k) {
+      float* dst = c.wav + (size_t)j.idx[k] * c.hop * c.T0;
+      const size_t valid = (size_t)c.hop * lb[k];
+      memcpy(dst, &ob[(size_t)k * row], sizeof(float) * valid);
+      memset(dst + valid, 0, sizeof(float) * ((size_t)c.hop * c.T0 - valid));
+    }
+  }
+  return GSV_OK;
+}
+
+// Restores the calling thread's current device when the call returns.
+struct DeviceGuard {
+  int prev = -1;
+  DeviceGuard() {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int multi_impl(gsvdec* const* hs, int n, const float* z, const float* g, const int32_t* lengths, int B, int T0,
+               float* wav, int mem_kind, cudaStream_t st) {
+  if (!hs || n < 1 || n > kMultiMaxHandles)
+    return set_err(GSV_E_INVALID_ARG, "need 1..%d handles (got %d)", kMultiMaxHandles, n);
+  if (!z || !wav) return set_err(GSV_E_INVALID_ARG, "z and wav must not be NULL");
+  if (B <= 0 || T0 <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+    return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
+  gsvdec* h0 = hs[0];
+  for (int i = 0; i < n; ++i) {
+    if (!hs[i]) return set_err(GSV_E_INVALID_ARG, "handle %d is NULL", i);
+    for (int k = 0; k < i; ++k)
+      if (hs[k] == hs[i]) return set_err(GSV_E_INVALID_ARG, "handle %d is passed twice", i);
+    const gsvdec* h = hs[i];
+    if (h->mode != h0->mode || h->in_ch != h0->in_ch || h->gin != h0->gin || h->hop != h0->hop ||
+        h->C0 != h0->C0 || h->stages.size() != h0->stages.size() || h->has_cond != h0->has_cond)
+      return set_err(GSV_E_INVALID_ARG, "handle %d holds a different model or mode than handle 0", i);
+  }
+  if ((int64_t)B * max_act_elems(h0, T0) > (int64_t)1 << 40) return set_err(GSV_E_INVALID_ARG, "request too large");
+  for (int i = 0; i < n; ++i) GSV_TRY(take_async_error(hs[i]));
+  DeviceGuard guard;
+  MultiCall c;
+  c.z = z;
+  c.g = g;
+  c.len_user = lengths;
+  c.B = B;
+  c.T0 = T0;
+  c.in_ch = h0->in_ch;
+  c.gin = h0->gin;
+  c.hop = h0->hop;
+  c.mem_kind = mem_kind;
+  c.dev0 = h0->device;
+  c.wav = wav;
+  c.ev_in = nullptr;
+  c.len.assign(B, T0);
+  CUDA_TRY(cudaSetDevice(c.dev0));
+  if (lengths) {
+    if (mem_kind == GSV_MEM_HOST) {
+      std::copy(lengths, lengths + B, c.len.begin());
+    } else {  // the plan needs them on the host: wait for the caller's stream
+      CUDA_TRY(cudaMemcpyAsync(c.len.data(), lengths, sizeof(int) * B, cudaMemcpyDeviceToHost, st));
+      CUDA_TRY(cudaStreamSynchronize(st));
+    }
+    for (int b = 0; b < B; ++b)
+      if (c.len[b] < 0 || c.len[b] > T0)
+        return set_err(GSV_E_INVALID_ARG, "lengths[%d] = %d outside [0, %d]", b, c.len[b], T0);
+  }
+  // Plan.
+  std::vector<std::vector<MultiJob>> jobs(n);
+  c.chunked = B == 1 && n > 1 && c.len[0] > 0;
+  if (c.chunked) {
+    const int L = c.len[0];
+    const int base = L / n, extra = L % n;
+    for (int r = 0, b = 0; r < n; ++r) {
+      const int m = base + (r < extra ? 1 : 0);
+      if (m > 0) {
+        MultiJob j;
+        j.b = b;
+        j.e = b + m;
+        j.lo = std::max(0, b - kMultiChunkHalo);
+        j.hi = std::min(L, b + m + kMultiChunkHalo);
+        jobs[r].push_back(j);
+      }
+      b += m;
+    }
+  } else {
+    std::vector<int> ids;
+    for (int b = 0; b < B; ++b)
+      if (c.len[b] > 0) ids.push_back(b);
+    const auto share = plan_utterances(c.len, ids, n);
+    for (int r = 0; r < n; ++r)
+      for (auto& bk : plan_buckets(c.len, share[r])) {
+        MultiJob j;
+        j.T = 0;
+        for (int u : bk) j.T = std::max(j.T, c.len[u]);
+        j.idx = std::move(bk);
+        jobs[r].push_back(std::move(j));
+      }
+  }
+  if (mem_kind == GSV_MEM_DEVICE) {
+    if (!h0->mev_in) CUDA_TRY(cudaEventCreateWithFlags(&h0->mev_in, cudaEventDisableTiming));
+    CUDA_TRY(cudaEventRecord(h0->mev_in, st));
+    c.ev_in = h0->mev_in;
+  }
+  // Run: one host thread per busy worker (the caller's thread takes the first).
+  std::vector<int> rc(n, GSV_OK);
+  std::vector<std::string> msg(n);
+  auto work = [&](int r) {
+    rc[r] = mem_kind == GSV_MEM_DEVICE ? multi_worker_device(hs[r], jobs[r], c) : multi_worker_host(hs[r], jobs[r], c);
+    if (rc[r] != GSV_OK) msg[r] = g_last_error;
+  };
+  std::vector<std::thread> threads;
+  int first = -1;
+  for (int r = 0; r < n; ++r) {
+    if (jobs[r].empty()) continue;
+    if (first < 0) first = r;
+    else threads.emplace_back(work, r);
+  }
+  if (first >= 0) work(first);
+  for (auto& t : threads) t.join();
+  CUDA_TRY(cudaSetDevice(c.dev0));
+  for (int r = 0; r < n; ++r)
+    if (rc[r] != GSV_OK) return set_err(rc[r], "device %d (handle %d): %s", hs[r]->device, r, msg[r].c_str());
+  if (mem_kind == GSV_MEM_DEVICE) {
+    for (int r = 0; r < n; ++r)
+      if (!jobs[r].empty()) CUDA_TRY(cudaStreamWaitEvent(st, hs[r]->mev_done, 0));
+    // Samples past each utterance's length (and all of an empty one) are 0.
+    if (lengths) CUDA_TRY(launch_zero_tails(wav, lengths, B, T0, c.hop, st));
+  } else {
+    for (int b = 0; b < B; ++b) {
+      if (c.chunked || c.len[b] == 0) {
+        const size_t valid = (size_t)c.hop * c.len[b];
+        memset(wav + (size_t)b * c.hop * T0 + valid, 0, sizeof(float) * ((size_t)c.hop * T0 - valid));
+      }
+    }
+  }
+  return GSV_OK;
+}
+
+}  // namespace
+}  // namespace gsv
+
+extern "C" int gsvdec_forward_multi(gsvdec_t* const* handles, int n_handles, const float* z, const float* g,
+                                    const int32_t* lengths, int B, int T0, float* wav, int mem_kind,
+                                    void* stream) {
+  return gsv::multi_impl(handles, n_handles, z, g, lengths, B, T0, wav, mem_kind, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gsvdec_plan_multi(const int32_t* lengths, int B, int T0, int n_workers, int32_t* worker,
+                                 int32_t* bucket) {
+  if (!worker || !bucket || B <= 0 || T0 <= 0 || n_workers < 1 || n_workers > gsv::kMultiMaxHandles)
+    return gsv::set_err(GSV_E_INVALID_ARG, "bad arguments");
+  std::vector<int> len(B, T0);
+  if (lengths)
+    for (int b = 0; b < B; ++b) {
+      if (lengths[b] < 0 || lengths[b] > T0)
+        return gsv::set_err(GSV_E_INVALID_ARG, "lengths[%d] = %d outside [0, %d]", b, lengths[b], T0);
+      len[b] = lengths[b];
+    }
+  std::vector<int> ids;
+  for (int b = 0; b < B; ++b) {
+    worker[b] = -1;
+    bucket[b] = -1;
+    if (len[b] > 0) ids.push_back(b);
+  }
+  const auto share = gsv::plan_utterances(len, ids, n_workers);
+  for (int r = 0; r < n_workers; ++r) {
+    const auto bks = gsv::plan_buckets(len, share[r]);
+    for (int k = 0; k < (int)bks.size(); ++k)
+      for (int u : bks[k]) {
+        worker[u] = r;
+        bucket[u] = k;
+      }
+  }
+  return GSV_OK;
+}

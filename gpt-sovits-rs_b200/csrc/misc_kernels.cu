@@ -52,6 +52,20 @@ __global__ void cond_kernel(const float* __restrict__ g, const float* __restrict
   if (lane == 0) out[(size_t)b * C + c] = s + (bc ? bc[c] : 0.0f);
 }
 
+// wav [B][row]: samples [hop * len[b], row) of utterance b set to 0 (the
+// tails past each utterance's own length in a multi-device decode).
+__global__ void zero_tails_kernel(float* __restrict__ wav, const int* __restrict__ len, long long row,
+                                  int hop, int T0) {
+  pdl_wait();
+  const int b = blockIdx.y;
+  int l = len[b];
+  l = l < 0 ? 0 : (l > T0 ? T0 : l);
+  float* w = wav + (size_t)b * row;
+  for (long long i = (long long)l * hop + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < row;
+       i += (long long)gridDim.x * blockDim.x)
+    w[i] = 0.0f;
+}
+
 struct StageLen {
   int mul[16];
   int add[16];
@@ -322,6 +336,18 @@ cudaError_t launch_lengths(const int* len_in, int B, int T0, const int* mul, con
   for (int s = 0; s < nstage; ++s) { sl.mul[s] = mul[s]; sl.add[s] = add[s]; }
   {
     const cudaError_t e_ = launch_k(lengths_kernel, cdiv(B, 128), 128, 0, st, len_in, B, T0, sl, nstage, lens);
+    if (e_ != cudaSuccess) return e_;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_zero_tails(float* wav, const int* len, int B, int T0, int hop, cudaStream_t st) {
+  if (B <= 0) return cudaSuccess;
+  if (B > 65535) return cudaErrorInvalidValue;
+  const long long row = (long long)T0 * hop;
+  const int gx = (int)std::min<long long>(cdiv((int)std::min<long long>(row, 1 << 30), 256), 64);
+  {
+    const cudaError_t e_ = launch_k(zero_tails_kernel, dim3(std::max(gx, 1), B), 256, 0, st, wav, len, row, hop, T0);
     if (e_ != cudaSuccess) return e_;
   }
   return cudaGetLastError();

@@ -91,12 +91,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 // (wake-up measured at about 120 cycles, and a sleeping warp takes no issue
 // slots).  Bounded by kFastWaitNs of wall time; abandoned as soon as another
 // role gave up.
-__device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity, volatile int* abort,
+                                               uint64_t limit_ns = kFastWaitNs) {
   if (mbar_try_nohint(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1; i != 0; ++i) {
     if (mbar_try_nohint(bar, parity)) return true;
-    if ((i & 15u) == 0 && (*abort || global_ns() - t0 > kFastWaitNs)) return false;
+    if ((i & 15u) == 0 && (*abort || global_ns() - t0 > limit_ns)) return false;
   }
   return false;
 }
@@ -191,9 +192,14 @@ __host__ __device__ constexpr uint32_t idesc_bf16() {
          ((uint32_t)(kM >> 4) << 24);
 }
 
+// The error word may live in mapped host memory (the handle's), so it is set
+// with a plain system-visible store: any non-zero code marks the call failed.
 __device__ __forceinline__ void raise_err(int* err, volatile int* abort, int code) {
   *abort = 1;
-  if (err) atomicExch(err, code);
+  if (err) {
+    *reinterpret_cast<volatile int*>(err) = code;
+    __threadfence_system();
+  }
 }
 
 __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {

@@ -137,12 +137,21 @@ def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray
     device tensors (lengths as an int32 device tensor) and returns a device
     waveform, the pieces are gathered over the process group as device
     tensors, and rank 0 gets device tensors back.
+
+    With host arrays and a CUDA `device`, `decode` also receives device
+    tensors: the rank's share of z / g is staged with ONE host-to-device copy
+    (pinned), its buckets run on the device with no host sync between them,
+    and rank 0 brings the gathered waveform back with ONE device-to-host copy
+    into a pinned buffer and returns numpy views of it.  The buffer is reused
+    by the next such call: copy the views to keep them past it.
     """
     import torch
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
     plan = plan_utterances(lengths, world)
     mine = plan[rank]
+    if not isinstance(z, torch.Tensor) and str(device).startswith("cuda"):
+        return _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets, plan)
     on_dev = isinstance(z, torch.Tensor)
     if mine:
         parts = {}
@@ -178,6 +187,70 @@ def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray
         for i in idx:
             n = int(lengths[i]) * hop
             out[i] = got[r][off:off + n]
+            off += n
+    return out
+
+
+_PINNED = {}
+
+
+def _pinned(n: int, dtype):
+    """A pinned host buffer of at least n elements, reused across calls (page
+    locking hundreds of MB per call would cost more than the copy)."""
+    import torch
+    key = str(dtype)
+    buf = _PINNED.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 1), dtype=dtype, pin_memory=True)
+        _PINNED[key] = buf
+    return buf[:n]
+
+
+def _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets, plan):
+    """decode_batch_sharded for host arrays on a CUDA device: one H2D of this
+    rank's share, device buckets, device gather, one D2H on rank 0."""
+    import torch
+    rank = dist.get_rank(group)
+    mine = plan[rank]
+    T0 = int(z.shape[2])
+    if mine:
+        zs = _pinned(len(mine) * z.shape[1] * T0, torch.float32).view(len(mine), z.shape[1], T0)
+        zs.numpy()[:] = z[mine]
+        zd = zs.to(device, non_blocking=True)
+        gd = None
+        if g is not None:
+            gs = _pinned(len(mine) * int(np.prod(g.shape[1:])), torch.float32).view(len(mine), *g.shape[1:])
+            gs.numpy()[:] = g[mine]
+            gd = gs.to(device, non_blocking=True)
+        local = [int(lengths[i]) for i in mine]
+        parts = {}
+        for bucket in plan_buckets(local, max_buckets):
+            lens = [local[k] for k in bucket]
+            T = max(lens)
+            it = torch.tensor(bucket, device=device)
+            zb = zd.index_select(0, it)[:, :, :T].contiguous()
+            gb = None if gd is None else gd.index_select(0, it).contiguous()
+            lb = torch.tensor(lens, dtype=torch.int32, device=device)
+            wav = decode(zb, gb, lb).reshape(len(bucket), T * hop)
+            for k, i in enumerate(bucket):
+                parts[mine[i]] = wav[k, : lens[k] * hop]
+        piece = torch.cat([parts[i] for i in mine])
+    else:
+        piece = torch.zeros(0, device=device)
+    maxlen = max(1, max(sum(int(lengths[i]) for i in p) for p in plan) * hop)
+    got = _gather_to_root(piece, int(piece.numel()), maxlen, dist, group, device, as_numpy=False)
+    if got is None:
+        return None
+    flat = torch.cat(got)
+    host = _pinned(flat.numel(), torch.float32)
+    host.copy_(flat)  # one device-to-host copy of every piece
+    arr = host.numpy()
+    out: List[Optional[np.ndarray]] = [None] * len(lengths)
+    off = 0
+    for idx in plan:
+        for i in idx:
+            n = int(lengths[i]) * hop
+            out[i] = arr[off:off + n]
             off += n
     return out
 

@@ -295,6 +295,76 @@ int gsvdec_forward_noalloc(gsvdec_t* h, const float* z, const float* g, const in
                            int B, int T0, float* wav, void* stream);
 int64_t gsvdec_noalloc_scratch_bytes(void);
 
+/* ---- Several devices ------------------------------------------------------
+ * Decoder::forward over several GPUs in one call: handles[i] is a handle
+ * created on device i of the job (the same checkpoint and mode on each; two
+ * handles on one device are allowed and run as two workers).  z, g, lengths
+ * and wav are as in gsvdec_forward; with GSV_MEM_DEVICE they live on
+ * handles[0]'s device and `stream` is a stream of that device.
+ *   B > 1 (or one handle): utterances are split over the handles
+ *     (longest-processing-time balance of the frame counts), each handle
+ *     decoding its share in up to 8 length-bucketed masked batches
+ *     (gsvdec_plan_multi shows the plan);
+ *   B == 1: the utterance is split into contiguous frame ranges, one per
+ *     handle, each decoded with 16 input frames recomputed on both sides.
+ * Either way every utterance's samples equal those of gsvdec_forward on it
+ * alone (with its own length), and samples past hop*lengths[b] are 0.
+ * Each handle works on its own stream from its own host thread; inputs reach
+ * a device, and waveform pieces reach handles[0]'s device (or the host), by
+ * copy-engine copies -- no kernel reads another device's memory.
+ * GSV_MEM_HOST: the call returns when wav is complete.  GSV_MEM_DEVICE: the
+ * work starts after the work already queued on `stream` and wav is complete
+ * in `stream` order when the call returns (the call itself waits for
+ * `stream` only when lengths are given, to plan with them on the host).  A
+ * device wait that gives up in a stream-async call is reported by
+ * gsvdec_sync_status or the next call on the handle concerned.
+ * Calls on one handle must not overlap, as for every other call.  No
+ * reference counterpart: the reference decodes on one device
+ * (src/config/mod.rs:68-80; SoVITSModel::synthesize_with_speed_and_sv,
+ * src/models/sovits.rs:400, calls Decoder::forward once per utterance). */
+int gsvdec_forward_multi(gsvdec_t* const* handles, int n_handles, const float* z, const float* g,
+                         const int32_t* lengths, int B, int T0, float* wav, int mem_kind, void* stream);
+
+/* The utterance plan gsvdec_forward_multi uses for B > 1 on n_workers
+ * handles: worker[b] and bucket[b] (index of utterance b's batch on its
+ * worker, batches by increasing length) for every utterance, -1 for an
+ * empty one (lengths[b] == 0).  lengths may be NULL (all T0).  Host only. */
+int gsvdec_plan_multi(const int32_t* lengths, int B, int T0, int n_workers, int32_t* worker,
+                      int32_t* bucket);
+
+/* ---- Status of stream-async calls and failure hooks -----------------------
+ * Calls with GSV_MEM_DEVICE pointers (and gsvdec_forward_noalloc) return once
+ * their kernels are queued.  A bounded device wait that gives up inside them
+ * (after about 2 s without progress) stops its kernel and sets the handle's
+ * error word.  It is reported as GSV_E_TIMEOUT by the first of:
+ *   - gsvdec_sync_status(h, stream), which waits for `stream` and then
+ *     reads and clears the word;
+ *   - the next host-memory call on the handle (it syncs its stream);
+ *   - the entry of any later call on the handle, once the kernel has ended:
+ *     that call then returns GSV_E_TIMEOUT without doing anything else (the
+ *     word is cleared, so the call after it proceeds).
+ * No reference counterpart beyond its Result propagation (src/lib.rs:76-97). */
+int gsvdec_sync_status(gsvdec_t* h, void* stream);
+
+/* Self-test of the give-up path: queues on `stream` one kernel that runs the
+ * library's bounded device wait on a barrier nothing completes, limited to
+ * limit_ns (1e3..1e10).  The wait runs out and reports through the handle's
+ * error word like any decode kernel: gsvdec_sync_status then returns
+ * GSV_E_TIMEOUT and the handle keeps working.  Nothing else is in flight in
+ * that kernel when it gives up.  No reference counterpart. */
+int gsvdec_selftest_wait(gsvdec_t* h, int64_t limit_ns, void* stream);
+
+/* Allocation-failure hook (process-wide, for tests of the callers' error
+ * paths): with n >= 0 the next n device allocations of the library succeed
+ * and every one after them fails with GSV_E_OOM, until the hook is reset
+ * with n < 0 (the default).  A call that fails this way leaves its handle
+ * usable.  No reference counterpart. */
+int gsvdec_set_alloc_fail_after(int n);
+
+/* Device bytes the handle holds for per-call workspaces (decoder, single
+ * layer, flow, EncP), i.e. everything but its packed weights. */
+int gsvdec_workspace_bytes(const gsvdec_t* h, int64_t* bytes);
+
 /* Thread-local message describing the last error on this thread. */
 const char* gsvdec_last_error(void);
 

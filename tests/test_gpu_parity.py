@@ -334,3 +334,58 @@ def test_every_layer_in_isolation(gsv, sd_unit, mode):
             worst = max(worst, err)
             assert err <= BF16_LAYER_REL_L2, (name, err)
     dec.close()
+
+
+def test_bf16_cfg2_batch_against_oracle(gsv, sd_n001):
+    """The benchmark's own batch, 16 x 10 s in BF16 with N(0, 0.01) weights --
+    the sizes at which the persistent multi-tile walk, the two-window tiles and
+    the TMA-store epilogue run -- compared directly with the oracle decoding
+    utterances 0 and 15 alone: SNR >= 30 dB each."""
+    z, g = gsv.synth.make_inputs(16, 500)
+    dec = gsv.Decoder.load(sd_n001, device=0, mode="bf16")
+    try:
+        wav = dec.forward(z, g).reshape(16, -1)
+    finally:
+        dec.close()
+    for u in (0, 15):
+        ref = oracle.decoder_forward(sd_n001, z[u:u + 1], g[u:u + 1])
+        assert snr_db(wav[u], ref) >= BF16_SNR_DB, u
+
+
+def _distinct_layers():
+    """One conv per distinct shape at the per-layer-sweep sizes (10 s per
+    utterance): conv_pre, the 5 ConvTranspose, the 9 (k, d) ResBlock shapes of
+    each width (convs2 share the d = 1 shapes), conv_post."""
+    Ls = [500]
+    for s in (10, 8, 2, 2, 2):
+        Ls.append(Ls[-1] * s)
+    out = [("dec.conv_pre", 192, Ls[0])]
+    for i in range(5):
+        out.append((f"dec.ups.{i}", (512, 256, 128, 64, 32)[i], Ls[i]))
+        for r in range(3):
+            for j in range(3):
+                out.append((f"dec.resblocks.{3 * i + r}.convs1.{j}", (256, 128, 64, 32, 16)[i], Ls[i + 1]))
+    out.append(("dec.conv_post", 16, Ls[5]))
+    return out
+
+
+@pytest.mark.parametrize("mode", ["bf16", "fp32"])
+def test_every_layer_shape_at_sweep_sizes(gsv, sd_unit, mode):
+    """Each distinct conv shape at the sweep's 10 s lengths (B = 2), fed the
+    same fp32 input as the oracle: BF16 within the per-layer relative-L2 bar of
+    1e-2, FP32 within 1e-4 relative max error."""
+    dec = gsv.Decoder.load(sd_unit, device=0, mode=mode)
+    rng = np.random.default_rng(124)
+    try:
+        for name, cin, L in _distinct_layers():
+            x = rng.standard_normal((2, cin, L), dtype=np.float32)
+            y = dec.layer_forward(name, x)
+            ref = _layer_ref(sd_unit, name, x)
+            assert y.shape == ref.shape, name
+            if mode == "fp32":
+                assert rel_max(y, ref) <= FP32_REL, name
+            else:
+                err = rel_l2(y, ref)
+                assert err <= BF16_LAYER_REL_L2, (name, err)
+    finally:
+        dec.close()

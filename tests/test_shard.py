@@ -177,3 +177,27 @@ def test_long_utterance_chunked_over_two_gloo_ranks(gsv, tmp_path):
 def test_dead_rank_fails_fast(gsv, tmp_path):
     _run("dead", tmp_path)
     assert (tmp_path / "dead.txt").read_text().startswith("raised")
+
+
+def test_c_abi_plan_matches_python_planner(gsv):
+    """gsvdec_plan_multi (the C++ planner behind gsvdec_forward_multi) makes the
+    same utterance shares and length buckets as shard.plan_utterances /
+    shard.plan_buckets, and leaves empty utterances out."""
+    shard = gsv.shard
+    rng = np.random.default_rng(7)
+    for n, world in ((256, 8), (256, 1), (33, 4), (5, 8), (1, 1), (40, 3)):
+        lens = rng.integers(1, 1001, n).astype(np.int32)
+        worker, bucket = gsv.plan_multi(lens, world, T0=1000)
+        plan = shard.plan_utterances(lens, world)
+        for r, mine in enumerate(plan):
+            assert sorted(np.nonzero(worker == r)[0].tolist()) == mine
+            bks = shard.plan_buckets([int(lens[i]) for i in mine], 8, overhead=300)
+            for k, bk in enumerate(bks):
+                assert sorted(np.nonzero((worker == r) & (bucket == k))[0].tolist()) == [mine[i] for i in bk]
+            assert int((worker == r).sum()) == len(mine)
+    lens = np.array([5, 0, 7, 0], np.int32)
+    worker, bucket = gsv.plan_multi(lens, 2, T0=8)
+    assert worker[1] == -1 and worker[3] == -1 and bucket[1] == -1
+    assert set(worker[[0, 2]].tolist()) == {0, 1}
+    with pytest.raises(gsv.GsvDecError):
+        gsv.plan_multi(np.array([9], np.int32), 2, T0=8)  # longer than T0
