@@ -13,7 +13,19 @@ data path).
 
 value     audio-seconds per second, whole job, inputs resident in HBM.
 e2e       the same metric through the public C-ABI call with host buffers
-          (H2D of z/g and D2H of the waveform inside every timed step).
+          (H2D of z/g and D2H of the waveform inside every timed step):
+          gsvdec_forward with GSV_MEM_HOST_ASYNC on pinned buffers (one step's
+          copies overlap the neighbouring steps' decodes); e2e.blocking is the
+          blocking GSV_MEM_HOST call.
+extra keys, the other configs of the same job in the same run:
+          varlen256  256 utterances of 2-20 s, length-masked, sharded by
+                     utterance over the N ranks (strong scaling), with parity;
+          long60     one 60 s utterance in N halo time chunks (strong
+                     scaling), with parity;
+          fp32_cfg1  the fp32 CUDA-core mode on batch 1 x 5 s, with its
+                     roofline against the FP32 peak (rank 0).
+          With N > 1 the headline's waveforms are gathered to rank 0 over NCCL
+          inside the timed region too.
 roofline  the tap-GEMM conv launches: achieved = algorithmic FLOPs / average
           launch time (CUDA events around every launch on the forward's
           stream, over the timed region); layer_roofline adds the
@@ -911,25 +923,43 @@ def main():
     dec.set_stage_timing(0)
 
     # ---- end to end through the public call with host buffers (e2e) --------
+    # Every step copies its z / g in from pinned host memory and its waveform
+    # back out.  Headline: gsvdec_forward with GSV_MEM_HOST_ASYNC, the call a
+    # serving loop makes -- the copies of one step run while the steps next to
+    # it decode.  Also reported: the blocking GSV_MEM_HOST call, one step at a
+    # time (copy in, decode, copy out, stream sync).
     zh = torch.from_numpy(z).pin_memory()
     gh = torch.from_numpy(g).pin_memory()
     wh = torch.empty(B * T0 * hop, dtype=torch.float32).pin_memory()
     zn, gn, wn = zh.numpy(), gh.numpy(), wh.numpy()
-    for _ in range(args.warmup):
-        dec.forward(zn, gn, out=wn, stream=stream.cuda_stream)
-    barrier()
-    torch.cuda.synchronize()
-    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    h0.record(stream)
-    for _ in range(args.steps):
-        dec.forward(zn, gn, out=wn, stream=stream.cuda_stream)
-    h1.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    ms_e2e = max_over_ranks(h0.elapsed_time(h1))
+
+    def timed_host(call):
+        for _ in range(args.warmup):
+            call()
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for _ in range(args.steps):
+            call()
+        h1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(h0.elapsed_time(h1))
+
+    ms_e2e = timed_host(lambda: dec.forward_async(zh, gh, out=wh, stream=stream.cuda_stream))
+    dec.sync_status(stream.cuda_stream)
+    wav_async = wn.copy()
+    ms_block = timed_host(lambda: dec.forward(zn, gn, out=wn, stream=stream.cuda_stream))
+    assert np.array_equal(wav_async, wn), "overlapped and blocking host calls disagree"
     e2e = {"value": ws * secs_per_step * args.steps / (ms_e2e / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": int(zn.nbytes + gn.nbytes), "d2h_bytes_per_step": int(wn.nbytes),
-           "ms_per_step": ms_e2e / args.steps}
+           "ms_per_step": ms_e2e / args.steps,
+           "call": "gsvdec_forward(GSV_MEM_HOST_ASYNC) on pinned host buffers, one call per step",
+           "blocking": {"value": ws * secs_per_step * args.steps / (ms_block / 1e3),
+                        "ms_per_step": ms_block / args.steps,
+                        "call": "gsvdec_forward(GSV_MEM_HOST): copy in, decode, copy out, sync, per step"}}
 
     # ---- roofline of the dominant kernel + layer-weighted fraction ----------
     pk, pk_kind = peaks()

@@ -29,7 +29,7 @@ STATUS = {
     -5: "GSV_E_CUDA", -6: "GSV_E_OOM", -7: "GSV_E_UNSUPPORTED", -8: "GSV_E_TIMEOUT",
 }
 MODES = {"fp32": 0, "bf16": 1}
-MEM_HOST, MEM_DEVICE = 0, 1
+MEM_HOST, MEM_DEVICE, MEM_HOST_ASYNC = 0, 1, 2
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 
 # Every symbol include/gsvdec.h declares (checked by the CPU test suite).
@@ -266,6 +266,26 @@ class Decoder:
             None if g is None else ctypes.c_void_p(g.data_ptr()),
             None if lengths is None else ctypes.c_void_p(lengths.data_ptr()),
             B, T0, ctypes.c_void_p(out.data_ptr()), MEM_DEVICE, ctypes.c_void_p(st)))
+        return out
+
+    def forward_async(self, z, g=None, lengths=None, out=None, stream=None):
+        """Overlapped host-memory forward (GSV_MEM_HOST_ASYNC) on CPU tensors --
+        pinned for the copies to overlap: the copies in, the decode and the copy
+        out are queued and the call returns; ``out`` is complete once
+        ``stream`` (default: torch's current stream) has passed the call.
+        Consecutive calls overlap one call's copies with the next decode.  The
+        tensors must stay alive and untouched until then."""
+        import torch
+        B, _, T0 = z.shape
+        assert not z.is_cuda and z.dtype == torch.float32 and z.is_contiguous()
+        if out is None:
+            out = torch.empty(B * self.out_len(T0), dtype=torch.float32, pin_memory=True)
+        assert not out.is_cuda and out.numel() == B * self.out_len(T0) and out.is_contiguous()
+        if stream is None:
+            stream = torch.cuda.current_stream(self.info["device"]).cuda_stream
+        p = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        _check(library().gsvdec_forward(self._h, p(z), p(g), p(lengths), B, T0, p(out), MEM_HOST_ASYNC,
+                                        ctypes.c_void_p(stream)))
         return out
 
     def forward_noalloc(self, z, g=None, lengths=None, out=None, stream=None):

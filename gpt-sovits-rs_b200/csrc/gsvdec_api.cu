@@ -706,6 +706,24 @@ struct gsvdec {
   // and events, created on first use on the handle's device.
   cudaStream_t mstream = nullptr;
   cudaEvent_t mev_in = nullptr, mev_done = nullptr;
+  // Overlapped host-memory forward (GSV_MEM_HOST_ASYNC): input copies, decode
+  // and output copies on three streams, two staging slots used alternately so
+  // one call's copies overlap the neighbouring calls' decodes.
+  struct AsyncSlot {
+    float* z = nullptr;
+    float* g = nullptr;
+    int* len = nullptr;
+    float* wav = nullptr;
+    cudaEvent_t in_done = nullptr, comp_done = nullptr, out_done = nullptr;
+  };
+  AsyncSlot aslot[2];
+  cudaStream_t cs_in = nullptr, cs_comp = nullptr, cs_out = nullptr;
+  cudaEvent_t ev_join = nullptr;
+  void* aws = nullptr;  // both slots' staging
+  size_t aws_bytes = 0;
+  unsigned aseq = 0;
+  bool async_run = false;  // the last call using the decoder workspace was an overlapped one
+  cudaStream_t async_stream = nullptr;  // ... made with this stream
 };
 
 namespace gsv {
@@ -874,7 +892,7 @@ struct Workspace {
   float* tap;     // fp32 time-major tap scratch (debug taps only)
 };
 
-int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w) {
+int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_t drain = nullptr) {
   const size_t act = max_act_elems(h, T0) * (size_t)B;
   const size_t eb = act_bytes(h);
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
@@ -890,6 +908,7 @@ int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w) {
   size_t o_wav = need; need += al((size_t)B * L * 4);
   size_t o_tap = need; if (with_tap) need += al(act * 4);
   if (need > h->ws_bytes) {
+    if (drain) CUDA_TRY(cudaStreamSynchronize(drain));  // work in flight there may still use it
     if (h->ws) CUDA_TRY(cudaFree(h->ws));
     h->ws = nullptr;
     h->ws_bytes = 0;
@@ -1738,8 +1757,112 @@ void destroy_impl(gsvdec* h) {
   if (h->mstream) cudaStreamDestroy(h->mstream);
   if (h->mev_in) cudaEventDestroy(h->mev_in);
   if (h->mev_done) cudaEventDestroy(h->mev_done);
+  for (auto& sl : h->aslot)
+    for (cudaEvent_t e : {sl.in_done, sl.comp_done, sl.out_done})
+      if (e) cudaEventDestroy(e);
+  for (cudaStream_t x : {h->cs_in, h->cs_comp, h->cs_out})
+    if (x) cudaStreamDestroy(x);
+  if (h->ev_join) cudaEventDestroy(h->ev_join);
+  cudaFree(h->aws);
   cudaSetDevice(prev);
   delete h;
+}
+
+// A call that uses the decoder workspace from `st` after overlapped calls
+// (whose decodes run on cs_comp) is ordered after them.
+int join_async(gsvdec* h, cudaStream_t st) {
+  if (!h->async_run) return GSV_OK;
+  CUDA_TRY(cudaEventRecord(h->ev_join, h->cs_comp));
+  CUDA_TRY(cudaStreamWaitEvent(st, h->ev_join, 0));
+  h->async_run = false;
+  return GSV_OK;
+}
+
+// GSV_MEM_HOST_ASYNC: host z / g / lengths / wav, everything queued and the
+// call returns.  Call i uses staging slot i % 2:
+//   cs_in   waits until the slot's previous call is done with the slot (its
+//           output copy ended), then copies z / g / lengths in;
+//   cs_comp waits for those copies and until the slot's previous output copy
+//           has read its waveform staging, then decodes (the decoder
+//           workspace is only ever used from cs_comp, so decodes stay in
+//           order);
+//   cs_out  waits for the decode and copies the requested samples out;
+//   `st`    waits for that copy: the waveform is complete in `st` order.
+// The copies of call i thus run while calls i - 1 / i + 1 decode.
+int forward_host_async(gsvdec* h, const float* z, const float* g, const int32_t* lengths, int B, int Tsrc,
+                       int t_off, int T0, float* wav, cudaStream_t st, int64_t wav_skip, int64_t wav_count) {
+  for (cudaStream_t* x : {&h->cs_in, &h->cs_comp, &h->cs_out})
+    if (!*x) CUDA_TRY(cudaStreamCreateWithFlags(x, cudaStreamNonBlocking));
+  if (!h->ev_join) CUDA_TRY(cudaEventCreateWithFlags(&h->ev_join, cudaEventDisableTiming));
+  for (auto& sl : h->aslot)
+    for (cudaEvent_t* e : {&sl.in_done, &sl.comp_done, &sl.out_done})
+      if (!*e) CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+  const int L = out_len(h, T0);
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t nz = (size_t)B * h->in_ch * T0, ng = (size_t)B * std::max(h->gin, 1), nw = (size_t)B * L;
+  const size_t slot = al(nz * 4) + al(ng * 4) + al((size_t)B * 4) + al(nw * 4);
+  // Buffers are replaced only once nothing in flight uses them.
+  if (2 * slot > h->aws_bytes) {
+    for (cudaStream_t x : {h->cs_in, h->cs_comp, h->cs_out}) CUDA_TRY(cudaStreamSynchronize(x));
+    if (h->aws) CUDA_TRY(cudaFree(h->aws));
+    h->aws = nullptr;
+    h->aws_bytes = 0;
+    CUDA_TRY(dev_malloc(&h->aws, 2 * slot));
+    h->aws_bytes = 2 * slot;
+  }
+  // Slots keep a fixed stride (half the arena) whatever this call's sizes, so
+  // a call never writes into the other slot, whose call may be in flight.
+  const size_t stride = h->aws_bytes / 2 / 256 * 256;
+  for (int k = 0; k < 2; ++k) {
+    char* p = static_cast<char*>(h->aws) + k * stride;
+    gsvdec::AsyncSlot& sl = h->aslot[k];
+    sl.z = reinterpret_cast<float*>(p);
+    sl.g = reinterpret_cast<float*>(p + al(nz * 4));
+    sl.len = reinterpret_cast<int*>(p + al(nz * 4) + al(ng * 4));
+    sl.wav = reinterpret_cast<float*>(p + al(nz * 4) + al(ng * 4) + al((size_t)B * 4));
+  }
+  // The decoder workspace (replaced only after the decodes in flight end).
+  Workspace w;
+  GSV_TRY(ensure_ws(h, B, T0, false, w, h->cs_comp));
+  // Join the caller's stream when the workspace was last used from it.
+  if (!h->async_run || h->async_stream != st) {
+    CUDA_TRY(cudaEventRecord(h->ev_join, st));
+    CUDA_TRY(cudaStreamWaitEvent(h->cs_comp, h->ev_join, 0));
+    h->async_run = true;
+    h->async_stream = st;
+  }
+  gsvdec::AsyncSlot& sl = h->aslot[h->aseq++ % 2];
+  // inputs: the slot is free once its previous call's output copy is done
+  // (which follows that call's decode)
+  CUDA_TRY(cudaStreamWaitEvent(h->cs_in, sl.out_done, 0));
+  if (Tsrc == T0 && t_off == 0)
+    CUDA_TRY(cudaMemcpyAsync(sl.z, z, nz * 4, cudaMemcpyHostToDevice, h->cs_in));
+  else
+    CUDA_TRY(cudaMemcpy2DAsync(sl.z, sizeof(float) * T0, z + t_off, sizeof(float) * Tsrc, sizeof(float) * T0,
+                               (size_t)B * h->in_ch, cudaMemcpyHostToDevice, h->cs_in));
+  const float* gd = nullptr;
+  if (h->has_cond && g) {
+    CUDA_TRY(cudaMemcpyAsync(sl.g, g, sizeof(float) * (size_t)B * h->gin, cudaMemcpyHostToDevice, h->cs_in));
+    gd = sl.g;
+  }
+  const int* ld = nullptr;
+  if (lengths) {
+    CUDA_TRY(cudaMemcpyAsync(sl.len, lengths, sizeof(int) * (size_t)B, cudaMemcpyHostToDevice, h->cs_in));
+    ld = sl.len;
+  }
+  CUDA_TRY(cudaEventRecord(sl.in_done, h->cs_in));
+  // decode
+  CUDA_TRY(cudaStreamWaitEvent(h->cs_comp, sl.in_done, 0));
+  CUDA_TRY(cudaStreamWaitEvent(h->cs_comp, sl.out_done, 0));
+  GSV_TRY(forward_device(h, sl.z, T0, 0, gd, ld, B, T0, sl.wav, w, nullptr, h->cs_comp));
+  CUDA_TRY(cudaEventRecord(sl.comp_done, h->cs_comp));
+  // outputs
+  CUDA_TRY(cudaStreamWaitEvent(h->cs_out, sl.comp_done, 0));
+  CUDA_TRY(cudaMemcpyAsync(wav, sl.wav + wav_skip, sizeof(float) * (size_t)wav_count, cudaMemcpyDeviceToHost,
+                           h->cs_out));
+  CUDA_TRY(cudaEventRecord(sl.out_done, h->cs_out));
+  CUDA_TRY(cudaStreamWaitEvent(st, sl.out_done, 0));
+  return collect_timing(h, h->cs_comp);
 }
 
 int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengths, int B,
@@ -1748,12 +1871,15 @@ int forward_impl(gsvdec* h, const float* z, const float* g, const int32_t* lengt
   if (!h) return set_err(GSV_E_INVALID_ARG, "handle is NULL");
   if (!z || !wav) return set_err(GSV_E_INVALID_ARG, "z and wav must not be NULL");
   if (B <= 0 || T0 <= 0) return set_err(GSV_E_INVALID_ARG, "B=%d and T0=%d must be positive", B, T0);
-  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE)
+  if (mem_kind != GSV_MEM_HOST && mem_kind != GSV_MEM_DEVICE && !(mem_kind == GSV_MEM_HOST_ASYNC && !taps))
     return set_err(GSV_E_INVALID_ARG, "bad mem_kind %d", mem_kind);
   if ((int64_t)B * max_act_elems(h, T0) > (int64_t)1 << 40)
     return set_err(GSV_E_INVALID_ARG, "request too large");
   GSV_TRY(take_async_error(h));
   CUDA_TRY(cudaSetDevice(h->device));
+  if (mem_kind == GSV_MEM_HOST_ASYNC)
+    return forward_host_async(h, z, g, lengths, B, Tsrc, t_off, T0, wav, st, wav_skip, wav_count);
+  GSV_TRY(join_async(h, st));
   Workspace w;
   GSV_TRY(ensure_ws(h, B, T0, taps != nullptr, w));
   const int L = out_len(h, T0);
@@ -1923,6 +2049,7 @@ int flow_impl(gsvdec* h, const float* zp, const float* g, const int32_t* lengths
   const float* gdec = (h->has_cond && gd && h->gin == h->flow_gin) ? gd : nullptr;
   if (h->has_cond && gd && h->gin != h->flow_gin)
     return set_err(GSV_E_SHAPE, "flow cond width %d != decoder cond width %d", h->flow_gin, h->gin);
+  GSV_TRY(join_async(h, st));
   Workspace w;
   GSV_TRY(ensure_ws(h, B, T0, false, w));
   const int L = out_len(h, T0);
@@ -2714,6 +2841,7 @@ int multi_worker_device(gsvdec* h, const std::vector<MultiJob>& jobs, const Mult
   if (!h->mev_done) CUDA_TRY(cudaEventCreateWithFlags(&h->mev_done, cudaEventDisableTiming));
   const cudaStream_t s = h->mstream;
   CUDA_TRY(cudaStreamWaitEvent(s, c.ev_in, 0));
+  GSV_TRY(join_async(h, s));
   int maxB = 1, maxT = 1;
   for (const MultiJob& j : jobs) {
     maxB = std::max(maxB, c.chunked ? 1 : (int)j.idx.size());
@@ -2781,6 +2909,7 @@ int multi_worker_host(gsvdec* h, const std::vector<MultiJob>& jobs, const MultiC
   CUDA_TRY(cudaSetDevice(h->device));
   if (!h->mstream) CUDA_TRY(cudaStreamCreateWithFlags(&h->mstream, cudaStreamNonBlocking));
   const cudaStream_t s = h->mstream;
+  GSV_TRY(join_async(h, s));
   const bool cond = c.g && h->has_cond;
   const size_t C = c.in_ch;
   std::vector<float> zb, gb, ob;

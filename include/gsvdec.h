@@ -56,6 +56,17 @@ extern "C" {
 /* Where the z / g / lengths / wav pointers of a forward call live. */
 #define GSV_MEM_HOST 0    /* host memory; the call copies in and out and syncs the stream */
 #define GSV_MEM_DEVICE 1  /* device memory on the handle's device; the call is stream-async */
+/* Host memory, stream-async and overlapped (gsvdec_forward / _chunk only):
+ * the call queues the copy of z / g / lengths in, the decode and the copy of
+ * wav out on three internal streams of the handle and returns; wav is
+ * complete in `stream` order.  Consecutive calls alternate two staging
+ * slots, so one call's copies run while the calls next to it decode.  The
+ * host buffers must stay untouched (and wav unread) until `stream` has
+ * passed the call; pinned buffers are needed for the copies to overlap.
+ * The decode is ordered after earlier calls on this handle, not after other
+ * work queued on `stream`.  Errors of the device waits as for stream-async
+ * calls (gsvdec_sync_status). */
+#define GSV_MEM_HOST_ASYNC 2
 
 typedef struct gsvdec_tensor {
   const char* name;   /* safetensors key, e.g. "dec.ups.0.weight_v" */

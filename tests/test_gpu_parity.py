@@ -389,3 +389,30 @@ def test_every_layer_shape_at_sweep_sizes(gsv, sd_unit, mode):
                 assert err <= BF16_LAYER_REL_L2, (name, err)
     finally:
         dec.close()
+
+
+def test_host_async_calls_overlap_and_match(gsv, dec_bf16):
+    """GSV_MEM_HOST_ASYNC: several calls in flight on pinned host buffers
+    (alternating staging slots, different shapes and lengths) each give the
+    blocking host-memory forward's samples; a device-memory call queued after
+    them on the same stream sees their decodes finished."""
+    import torch
+    shapes = [(2, 12, None), (3, 12, [12, 5, 1]), (2, 12, None), (1, 30, None)]
+    ins, outs, want = [], [], []
+    for i, (B, T0, lens) in enumerate(shapes):
+        z, g = gsv.synth.make_inputs(B, T0, seed_z=501 + i, seed_g=601 + i)
+        zt = torch.from_numpy(z).pin_memory()
+        gt = torch.from_numpy(g).pin_memory()
+        lt = None if lens is None else torch.tensor(lens, dtype=torch.int32).pin_memory()
+        ins.append((zt, gt, lt))
+        outs.append(torch.full((B * T0 * dec_bf16.hop,), float("nan")).pin_memory())
+        want.append(dec_bf16.forward(z, g, lengths=lens))
+    for (zt, gt, lt), o in zip(ins, outs):
+        dec_bf16.forward_async(zt, gt, lt, out=o)
+    zd = ins[0][0].cuda()
+    gd = ins[0][1].cuda()
+    dev = dec_bf16.forward_device(zd, gd)
+    dec_bf16.sync_status()
+    for o, w in zip(outs, want):
+        assert np.array_equal(o.numpy(), w)
+    assert np.array_equal(dev.cpu().numpy(), want[0])
