@@ -98,26 +98,34 @@ def halo_window(begin: int, end: int, T0: int, halo: int) -> Tuple[int, int]:
     return max(0, begin - halo), min(T0, end + halo)
 
 
-def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device, as_numpy: bool = True):
+def _gather_to_root(piece, n_valid: int, maxlen: int, dist, group, device, as_numpy: bool = True,
+                    sizes: Optional[Sequence[int]] = None):
     """Gather variable-length 1-D float32 pieces to rank 0 (zero-padded to
     `maxlen`); returns the list of trimmed pieces on rank 0 (numpy, or device
-    tensors with as_numpy=False), else None."""
+    tensors with as_numpy=False), else None.  `sizes` (every rank's n_valid,
+    known to all ranks from the plan) spares the size exchange: then the only
+    collective is the gather itself and nothing waits on the host."""
     import torch
     rank = dist.get_rank(group)
     world = dist.get_world_size(group)
-    buf = torch.zeros(maxlen, dtype=torch.float32, device=device)
-    if n_valid:
-        buf[:n_valid] = piece[:n_valid]
-    sizes = torch.tensor([n_valid], dtype=torch.int64, device=device)
-    all_sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
-    dist.all_gather(all_sizes, sizes, group=group)
-    gl = [torch.zeros(maxlen, dtype=torch.float32, device=device) for _ in range(world)] if rank == 0 else None
+    if n_valid == maxlen and piece.numel() == maxlen:
+        buf = piece.contiguous()
+    else:
+        buf = torch.zeros(maxlen, dtype=torch.float32, device=device)
+        if n_valid:
+            buf[:n_valid] = piece[:n_valid]
+    if sizes is None:
+        mine = torch.tensor([n_valid], dtype=torch.int64, device=device)
+        all_sizes = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
+        dist.all_gather(all_sizes, mine, group=group)
+        sizes = [int(t.item()) for t in all_sizes]
+    gl = [torch.empty(maxlen, dtype=torch.float32, device=device) for _ in range(world)] if rank == 0 else None
     dist.gather(buf, gather_list=gl, dst=0, group=group)
     if rank != 0:
         return None
     if not as_numpy:
-        return [gl[r][: int(all_sizes[r].item())] for r in range(world)]
-    return [gl[r][: int(all_sizes[r].item())].cpu().numpy() for r in range(world)]
+        return [gl[r][: int(sizes[r])] for r in range(world)]
+    return [gl[r][: int(sizes[r])].cpu().numpy() for r in range(world)]
 
 
 def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray],
@@ -174,11 +182,11 @@ def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray
         piece = torch.cat([parts[i] for i in mine]) if on_dev else np.concatenate([parts[i] for i in mine])
     else:
         piece = torch.zeros(0, device=z.device) if on_dev else np.zeros(0, np.float32)
-    maxlen = max(sum(int(lengths[i]) for i in p) for p in plan) * hop
-    maxlen = max(maxlen, 1)
+    sizes = [sum(int(lengths[i]) for i in p) * hop for p in plan]
+    maxlen = max(max(sizes), 1)
     n_valid = int(piece.numel()) if on_dev else piece.size
     src = piece if on_dev else torch.from_numpy(piece).to(device)
-    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev)
+    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev, sizes=sizes)
     if got is None:
         return None
     out: List[Optional[np.ndarray]] = [None] * len(lengths)
@@ -237,8 +245,9 @@ def _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets,
         piece = torch.cat([parts[i] for i in mine])
     else:
         piece = torch.zeros(0, device=device)
-    maxlen = max(1, max(sum(int(lengths[i]) for i in p) for p in plan) * hop)
-    got = _gather_to_root(piece, int(piece.numel()), maxlen, dist, group, device, as_numpy=False)
+    sizes = [sum(int(lengths[i]) for i in p) * hop for p in plan]
+    maxlen = max(1, max(sizes))
+    got = _gather_to_root(piece, int(piece.numel()), maxlen, dist, group, device, as_numpy=False, sizes=sizes)
     if got is None:
         return None
     flat = torch.cat(got)
@@ -273,10 +282,11 @@ def decode_long_chunked(decode_chunk: Callable, T0: int, hop: int, dist, group=N
     on_dev = isinstance(piece, torch.Tensor)
     if piece is None:
         piece = np.zeros(0, np.float32)
-    maxlen = max(1, max(ee - bb for bb, ee in chunks) * hop)
+    sizes = [(ee - bb) * hop for bb, ee in chunks]
+    maxlen = max(1, max(sizes))
     n_valid = int(piece.numel()) if on_dev else int(np.asarray(piece).size)
     src = piece if on_dev else torch.from_numpy(np.asarray(piece, np.float32)).to(device)
-    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev)
+    got = _gather_to_root(src, n_valid, maxlen, dist, group, device, as_numpy=not on_dev, sizes=sizes)
     if got is None:
         return None
     return torch.cat(got) if on_dev else np.concatenate(got)
