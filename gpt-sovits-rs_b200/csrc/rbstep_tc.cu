@@ -191,8 +191,13 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
       const uint32_t acc1 = tmem, acc2 = tmem + C;
       bool ok = mbar_wait(w_full, 0, abort);
       if (!ok) raise_err(err, abort, 12);
-      const uint32_t w1 = smem_u32(sW1), w2 = smem_u32(sW2), wi = smem_u32(sI);
-      const uint32_t ax = smem_u32(sAX), tb = smem_u32(sT);
+      // Descriptors built once and advanced by constant adds (address >> 4 in
+      // the descriptor's start field): the single issuing thread sets the pace
+      // of these short MMAs, so no per-MMA address arithmetic.
+      const uint64_t w1d = sdesc<C>(smem_u32(sW1)), w2d = sdesc<C>(smem_u32(sW2)), wid = sdesc<C>(smem_u32(sI));
+      const uint64_t axd = sdesc<C>(smem_u32(sAX)), tbd = sdesc<C>(smem_u32(sT));
+      constexpr uint64_t kRowD = S::kRow >> 4, kWD = S::kWPitch >> 4, kK = 2;
+      const uint64_t ax_step = (uint64_t)d * kRowD;
       uint32_t i = 0;
       for (int t = lc; t < ntiles && ok; t += ncta, ++i) {
         const uint32_t par = i & 1u;
@@ -202,13 +207,18 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
           break;
         }
         tc_fence_after();
-        uint32_t acc = 0;
-        for (int j = 0; j < k; ++j) {
-          const uint32_t a = ax + (uint32_t)(j * d) * S::kRow;
+        {
+          // conv1: k taps over row-shifted views (dilation d) of lrelu(window)
+          uint64_t ad = axd, bd = w1d;
+          mma_bf16_first(acc1, ad, bd, idesc);
 #pragma unroll
-          for (int kk = 0; kk < C / 16; ++kk) {
-            mma_bf16(acc1, sdesc<C>(a + kk * 32), sdesc<C>(w1 + j * S::kWPitch + kk * 32), idesc, acc);
-            acc = 1;
+          for (int kk = 1; kk < C / 16; ++kk) mma_bf16_acc(acc1, ad + kk * kK, bd + kk * kK, idesc);
+#pragma unroll 2
+          for (int j = 1; j < k; ++j) {
+            ad += ax_step;
+            bd += kWD;
+#pragma unroll
+            for (int kk = 0; kk < C / 16; ++kk) mma_bf16_acc(acc1, ad + kk * kK, bd + kk * kK, idesc);
           }
         }
         mma_commit(acc1_full);
@@ -218,20 +228,25 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
           break;
         }
         tc_fence_after();
-        acc = 0;
-        for (int j = 0; j < k; ++j) {
-          const uint32_t a = tb + (uint32_t)j * S::kRow;
+        {
+          // conv2: k taps over row-shifted views of t, then the residual as an
+          // identity MMA over the raw window
+          uint64_t ad = tbd, bd = w2d;
+          mma_bf16_first(acc2, ad, bd, idesc);
 #pragma unroll
-          for (int kk = 0; kk < C / 16; ++kk) {
-            mma_bf16(acc2, sdesc<C>(a + kk * 32), sdesc<C>(w2 + j * S::kWPitch + kk * 32), idesc, acc);
-            acc = 1;
+          for (int kk = 1; kk < C / 16; ++kk) mma_bf16_acc(acc2, ad + kk * kK, bd + kk * kK, idesc);
+#pragma unroll 2
+          for (int j = 1; j < k; ++j) {
+            ad += kRowD;
+            bd += kWD;
+#pragma unroll
+            for (int kk = 0; kk < C / 16; ++kk) mma_bf16_acc(acc2, ad + kk * kK, bd + kk * kK, idesc);
           }
         }
         const uint32_t s = i % kRbWindowStages;
-        const uint32_t xres = smem_u32(sX + s * P.a_stage) + (uint32_t)(h2 + h1) * S::kRow;
+        const uint64_t xd = sdesc<C>(smem_u32(sX + s * P.a_stage) + (uint32_t)(h2 + h1) * S::kRow);
 #pragma unroll
-        for (int kk = 0; kk < C / 16; ++kk)
-          mma_bf16(acc2, sdesc<C>(xres + kk * 32), sdesc<C>(wi + kk * 32), idesc, 1u);
+        for (int kk = 0; kk < C / 16; ++kk) mma_bf16_acc(acc2, xd + kk * kK, wid + kk * kK, idesc);
         mma_commit(x_empty + 8 * s);
         mma_commit(acc2_full);
       }

@@ -542,7 +542,17 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           continue;
         }
         const uint32_t d = tmem + buf * (MT * NT);
-        uint32_t accumulate = 0;
+        // The single issuing thread is the pace-setter of narrow tiles (a
+        // measured 45-64 cycles per MMA when the issue loop is straight-line
+        // code, several times that with per-MMA address and descriptor
+        // arithmetic): descriptors are built once per window / weight stage
+        // and advanced by constant adds (the 14-bit start-address field of a
+        // descriptor holds address >> 4, so byte offsets that keep the operand
+        // inside shared memory add as offset >> 4), and the first MMA of each
+        // window, which starts the accumulator, is issued on its own.
+        bool first = true;
+        constexpr uint64_t kK = 2;  // one 16-element K step = 32 bytes along the row
+        const uint64_t win_d = (uint64_t)(a_win >> 4);
         for (int s = 0; s < nseg && ok; ++s) {
           const SmSeg sg = ops[oi].seg[s];  // register copy
           for (int c0 = 0; c0 < sg.Cin && ok; c0 += CK) {
@@ -553,38 +563,43 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
               break;
             }
             tc_fence_after();
-            const uint32_t a_base = smem_u32(sA + st * a_stage) +
-                                    (uint32_t)(sg.off0 - sg.minoff) * (CK * 2);
-            const int row_step = sg.offstep * (CK * 2);
-            for (int j = 0; j < sg.ntaps; j += TPB) {
-              uint32_t b_base;
-              uint32_t sb = 0;
-              if (RES) {
-                b_base = smem_u32(sB + (size_t)(sg.wtap0 + j) * S::kBPitch);
-              } else {
-                sb = ib % SB;
+            uint64_t ad = sdesc<CK>(smem_u32(sA + st * a_stage) + (uint32_t)(sg.off0 - sg.minoff) * (CK * 2));
+            const uint64_t ad_step = (uint64_t)(int64_t)(sg.offstep * (CK * 2 / 16));  // one tap: offstep rows
+            // All K steps of one tap: window row shift in `ad`, weights in `bt`.
+            auto tap_mmas = [&](uint64_t bt) {
+#pragma unroll
+              for (int kk = 0; kk < CK / 16; ++kk) {
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                  if (kk == 0 && first)
+                    mma_bf16_first(d + m * NT, ad + m * win_d, bt, idesc);
+                  else
+                    mma_bf16_acc(d + m * NT, ad + m * win_d + kk * kK, bt + kk * kK, idesc);
+                }
+                first = false;
+              }
+              ad += ad_step;
+            };
+            if (RES) {
+              uint64_t bd = sdesc<CK>(smem_u32(sB + (size_t)sg.wtap0 * S::kBPitch));
+#pragma unroll 2
+              for (int j = 0; j < sg.ntaps; ++j) {
+                tap_mmas(bd);
+                bd += S::kBPitch >> 4;
+              }
+            } else {
+              for (int j = 0; j < sg.ntaps; j += TPB) {
+                const uint32_t sb = ib % SB;
                 if (!mbar_wait_fast(b_full + 8 * sb, (ib / SB) & 1u, abort)) {
                   raise_err(err, abort, 6);
                   ok = false;
                   break;
                 }
                 tc_fence_after();
-                b_base = smem_u32(sB + sb * TPB * S::kBPitch);
-              }
-              const int nt = min(TPB, sg.ntaps - j);
-              for (int t = 0; t < nt; ++t) {
-                const uint32_t a_tap = a_base + (uint32_t)((j + t) * row_step);
-                const uint32_t b_tap = b_base + (uint32_t)t * S::kBPitch;
+                const uint64_t bd = sdesc<CK>(smem_u32(sB + sb * TPB * S::kBPitch));
 #pragma unroll
-                for (int kk = 0; kk < CK / 16; ++kk) {
-#pragma unroll
-                  for (int m = 0; m < MT; ++m)
-                    mma_bf16(d + m * NT, sdesc<CK>(a_tap + m * a_win + kk * 32), sdesc<CK>(b_tap + kk * 32),
-                             idesc, accumulate);
-                  accumulate = 1;
-                }
-              }
-              if (!RES) {
+                for (int t = 0; t < TPB; ++t)
+                  if (t == 0 || j + t < sg.ntaps) tap_mmas(bd + (uint64_t)t * (S::kBPitch >> 4));
                 mma_commit(b_empty + 8 * sb);
                 ++ib;
               }

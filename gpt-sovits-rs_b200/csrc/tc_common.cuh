@@ -154,6 +154,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+// The same MMA with the accumulate flag fixed: D = A.B (starts an
+// accumulator) and D += A.B.  No predicate to compute per MMA.
+__device__ __forceinline__ void mma_bf16_first(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;" ::"r"(tmem), "l"(adesc), "l"(bdesc),
+               "r"(idesc));
+}
+__device__ __forceinline__ void mma_bf16_acc(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(tmem), "l"(adesc), "l"(bdesc),
+               "r"(idesc));
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)
