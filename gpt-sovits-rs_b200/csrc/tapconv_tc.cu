@@ -348,7 +348,7 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE, int MT>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
   using S = TcShape<CK, NT, NBUF, STG, MT>;
-  static_assert(MT == 1 || (MT == 2 && !GATE), "two-window tiles: plain and staged epilogues only");
+  static_assert(MT == 1 || ((MT == 2 || MT == 4) && !GATE), "multi-window tiles: plain and staged epilogues only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t a_win = (uint32_t)P.a_stage_bytes;  // one 128-row window (+ halo), 1024-aligned
@@ -935,14 +935,16 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   }
   // With staging the deeper rings (SA, SB) are kept when `per_sm` CTAs still
   // fit next to the 16 KB of staging, else they shrink to (SA2, SB2).
-  // Two-window tiles (MT = 2) halve the per-tile hand-offs where those bound
-  // the launch (measured per op kind on B200): every narrow op except the
-  // 16-channel branch sum, which is bound by its epilogue and keeps one
-  // window with more CTAs per SM; at 64 channels only the branch sum, whose
-  // long MMA chains outweigh the lost second CTA per SM.
+  // Multi-window tiles (MT = 2, 4) divide the per-tile hand-offs where those
+  // bound the launch (measured per op kind on B200): four windows for the
+  // 16-channel convs (rb4 step-2 conv1 0.336 -> 0.274 ms against two), two for
+  // the 32-channel ones, every narrow op except the 16-channel branch sum,
+  // which is bound by its epilogue and keeps one window with more CTAs per
+  // SM; at 64 channels the branch sum, whose long MMA chains outweigh the lost
+  // second CTA per SM, and the single-output convs where two CTAs still fit.
   if (ck == 16 && nt == 16 && P.n_tiles == 1)
     return branch_sum ? launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st)
-                      : launch_cfg<16, 16, true, 6, 1, 4, 0, false, 2>(P, st);
+                      : launch_cfg<16, 16, true, 3, 1, 4, 0, false, 4>(P, st);
   if (ck == 32 && nt == 32 && P.n_tiles == 1)
     return branch_sum ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
                       : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
@@ -956,6 +958,11 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     // CTAs per SM: the 64-column MMAs are short, and with two stages the MMA
     // warp waited on weight loads (measured: 64-channel conv1 / conv2 launches
     // 4-8 % faster).  The dilation-5 windows leave no room for it.
+    // Single-output convs: two-window tiles (one weight stage serves 256 rows)
+    // where two CTAs per SM still fit (measured on B200: the dilation-1
+    // conv1 0.321 -> 0.297 ms; the wider windows of dilations 3 / 5 do not
+    // fit and keep one window).
+    if (stg == 0 && cfg_fits<64, 64, false, 2, 2, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, 0, false, 2>(P, st);
     const bool deep = stg == 0 ? cfg_fits<64, 64, false, 2, 4, 4, 0>(P, 2) : cfg_fits<64, 64, false, 2, 3, 4, 2>(P, 2);
     return deep ? launch_staged<64, 64, false, 2, 4, 2, 3, 4>(P, stg, 2, st)
                 : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
