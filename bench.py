@@ -26,9 +26,10 @@ extra keys, the other configs of the same job in the same run:
                      roofline against the FP32 peak (rank 0).
           With N > 1 the headline's waveforms are gathered to rank 0 over NCCL
           inside the timed region too.
-roofline  the tap-GEMM conv launches: achieved = algorithmic FLOPs / average
-          launch time (CUDA events around every launch on the forward's
-          stream, over the timed region); layer_roofline adds the
+roofline  the dominant kernel (the 128-channel single-output tap GEMM):
+          achieved = algorithmic FLOPs / launch time (CUDA events around
+          every launch on the forward's stream); traffic from a single-launch
+          ncu capture; layer_roofline adds the
           layer-weighted fraction sum(t_roof) / sum(t_measured), t_roof =
           max(FLOPs / tensor peak, bytes / HBM peak) per conv; roofline_by_bound
           splits the same launches into compute-bound (TF/s against the tensor
@@ -972,21 +973,36 @@ def main():
     else:
         peak = FP32_CORE_TFLOPS
         bound = "fp32-core"
-    achieved = f_conv / t_conv / 1e12 if t_conv > 0 else None
+    achieved_all = f_conv / t_conv / 1e12 if t_conv > 0 else None
+    # The dominant kernel: the 128-channel single-output tap GEMM (rb1's three
+    # conv1 groups and its branch sum; tapconv_tc_kernel<64, 128, ...> with
+    # plain stores, the largest share of the forward in the ncu launch list).
+    # achieved = their algorithmic FLOPs / their CUDA-event time; traffic =
+    # DRAM bytes of one such launch from a single-launch ncu capture.
+    dom_names = ("rb1.step0.conv1", "rb1.step1.conv1", "rb1.step2.conv1", "rb1.final")
+    dom = [s for s in conv if s["name"] in dom_names]
+    f_dom = sum(s["flops"] for s in dom)
+    t_dom = sum(s["ms"] for s in dom) / 1e3
+    achieved = f_dom / t_dom / 1e12 if t_dom > 0 else None
     traffic = None
-    prof = ROOT / "profiles" / f"tapgemm_{args.mode}_B16x10s_traffic.json"
-    if prof.exists():
+    prof = ROOT / "profiles" / "tapconv_tc_64x128_rb1_conv1_traffic.json"
+    if args.mode == "bf16" and prof.exists():
         try:
-            traffic = json.loads(prof.read_text()).get("dram_bytes_per_step")
+            traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
         except (ValueError, OSError):
             traffic = None
     roof_s, meas_s, rows = layer_roofline(stats, args.mode, pk)
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if achieved else None, "traffic": traffic,
-                "kernel": "tap-GEMM conv launches of one forward (tapconv_tc + fused rbstep_tc: "
-                          "all 97 convs except conv_post)",
+                "traffic_unit": "DRAM bytes per launch (ncu, one rb1.step1.conv1 launch)",
+                "kernel": "tapconv_tc_kernel<64, 128, ...> single-output launches (rb1 conv1 groups and "
+                          "branch sum: 4 launches per forward, " + ", ".join(dom_names) + ")",
+                "launches_per_step": len(dom),
                 "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
-                                                 else "nominal fp32 CUDA-core")}
+                                                 else "nominal fp32 CUDA-core"),
+                "all_tap_gemm": {"achieved": achieved_all, "frac": achieved_all / peak if achieved_all else None,
+                                 "note": "every tap-GEMM launch (tapconv_tc + fused rbstep_tc), HBM-bound ones "
+                                         "included, against the tensor peak"}}
     by_bound = roofline_by_bound(stats, args.mode, pk)
     layer = {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
              "sum_meas_ms": 1e3 * meas_s, "hbm_gbs": pk["hbm_gbs"],
