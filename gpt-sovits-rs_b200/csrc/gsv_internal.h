@@ -69,6 +69,10 @@ struct TapConvGroup {
   TapConv op[kMaxGroup];
   int n;
   int* err;  // device error word set by a kernel whose bounded wait gave up (or null)
+  // FP32 CUDA-core kernel only: scratch for partial sums when a small launch
+  // is split over its input-channel chunks (null: never split).
+  float* partial;
+  long long partial_cap;  // floats available at `partial`
 };
 
 // Ceil-div helper usable on host and device.

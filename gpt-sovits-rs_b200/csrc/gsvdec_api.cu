@@ -652,6 +652,9 @@ struct gsvdec {
   // workspace
   void* ws = nullptr;
   size_t ws_bytes = 0;
+  // FP32 mode: split-K partial sums of the forward in flight (inside ws)
+  float* cur_part = nullptr;
+  long long cur_part_cap = 0;
   // stage timing (level 1) and per-launch profile (level 2)
   int timing = 0;
   cudaEvent_t ev[32] = {};
@@ -890,7 +893,13 @@ struct Workspace {
   int* lstage;
   float* wav;
   float* tap;     // fp32 time-major tap scratch (debug taps only)
+  float* part;    // FP32 mode: split-K partial sums of small launches (or null)
+  long long part_cap;
 };
+
+// Split-K scratch of the FP32 CUDA-core kernel: small launches (batch 1,
+// early stages) split their input-channel loop and reduce in order.
+constexpr long long kSplitScratchFloats = 1LL << 24;  // 64 MB
 
 int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_t drain = nullptr) {
   const size_t act = max_act_elems(h, T0) * (size_t)B;
@@ -907,6 +916,8 @@ int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_
   size_t o_ls = need; need += al((size_t)B * 4);
   size_t o_wav = need; need += al((size_t)B * L * 4);
   size_t o_tap = need; if (with_tap) need += al(act * 4);
+  const size_t part_floats = h->dt == Dt::F32 ? (size_t)kSplitScratchFloats : 0;
+  size_t o_part = need; need += al(part_floats * 4);
   if (need > h->ws_bytes) {
     if (drain) CUDA_TRY(cudaStreamSynchronize(drain));  // work in flight there may still use it
     if (h->ws) CUDA_TRY(cudaFree(h->ws));
@@ -925,6 +936,8 @@ int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_
   w.lstage = reinterpret_cast<int*>(p + o_ls);
   w.wav = reinterpret_cast<float*>(p + o_wav);
   w.tap = with_tap ? reinterpret_cast<float*>(p + o_tap) : nullptr;
+  w.part = part_floats ? reinterpret_cast<float*>(p + o_part) : nullptr;
+  w.part_cap = (long long)part_floats;
   return GSV_OK;
 }
 
@@ -1011,6 +1024,8 @@ constexpr int kIdentityResidualMinC = 32;
 int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& name,
               const Work& wk) {
   grp.err = h->d_err;
+  grp.partial = h->cur_part;
+  grp.partial_cap = h->cur_part_cap;
   cudaError_t e;
   if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
@@ -1075,6 +1090,18 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
                    const int* lens_in, int B, int T0, float* wav_dev, Workspace& w,
                    float* const* taps, cudaStream_t st) {
   PdlScope pdl((int64_t)B * T0 <= kPdlDecodeMaxFrames);
+  // This forward's split-K scratch (FP32 mode), for run_group, until it returns.
+  struct PartScope {
+    gsvdec* h;
+    PartScope(gsvdec* hh, float* p, long long cap) : h(hh) {
+      h->cur_part = p;
+      h->cur_part_cap = p ? cap : 0;
+    }
+    ~PartScope() {
+      h->cur_part = nullptr;
+      h->cur_part_cap = 0;
+    }
+  } part_scope(h, w.part, w.part_cap);
   h->launches = 0;
   h->n_ev = 0;
   if (h->timing >= 2) {
@@ -2667,6 +2694,14 @@ int carve_noalloc(const gsvdec* h, int B, int T0, char* base, size_t cap, Worksp
   for (int i = 0; i < 12; ++i) w.buf[i] = base + o_buf + i * al(act * eb);
   w.bias_bc = reinterpret_cast<float*>(base + o_bbc);
   w.lens = reinterpret_cast<int*>(base + o_len);
+  // FP32 mode: what is left of the array is the split-K scratch (the same
+  // split as gsvdec_forward's while it fits, so both give the same samples).
+  const size_t part_off = al(off);
+  const long long part_floats = h->dt == Dt::F32 && part_off < cap
+                                    ? std::min<long long>((long long)((cap - part_off) / 4), kSplitScratchFloats)
+                                    : 0;
+  w.part = part_floats ? reinterpret_cast<float*>(base + part_off) : nullptr;
+  w.part_cap = part_floats;
   return GSV_OK;
 }
 

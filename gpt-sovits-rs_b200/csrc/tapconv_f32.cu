@@ -11,6 +11,8 @@
 // RQ x RN register tile.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "gsv_epilogue.cuh"
 #include "gsv_kernels.h"
 #include "gsv_pdl.cuh"
@@ -22,6 +24,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kCK = 16;       // input channels per shared-memory chunk
 constexpr int kMaxSpan = 64;  // largest (ntaps - 1) * |offstep| supported
+constexpr int kMaxSplit = 8;  // largest split of one launch's K loop
+constexpr int kF32SmsHint = 148, kF32CtasPerSm = 3;  // a wave of this kernel on a B200
 
 // A CTA computes TQ x TN outputs; each thread an RQ x RN register tile (RQ
 // consecutive rows, RN consecutive columns).  Four columns per thread keep the
@@ -46,12 +50,26 @@ size_t f32_smem(int max_taps) {
   return sizeof(float) * ((size_t)kCK * Cfg<TN>::W + (size_t)max_taps * kCK * TN);
 }
 
+// Input-channel chunks of an op over all its segments (the K loop of one tile).
+__host__ __device__ inline int k_chunks(const TapConv& op) {
+  int nc = 0;
+  for (int s = 0; s < op.nseg; ++s) nc += cdiv(op.seg[s].Cin, kCK);
+  return nc;
+}
+
+// blockIdx.z = op * nsplit + split.  With nsplit > 1 a CTA accumulates only
+// the chunks [split * nc / nsplit, (split + 1) * nc / nsplit) of its tile and
+// stores the raw partial sums to grp.partial ([split][op][B][Q][N], `elems`
+// floats per (split, op)); f32_split_reduce adds the splits in order and runs
+// the epilogue.
 template <int TN>
-__global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_constant__ TapConvGroup grp) {
+__global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_constant__ TapConvGroup grp, int nsplit,
+                                                               long long elems) {
   pdl_wait();
   using C = Cfg<TN>;
   constexpr int RQ = C::RQ, RN = C::RN;
-  const TapConv& op = grp.op[blockIdx.z];
+  const int oi = blockIdx.z / nsplit, split = blockIdx.z - oi * nsplit;
+  const TapConv& op = grp.op[oi];
   const int b = blockIdx.x / op.row_tiles;
   if (b >= op.B) return;
   const int q0 = (blockIdx.x % op.row_tiles) * C::TQ;
@@ -68,6 +86,9 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
 #pragma unroll
     for (int j = 0; j < RN; ++j) acc[i][j] = 0.0f;
   const bool masked = op.len != nullptr && first_out_row(op, q0) >= op.len[b];
+  const int nc = k_chunks(op);
+  const int c_lo = (int)((long long)split * nc / nsplit), c_hi = (int)((long long)(split + 1) * nc / nsplit);
+  int ci = 0;  // running chunk index over (segment, chunk)
   if (!masked) {
     for (int s = 0; s < op.nseg; ++s) {
       const TapSeg& sg = op.seg[s];
@@ -76,7 +97,8 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
       const int last = sg.off0 + (sg.ntaps - 1) * sg.offstep;
       const int minoff = sg.offstep >= 0 ? sg.off0 : last;
       const int rows = C::TQ + (sg.ntaps - 1) * abs(sg.offstep);
-      for (int c0 = 0; c0 < sg.Cin; c0 += kCK) {
+      for (int c0 = 0; c0 < sg.Cin; c0 += kCK, ++ci) {
+        if (ci < c_lo || ci >= c_hi) continue;  // uniform over the CTA
         __syncthreads();
         for (int idx = tid; idx < rows * kCK; idx += kThreads) {
           const int r = idx / kCK, c = idx % kCK;
@@ -118,6 +140,20 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
       }
     }
   }
+  if (nsplit > 1) {
+    float* part = grp.partial + ((long long)split * grp.n + oi) * elems + (long long)b * op.Q * op.N;
+#pragma unroll
+    for (int i = 0; i < RQ; ++i) {
+      const int q = q0 + ty * RQ + i;
+      if (q >= op.Q) continue;
+#pragma unroll
+      for (int j = 0; j < RN; ++j) {
+        const int n = n0 + tx * RN + j;
+        if (n < op.N) part[(long long)q * op.N + n] = acc[i][j];
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < RQ; ++i) {
     const int q = q0 + ty * RQ + i;
@@ -127,6 +163,28 @@ __global__ void __launch_bounds__(kThreads) tapconv_f32_kernel(const __grid_cons
       const int n = n0 + tx * RN + j;
       if (n < op.N) epi_element<float>(op, b, q, n, acc[i][j]);
     }
+  }
+}
+
+// Sum of the splits of GEMM element (op, b, q, n), in split order, then the
+// fused epilogue.
+__global__ void __launch_bounds__(256) f32_split_reduce(const __grid_constant__ TapConvGroup grp, int nsplit,
+                                                        long long elems) {
+  pdl_wait();
+  const long long total = (long long)grp.n * elems;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int oi = (int)(i / elems);
+    const long long r = i - (long long)oi * elems;
+    const TapConv& op = grp.op[oi];
+    const long long qn = (long long)op.Q * op.N;
+    if (r >= (long long)op.B * qn) continue;
+    const int b = (int)(r / qn);
+    const int q = (int)((r - b * qn) / op.N);
+    const int n = (int)(r - b * qn - (long long)q * op.N);
+    float v = 0.0f;
+    for (int sp = 0; sp < nsplit; ++sp) v += grp.partial[((long long)sp * grp.n + oi) * elems + r];
+    epi_element<float>(op, b, q, n, v);
   }
 }
 
@@ -151,8 +209,30 @@ cudaError_t launch_tn(TapConvGroup g, cudaStream_t st) {
                                                (int)smem);
     if (e != cudaSuccess) return e;
   }
-  const cudaError_t e_ = launch_k(tapconv_f32_kernel<TN>, dim3(gx, gy, g.n), kThreads, smem, st, g);
+  // Small launches (short utterances, early stages) fill less than two waves
+  // of CTAs and run long tiles on a partly idle GPU: split their K loop over
+  // the input-channel chunks (partial sums, then an ordered reduction).
+  int nsplit = 1;
+  long long elems = 0;
+  int min_nc = 1 << 30;
+  for (int i = 0; i < g.n; ++i) {
+    elems = std::max(elems, (long long)g.op[i].B * g.op[i].Q * g.op[i].N);
+    min_nc = std::min(min_nc, k_chunks(g.op[i]));
+  }
+  const long long ctas = (long long)gx * gy * g.n, target = 2LL * kF32SmsHint * kF32CtasPerSm;
+  if (g.partial && ctas < target && min_nc >= 2) {
+    nsplit = (int)std::min<long long>({(target + ctas - 1) / ctas, (long long)kMaxSplit, (long long)min_nc});
+    while (nsplit > 1 && (long long)nsplit * g.n * elems > g.partial_cap) --nsplit;
+  }
+  const cudaError_t e_ = launch_k(tapconv_f32_kernel<TN>, dim3(gx, gy, g.n * nsplit), kThreads, smem, st, g, nsplit,
+                                  elems);
   if (e_ != cudaSuccess) return e_;
+  if (nsplit > 1) {
+    const long long total = (long long)g.n * elems;
+    const int blocks = (int)std::min<long long>((total + 255) / 256, 148LL * 8);
+    const cudaError_t e2 = launch_k(f32_split_reduce, blocks, 256, 0, st, g, nsplit, elems);
+    if (e2 != cudaSuccess) return e2;
+  }
   return cudaGetLastError();
 }
 

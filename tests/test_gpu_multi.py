@@ -4,7 +4,9 @@ Several handles -- one per GPU when the box has several, else several handles
 on device 0, which run as separate workers on separate streams -- must give
 every utterance the waveform of the single-handle forward on it alone: bit for
 bit in BF16 mode (the masked and the halo-chunked decodes are exact there),
-within 1e-6 relative in FP32 mode.  Samples past an utterance's length are 0.
+within 1e-5 relative in FP32 mode, whose small launches split their channel
+loop by launch size (so a batch and a lone utterance may round differently).
+Samples past an utterance's length are 0.
 """
 from __future__ import annotations
 
@@ -32,7 +34,7 @@ def sd(gsv):
 def _same(got, want, mode):
     if mode == "bf16":
         return np.array_equal(got, want)
-    return rel_max(got, want) <= 1e-6
+    return rel_max(got, want) <= 1e-5
 
 
 @pytest.mark.parametrize("mode", ["bf16", "fp32"])

@@ -117,7 +117,9 @@ def test_fp32_chunked_equals_whole(gsv, dec_fp32):
     parts = [dec_fp32.forward_chunk(z, g, a, b, halo=16) for a, b in ((0, 17), (17, 38), (38, 60))]
     chunked = np.concatenate(parts)
     assert chunked.shape == whole.shape
-    assert rel_max(chunked, whole) <= 1e-6
+    # FP32 launches this small split their channel loop by launch size, so the
+    # chunks and the whole utterance may round differently (BF16 is exact).
+    assert rel_max(chunked, whole) <= 1e-5
 
 
 def test_fp32_device_memory_path(gsv, dec_fp32):
