@@ -960,9 +960,11 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     // 4-8 % faster).  The dilation-5 windows leave no room for it.
     // Single-output convs: two-window tiles (one weight stage serves 256 rows)
     // where two CTAs per SM still fit (measured on B200: the dilation-1
-    // conv1 0.321 -> 0.297 ms; the wider windows of dilations 3 / 5 do not
-    // fit and keep one window).
+    // conv1 0.321 -> 0.297 ms), else -- the wider windows of dilations 3 / 5
+    // -- with a single window stage, the other CTA on the SM covering the
+    // next window's load (0.33 / 0.35 -> 0.30 ms, forward -1 % sustained).
     if (stg == 0 && cfg_fits<64, 64, false, 2, 2, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, 0, false, 2>(P, st);
+    if (stg == 0 && cfg_fits<64, 64, false, 1, 3, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, 0, false, 2>(P, st);
     const bool deep = stg == 0 ? cfg_fits<64, 64, false, 2, 4, 4, 0>(P, 2) : cfg_fits<64, 64, false, 2, 3, 4, 2>(P, 2);
     return deep ? launch_staged<64, 64, false, 2, 4, 2, 3, 4>(P, stg, 2, st)
                 : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
