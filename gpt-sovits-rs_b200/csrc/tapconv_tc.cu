@@ -965,6 +965,11 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
     // next window's load (0.33 / 0.35 -> 0.30 ms, forward -1 % sustained).
     if (stg == 0 && cfg_fits<64, 64, false, 2, 2, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, 0, false, 2>(P, st);
     if (stg == 0 && cfg_fits<64, 64, false, 1, 3, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, 0, false, 2>(P, st);
+    // The staged two-output convs (conv2) the same way, with three weight
+    // stages (0.417 / 0.431 -> 0.383 / 0.415 ms; two weight stages gained
+    // nothing).  The branch sum, tried the same way, went 0.31 -> 0.38 ms and
+    // keeps its configuration below.
+    if (stg == 2 && cfg_fits<64, 64, false, 1, 3, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, 2, false, 2>(P, st);
     const bool deep = stg == 0 ? cfg_fits<64, 64, false, 2, 4, 4, 0>(P, 2) : cfg_fits<64, 64, false, 2, 3, 4, 2>(P, 2);
     return deep ? launch_staged<64, 64, false, 2, 4, 2, 3, 4>(P, stg, 2, st)
                 : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
