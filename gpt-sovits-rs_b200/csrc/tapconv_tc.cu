@@ -98,6 +98,7 @@ struct EpiArgs {
   __nv_bfloat16* __restrict__ act;
   float slope, inv_div;
   bool has_div;
+  bool v8;  // both output bases 32-byte aligned: one 256-bit store per 16-column run
 };
 
 __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, int b) {
@@ -119,6 +120,7 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   a.slope = o.slope;
   a.has_div = o.div != 1.0f;
   a.inv_div = o.div;
+  a.v8 = ((reinterpret_cast<uintptr_t>(a.raw) | reinterpret_cast<uintptr_t>(a.act)) & 31) == 0;
   return a;
 }
 
@@ -179,14 +181,25 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
     }
   }
   const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
+  // e0 is a multiple of 16 elements (32 bytes): with 32-byte aligned bases a
+  // run is one full sector, written by one 256-bit store.
   if (a.raw) {
-    *reinterpret_cast<uint4*>(a.raw + e0) = u0;
-    *reinterpret_cast<uint4*>(a.raw + e0 + 8) = u1;
+    if (a.v8) {
+      st_global_v8(a.raw + e0, u0, u1);
+    } else {
+      *reinterpret_cast<uint4*>(a.raw + e0) = u0;
+      *reinterpret_cast<uint4*>(a.raw + e0 + 8) = u1;
+    }
   }
   if (a.act) {
     const __nv_bfloat162 s2 = __float2bfloat162_rn(a.slope);
-    *reinterpret_cast<uint4*>(a.act + e0) = lrelu_bf16x8(u0, s2);
-    *reinterpret_cast<uint4*>(a.act + e0 + 8) = lrelu_bf16x8(u1, s2);
+    const uint4 w0 = lrelu_bf16x8(u0, s2), w1 = lrelu_bf16x8(u1, s2);
+    if (a.v8) {
+      st_global_v8(a.act + e0, w0, w1);
+    } else {
+      *reinterpret_cast<uint4*>(a.act + e0) = w0;
+      *reinterpret_cast<uint4*>(a.act + e0 + 8) = w1;
+    }
   }
 }
 

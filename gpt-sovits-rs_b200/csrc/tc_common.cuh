@@ -221,6 +221,13 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = o;
 }
 
+// One 256-bit global store of two 16-byte halves (p 32-byte aligned; sm_100).
+__device__ __forceinline__ void st_global_v8(void* p, uint4 lo, uint4 hi) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x), "r"(lo.y),
+               "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+               : "memory");
+}
+
 // 8 floats -> 8 packed bf16 (round to nearest even).
 __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
   uint4 o;
