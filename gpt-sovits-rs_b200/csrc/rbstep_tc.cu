@@ -260,6 +260,7 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
     const uint32_t ax = smem_u32(sAX), tb = smem_u32(sT);
     const float slope = P.slope;
     const __nv_bfloat162 slope2 = __float2bfloat162_rn(slope);
+    const bool v8 = ((reinterpret_cast<uintptr_t>(op.out_raw) | reinterpret_cast<uintptr_t>(op.out_act)) & 31) == 0;
     const int L = P.L;
     bool ok = true;
     // a(i): lrelu of window i into the conv1 operand buffer (same swizzle).
@@ -333,13 +334,24 @@ __global__ void __launch_bounds__(kRbThreads, 1) rbstep_kernel(const __grid_cons
           for (int e = 0; e < 16; ++e) v[e] = dead ? 0.0f : v[e] + sb[C + c0 + e];
           const uint4 x0 = pack_bf16x8(v), x1 = pack_bf16x8(v + 8);
           if (store) {
+            // A 16-channel run is 32 bytes at a 32-byte offset: one 256-bit
+            // store where the output bases are 32-byte aligned.
             if (op.out_raw) {
-              *reinterpret_cast<uint4*>(op.out_raw + base + c0) = x0;
-              *reinterpret_cast<uint4*>(op.out_raw + base + c0 + 8) = x1;
+              if (v8) {
+                st_global_v8(op.out_raw + base + c0, x0, x1);
+              } else {
+                *reinterpret_cast<uint4*>(op.out_raw + base + c0) = x0;
+                *reinterpret_cast<uint4*>(op.out_raw + base + c0 + 8) = x1;
+              }
             }
             if (op.out_act) {
-              *reinterpret_cast<uint4*>(op.out_act + base + c0) = lrelu_bf16x8(x0, slope2);
-              *reinterpret_cast<uint4*>(op.out_act + base + c0 + 8) = lrelu_bf16x8(x1, slope2);
+              const uint4 a0 = lrelu_bf16x8(x0, slope2), a1 = lrelu_bf16x8(x1, slope2);
+              if (v8) {
+                st_global_v8(op.out_act + base + c0, a0, a1);
+              } else {
+                *reinterpret_cast<uint4*>(op.out_act + base + c0) = a0;
+                *reinterpret_cast<uint4*>(op.out_act + base + c0 + 8) = a1;
+              }
             }
           }
         }

@@ -98,7 +98,8 @@ struct EpiArgs {
   __nv_bfloat16* __restrict__ act;
   float slope, inv_div;
   bool has_div;
-  bool v8;  // both output bases 32-byte aligned: one 256-bit store per 16-column run
+  bool v8;   // both output bases 32-byte aligned: one 256-bit store per 16-column run
+  bool v8r;  // every residual base 32-byte aligned: one 256-bit load per run
 };
 
 __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, int b) {
@@ -121,6 +122,10 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   a.has_div = o.div != 1.0f;
   a.inv_div = o.div;
   a.v8 = ((reinterpret_cast<uintptr_t>(a.raw) | reinterpret_cast<uintptr_t>(a.act)) & 31) == 0;
+  uintptr_t ra = 0;
+#pragma unroll
+  for (int r = 0; r < kMaxRes; ++r) ra |= reinterpret_cast<uintptr_t>(a.res[r]);
+  a.v8r = (ra & 31) == 0;
   return a;
 }
 
@@ -163,9 +168,16 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
     for (int r = 0; r < kMaxRes; ++r) {  // residual runs: 16 contiguous bf16
       if (r >= a.nres) break;
       const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
+      uint4 ru[2];
+      if (a.v8r) {
+        ld_global_nc_v8(rp, ru[0], ru[1]);
+      } else {
+        ru[0] = __ldg(rp);
+        ru[1] = __ldg(rp + 1);
+      }
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
-        const uint4 u = __ldg(rp + k);
+        const uint4 u = ru[k];
         const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {

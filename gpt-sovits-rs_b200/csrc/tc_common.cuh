@@ -228,6 +228,13 @@ __device__ __forceinline__ void st_global_v8(void* p, uint4 lo, uint4 hi) {
                : "memory");
 }
 
+// One 256-bit read-only global load into two 16-byte halves (p 32-byte aligned).
+__device__ __forceinline__ void ld_global_nc_v8(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y), "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+
 // 8 floats -> 8 packed bf16 (round to nearest even).
 __device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
   uint4 o;
