@@ -18,8 +18,8 @@
 //              alternating accumulators between tiles so the epilogue of one
 //              tile overlaps the MMAs of the next.
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator, bias / cond /
-//              branch-average / LeakyReLU (gsv_epilogue.cuh), 16-byte bf16
-//              stores; then hand the accumulator back.
+//              branch-average / LeakyReLU (gsv_epilogue.cuh), one 256-bit
+//              bf16 store per 16-column run; then hand the accumulator back.
 // A ResBlock residual enters the MMA as one more segment with identity
 // weights (exact: bf16 x 1.0 accumulated in fp32), so the epilogue issues no
 // global loads.  Every mbarrier wait is bounded; a wait that gives up sets
@@ -34,10 +34,6 @@ namespace gsv {
 namespace {
 
 constexpr int kThreads = 192;
-// Epilogue output paths: plain 16-byte stores, or chunks staged in shared
-// memory and written by TMA tensor stores through a 3-D (Conv1d) or 4-D
-// (ConvTranspose: output row t = s * u + v) view of the output.
-constexpr int kOutPlain = 0, kOutConv = 1, kOutConvT = 2;
 constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
 
 struct alignas(64) TcParams {
@@ -54,12 +50,6 @@ struct alignas(64) TcParams {
   int w_tiles;                 // resident weight tiles
   int bias_off[kMaxGroup];     // each op's offset in the shared bias table
   int bias_floats;             // size of the shared bias table
-  // Output tensor maps for the TMA-store epilogue: [2 * op] raw, [2 * op + 1] act.
-  CUtensorMap mapOut[2 * kMaxGroup];
-  int out_mode[kMaxGroup];     // kOutPlain / kOutConv (C, L, B) / kOutConvT (C, s, L/s, B)
-  int out_scw[kMaxGroup];      // channels per staged chunk (16 or 32)
-  int out_s[kMaxGroup];        // ConvTranspose stride (phases per GEMM row)
-  int out_pad[kMaxGroup];      // ConvTranspose crop in output rows
   int len_smem;                // per-op valid lengths copied to shared memory (B ints each)
 };
 
@@ -72,8 +62,7 @@ struct SmSeg {
 };
 struct SmOp {
   int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
-  int nres, out_mode, scw, stride;
-  int pad, gate, bias_bc_ld, pad_;
+  int nres, gate, bias_bc_ld, pad_;
   const __nv_bfloat16* res[4];
   const int* len;
   const float* bias;
@@ -215,92 +204,7 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
   }
 }
 
-// Values of the 16 consecutive GEMM columns [n, n + 16) of row q (bias, cond,
-// residuals, division, row mask) computed in place in `v`; false when the run
-// falls outside the output (cropped ConvTranspose rows), which the TMA path
-// leaves to the tensor map's bounds.
-__device__ __forceinline__ bool epi16_values(const EpiArgs& a, int q, int n, float* v) {
-  const int e0 = q * a.N + n - a.crop;
-  if (e0 < 0 || e0 >= a.total) return false;
-  const int t = a.shift >= 0 ? e0 >> a.shift : e0 / a.Cout;
-  const int c = e0 - t * a.Cout;
-  if (t >= a.lim) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    return true;
-  }
-  const float4* bb = reinterpret_cast<const float4*>(a.bias + c);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float4 bv = bb[k];
-    v[4 * k + 0] += bv.x;
-    v[4 * k + 1] += bv.y;
-    v[4 * k + 2] += bv.z;
-    v[4 * k + 3] += bv.w;
-  }
-  if (a.bias_bc != nullptr) {
-    const float4* gb = reinterpret_cast<const float4*>(a.bias_bc + c);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float4 bv = __ldg(gb + k);
-      v[4 * k + 0] += bv.x;
-      v[4 * k + 1] += bv.y;
-      v[4 * k + 2] += bv.z;
-      v[4 * k + 3] += bv.w;
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kMaxRes; ++r) {
-    if (r >= a.nres) break;
-    const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      const uint4 u = __ldg(rp + k);
-      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __bfloat1622float2(h2[i]);
-        v[8 * k + 2 * i] = f.x + v[8 * k + 2 * i];
-        v[8 * k + 2 * i + 1] = f.y + v[8 * k + 2 * i + 1];
-      }
-    }
-  }
-  if (a.has_div) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
-  }
-  return true;
-}
-
-__device__ __forceinline__ void sts128(uint32_t addr, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
-
-// Byte address of 16-byte chunk h of staging row r (rows of 2 * scw bytes,
-// swizzled like the output map: SW64 for 32-channel rows, SW32 for 16).
-__device__ __forceinline__ uint32_t stage_addr(uint32_t base, int r, int h, int scw) {
-  const uint32_t a = base + (uint32_t)(r * scw * 2 + h * 16);
-  return a ^ (((a >> 7) & (scw == 32 ? 3u : 1u)) << 4);
-}
-
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2,
-                                             int c3) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-               : "memory");
-}
-
-template <int CK, int NT, int NBUF, int STG, int MT = 1>
+template <int CK, int NT, int NBUF, int MT = 1>
 struct TcShape {
   static constexpr uint32_t kBBytes = NT * CK * 2;
   static constexpr uint32_t kBPitch = (kBBytes + 1023) / 1024 * 1024;
@@ -308,11 +212,6 @@ struct TcShape {
   // stage, so narrow tiles (whose 4 MMAs per tap are short) load two taps at
   // a time.
   static constexpr int kTapsPerB = NT <= 64 ? 2 : 1;
-  // TMA-store staging: per epilogue warp, 32 rows x 32 channels bf16 for each
-  // of the STG staged outputs (raw and/or act).
-  static constexpr uint32_t kStageOut = 32 * 32 * 2;
-  static constexpr uint32_t kStageWarp = STG * kStageOut;
-  static constexpr uint32_t kStageBytes = 4 * kStageWarp;
   static constexpr int kCols = NBUF * MT * NT;  // NBUF accumulators of MT x NT fp32 columns
   static constexpr uint32_t kTmemCols =
       kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
@@ -367,13 +266,12 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 // are paid once per 256 rows -- the narrow layers' MMAs are too short to hide them);
 // SA: activation-window ring depth (stages of MT windows); SB: streamed weight ring depth (RES = false);
 // NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
-// STG: 1 or 2 outputs leave through shared-memory staging and TMA tensor
-// stores (0: plain stores); GATE: the ops are gated-activation ops (kept out
-// of the other instantiations, whose register budget it would raise).
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE, int MT>
+// GATE: the ops are gated-activation ops (kept out of the other
+// instantiations, whose register budget it would raise).
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE, int MT>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
-  using S = TcShape<CK, NT, NBUF, STG, MT>;
-  static_assert(MT == 1 || ((MT == 2 || MT == 4) && !GATE), "multi-window tiles: plain and staged epilogues only");
+  using S = TcShape<CK, NT, NBUF, MT>;
+  static_assert(MT == 1 || ((MT == 2 || MT == 4) && !GATE), "multi-window tiles: plain epilogue only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t a_win = (uint32_t)P.a_stage_bytes;  // one 128-row window (+ halo), 1024-aligned
@@ -382,8 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
   uint8_t* sB = smem + SA * a_stage;
   constexpr int TPB = RES ? 1 : S::kTapsPerB;
   const int nbt = RES ? P.w_tiles : SB * TPB;
-  uint8_t* sStage = sB + (size_t)nbt * S::kBPitch;  // 1024-byte aligned
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + S::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + (size_t)nbt * S::kBPitch);
   const uint32_t a_full = smem_u32(bars);
   const uint32_t a_empty = a_full + 8 * SA;
   const uint32_t b_full = a_empty + 8 * SA;
@@ -412,10 +309,6 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     o.crop = g.crop;
     o.cout_shift = (g.Cout & (g.Cout - 1)) == 0 ? __ffs(g.Cout) - 1 : -1;
     o.nres = g.nres;
-    o.out_mode = P.out_mode[threadIdx.x];
-    o.scw = P.out_scw[threadIdx.x];
-    o.stride = P.out_s[threadIdx.x];
-    o.pad = P.out_pad[threadIdx.x];
     o.gate = g.gate;
     o.bias_bc_ld = g.bias_bc_ld ? g.bias_bc_ld : g.Cout;
     for (int r = 0; r < kMaxRes; ++r)
@@ -641,9 +534,6 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int row = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t stg_raw = smem_u32(sStage) + (uint32_t)quarter * S::kStageWarp;
-    const uint32_t stg_act = STG == 2 ? stg_raw + S::kStageOut : stg_raw;  // one output: one buffer
-    bool pending = false;  // a TMA store of this warp may still be reading its staging
     uint32_t i = 0;
     for (TileWalker w(blockIdx.x, gridDim.x, n_tiles, nops, row_tiles); w.t < total; w.next(), ++i) {
       const int oi = w.oi, n0 = w.nt * NT, b = w.b;
@@ -656,7 +546,6 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       }
       tc_fence_after();
       const EpiArgs ea = epi_args(o, sbias, b);
-      const int mode = STG > 0 ? o.out_mode : kOutPlain, scw = STG > 0 ? o.scw : 16;
 #pragma unroll 1
       for (int m = 0; m < MT; ++m) {
         const int q0 = w.qt * kTileRows + m * kM;
@@ -695,75 +584,21 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
           continue;
         }
 #pragma unroll 1
-        for (int cc = 0; cc < NT; cc += scw) {
-          // Destination of this warp's chunk: rows q0 + 32 * quarter .. + 31,
-          // GEMM columns n0 + cc .. + scw - 1.
-          bool tma = mode != kOutPlain;
-          int oc = n0 + cc, ov = 0, ou = q0 + quarter * 32;
-          if (mode == kOutConvT) {
-            const int p = oc / o.Cout;  // phase: output row t = s * q - pad + p
-            oc -= p * o.Cout;
-            const int vv = p - o.pad;
-            const int du = vv >= 0 ? vv / o.stride : -((o.stride - 1 - vv) / o.stride);
-            ov = vv - du * o.stride;
-            ou += du;
-            tma = ou >= 0;  // a store never starts at a negative row: plain stores there
-          }
-          if (tma && pending) {
-            if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-            __syncwarp();
-            pending = false;
-          }
-#pragma unroll 1
-          for (int c0 = cc; c0 < cc + scw; c0 += 16) {
-            float v[16];
-            if (!masked) {
-              tmem_ld16(acc + (uint32_t)c0, v);
-            } else {
+        for (int c0 = 0; c0 < NT; c0 += 16) {
+          float v[16];
+          if (!masked) {
+            tmem_ld16(acc + (uint32_t)c0, v);
+          } else {
 #pragma unroll
-              for (int k = 0; k < 16; ++k) v[k] = 0.0f;
-            }
-            if (!tma) {
-              if (live) epi16(ea, q, n0 + c0, v);
-              continue;
-            }
-            // Rows outside the output are clipped by the tensor map.
-            epi16_values(ea, q, n0 + c0, v);
-            const int h = (c0 - cc) / 8;
-            const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
-            if (ea.raw) {
-              sts128(stage_addr(stg_raw, lane, h, scw), u0);
-              sts128(stage_addr(stg_raw, lane, h + 1, scw), u1);
-            }
-            if (ea.act) {
-              const __nv_bfloat162 s2 = __float2bfloat162_rn(ea.slope);
-              sts128(stage_addr(stg_act, lane, h, scw), lrelu_bf16x8(u0, s2));
-              sts128(stage_addr(stg_act, lane, h + 1, scw), lrelu_bf16x8(u1, s2));
-            }
+            for (int k = 0; k < 16; ++k) v[k] = 0.0f;
           }
-          if (tma) {
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              if (mode == kOutConv) {
-                if (ea.raw) tma_store_3d(&P.mapOut[2 * oi], stg_raw, oc, ou, b);
-                if (ea.act) tma_store_3d(&P.mapOut[2 * oi + 1], stg_act, oc, ou, b);
-              } else {
-                if (ea.raw) tma_store_4d(&P.mapOut[2 * oi], stg_raw, oc, ov, ou, b);
-                if (ea.act) tma_store_4d(&P.mapOut[2 * oi + 1], stg_act, oc, ov, ou, b);
-              }
-              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-            }
-            pending = true;
-          }
+          if (live) epi16(ea, q, n0 + c0, v);
         }
       }  // windows of the tile
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + 8 * buf);
     }
-    // Every TMA store of this warp has finished before the CTA exits.
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
   // This CTA's work is done: the next kernel's CTAs may be scheduled.
   pdl_trigger();
@@ -776,51 +611,28 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------------- host side
-// Output map of the TMA-store epilogue: box of scw channels x 32 rows, swizzled
-// like the staging rows.  Conv1d: (C, L, B).  ConvTranspose with stride s:
-// (C, s, L / s, B), so the rows of one phase of a GEMM row block are a box.
-bool encode_out(CUtensorMap* m, void* y, int mode, int B, int Lout, int Cout, int s, int scw) {
-  const CUtensorMapSwizzle sw = scw == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B;
-  if (mode == kOutConv) {
-    cuuint64_t dims[3] = {(cuuint64_t)Cout, (cuuint64_t)Lout, (cuuint64_t)B};
-    cuuint64_t strides[2] = {(cuuint64_t)Cout * 2, (cuuint64_t)Lout * Cout * 2};
-    cuuint32_t box[3] = {(cuuint32_t)scw, 32, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, y, dims, strides, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-  }
-  cuuint64_t dims[4] = {(cuuint64_t)Cout, (cuuint64_t)s, (cuuint64_t)(Lout / s), (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)Cout * 2, (cuuint64_t)s * Cout * 2, (cuuint64_t)Lout * Cout * 2};
-  cuuint32_t box[4] = {(cuuint32_t)scw, 1, 32, 1};
-  cuuint32_t es[4] = {1, 1, 1, 1};
-  return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, y, dims, strides, box, es,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, int MT = 1>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int MT = 1>
 size_t cfg_smem(const TcParams& P) {
-  using S = TcShape<CK, NT, NBUF, STG, MT>;
+  using S = TcShape<CK, NT, NBUF, MT>;
   const int nbt = RES ? P.w_tiles : SB * S::kTapsPerB;
-  return 1024 + (size_t)SA * MT * P.a_stage_bytes + (size_t)nbt * S::kBPitch + S::kStageBytes +
+  return 1024 + (size_t)SA * MT * P.a_stage_bytes + (size_t)nbt * S::kBPitch +
          8 * (2 * SA + 2 * SB + 2 * NBUF + 1) + 32 + sizeof(SmOp) * kMaxGroup +
          sizeof(float) * (size_t)P.bias_floats +
          (P.len_smem ? sizeof(int) * (size_t)kMaxGroup * P.grp.op[0].B : 0);
 }
 
 // True when `per_sm` CTAs of this configuration fit one SM's shared memory.
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, int MT = 1>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int MT = 1>
 bool cfg_fits(const TcParams& P, int per_sm) {
-  return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, STG, MT>(P) + 1024) <= (size_t)smem_per_sm();
+  return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, MT>(P) + 1024) <= (size_t)smem_per_sm();
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, int STG, bool GATE = false, int MT = 1>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE = false, int MT = 1>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
-  using S = TcShape<CK, NT, NBUF, STG, MT>;
-  const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, STG, MT>(P);
+  using S = TcShape<CK, NT, NBUF, MT>;
+  const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, MT>(P);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, STG, GATE, MT>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, GATE, MT>;
   // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
   // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
   int nregs = 0;
@@ -842,14 +654,6 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
     if (e_ != cudaSuccess) return e_;
   }
   return cudaGetLastError();
-}
-
-template <int CK, int NT, bool RES, int SA, int SB, int SA2, int SB2, int NBUF, int MT = 1>
-cudaError_t launch_staged(TcParams& P, int stg, int per_sm, cudaStream_t st) {
-  if (stg == 0) return launch_cfg<CK, NT, RES, SA, SB, NBUF, 0, false, MT>(P, st);
-  if (cfg_fits<CK, NT, RES, SA, SB, NBUF, 2, MT>(P, per_sm))
-    return launch_cfg<CK, NT, RES, SA, SB, NBUF, 2, false, MT>(P, st);
-  return launch_cfg<CK, NT, RES, SA2, SB2, NBUF, 2, false, MT>(P, st);
 }
 
 }  // namespace
@@ -905,49 +709,14 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   }
   P.bias_floats = boff;
   P.len_smem = g.op[0].B <= 1024;
-  for (int i = 0; i < g.n; ++i) {
-    const TapConv& op = P.grp.op[i];
-    P.out_mode[i] = kOutPlain;
-    P.out_scw[i] = op.Cout >= 32 ? 32 : 16;
-    P.out_s[i] = 1;
-    if (op.crop == 0 && op.N == op.Cout) {
-      P.out_mode[i] = kOutConv;
-    } else if (op.N % op.Cout == 0 && op.crop % op.Cout == 0 && op.Lout % (op.N / op.Cout) == 0) {
-      P.out_mode[i] = kOutConvT;
-      P.out_s[i] = op.N / op.Cout;
-      P.out_pad[i] = op.crop / op.Cout;
-    }
-    // Staged TMA stores pay off where a tile writes two outputs (raw and act)
-    // in rows of at least 64 bytes that a TMA box covers densely: Conv1d, and
-    // ConvTranspose of stride 2.  Elsewhere the plain 16-byte stores win.
-    // (Measured: one-output layers are slower staged -- the per-chunk wait for
-    // the staging buffer costs more than their plain stores.)
-    const bool dense = op.out_raw && op.out_act && op.Cout >= 32 &&
-                       (P.out_mode[i] == kOutConv || (P.out_mode[i] == kOutConvT && P.out_s[i] == 2));
-    if (!dense) P.out_mode[i] = kOutPlain;
-    if (P.out_mode[i] != kOutPlain) {
-      for (int k = 0; k < 2; ++k) {
-        void* out = k == 0 ? op.out_raw : op.out_act;
-        if (out && !encode_out(&P.mapOut[2 * i + k], out, P.out_mode[i], op.B, op.Lout, op.Cout, P.out_s[i],
-                               P.out_scw[i]))
-          P.out_mode[i] = kOutPlain;
-      }
-    }
-  }
   P.row_tiles = P.grp.op[0].row_tiles;
   P.n_tiles = g.op[0].N / nt;
   P.total_tiles = g.op[0].B * P.row_tiles * P.n_tiles * g.n;
   P.a_stage_bytes = (max_rows * ck * 2 + 1023) / 1024 * 1024;
   P.w_tiles = wtiles;
   if (P.total_tiles <= 0) return cudaSuccess;
-  // Narrow layers keep every weight tile of the launch resident in shared memory.
-  int stg = 0;  // outputs per tile staged for TMA stores (0: plain stores, else 2)
   bool gate = false;
-  for (int i = 0; i < g.n; ++i) {
-    if (P.out_mode[i] != kOutPlain)
-      stg = std::max(stg, (g.op[i].out_raw != nullptr) + (g.op[i].out_act != nullptr));
-    gate = gate || g.op[i].gate;
-  }
+  for (int i = 0; i < g.n; ++i) gate = gate || g.op[i].gate;
   // The three-branch sum (one GEMM over the branches' last convs, plus their
   // residuals as identity segments at >= 32 channels) has >= 3 segments.
   bool branch_sum = false;
@@ -955,49 +724,44 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   if (gate) {
     for (int i = 0; i < g.n; ++i)
       if (!g.op[i].gate) return cudaErrorInvalidValue;  // a group is all gated or none
-    if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, 0, true>(P, st);
+    if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, true>(P, st);
     return cudaErrorNotSupported;
   }
-  // With staging the deeper rings (SA, SB) are kept when `per_sm` CTAs still
-  // fit next to the 16 KB of staging, else they shrink to (SA2, SB2).
-  // Multi-window tiles (MT = 2, 4) divide the per-tile hand-offs where those
-  // bound the launch (measured per op kind on B200): four windows for the
-  // 16-channel convs (rb4 step-2 conv1 0.336 -> 0.274 ms against two), two for
-  // the 32-channel ones, every narrow op except the 16-channel branch sum,
-  // which is bound by its epilogue and keeps one window with more CTAs per
-  // SM; at 64 channels the branch sum, whose long MMA chains outweigh the lost
-  // second CTA per SM, and the single-output convs where two CTAs still fit.
+  // Narrow layers keep every weight tile of the launch resident in shared
+  // memory.  Multi-window tiles (MT = 2, 4) divide the per-tile hand-offs
+  // where those bound the launch (measured per op kind on B200): four windows
+  // for the 16-channel convs (rb4 step-2 conv1 0.336 -> 0.274 ms against two),
+  // two for the 32-channel ones, every narrow op except the 16-channel branch
+  // sum, which is bound by its epilogue and keeps one window with more CTAs
+  // per SM; at 64 channels the branch sum, whose long MMA chains outweigh the
+  // lost second CTA per SM, and the convs where two CTAs still fit.  Every
+  // epilogue writes with 256-bit stores: they beat the shared-memory staged
+  // TMA-store epilogue this kernel used to have for two-output layers (conv2
+  // 3-9 % at 64-256 channels, the stride-2 ConvTranspose 10 %).
   if (ck == 16 && nt == 16 && P.n_tiles == 1)
-    return branch_sum ? launch_cfg<16, 16, true, 6, 1, 4, 0>(P, st)
-                      : launch_cfg<16, 16, true, 3, 1, 4, 0, false, 4>(P, st);
+    return branch_sum ? launch_cfg<16, 16, true, 6, 1, 4>(P, st)
+                      : launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);
   if (ck == 32 && nt == 32 && P.n_tiles == 1)
-    return branch_sum ? launch_staged<32, 32, true, 3, 1, 2, 1, 4, 2>(P, stg, 2, st)
-                      : launch_staged<32, 32, true, 2, 1, 2, 1, 4, 2>(P, stg, 2, st);
-  // 256 columns (one CTA per SM): three window stages when nothing is staged
-  // (rb0 conv2 / branch sum 2-6 % faster than two).
-  if (ck == 64 && nt == 256) return launch_staged<64, 256, false, 3, 4, 2, 3, 2>(P, stg, 1, st);
-  if (ck == 64 && nt == 128) return launch_staged<64, 128, false, 2, 3, 2, 2, 2>(P, stg, 2, st);
+    return branch_sum ? launch_cfg<32, 32, true, 3, 1, 4, false, 2>(P, st)
+                      : launch_cfg<32, 32, true, 2, 1, 4, false, 2>(P, st);
+  // 256 columns (one CTA per SM): three window stages (rb0 conv2 / branch sum
+  // 2-6 % faster than two).
+  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 3, 4, 2>(P, st);
+  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2>(P, st);
   if (ck == 64 && nt == 64) {
-    if (branch_sum) return launch_staged<64, 64, false, 2, 2, 2, 2, 2, 2>(P, stg, 1, st);
-    // Four weight stages (eight taps in flight) where that still fits two
-    // CTAs per SM: the 64-column MMAs are short, and with two stages the MMA
-    // warp waited on weight loads (measured: 64-channel conv1 / conv2 launches
-    // 4-8 % faster).  The dilation-5 windows leave no room for it.
-    // Single-output convs: two-window tiles (one weight stage serves 256 rows)
-    // where two CTAs per SM still fit (measured on B200: the dilation-1
-    // conv1 0.321 -> 0.297 ms), else -- the wider windows of dilations 3 / 5
-    // -- with a single window stage, the other CTA on the SM covering the
-    // next window's load (0.33 / 0.35 -> 0.30 ms, forward -1 % sustained).
-    if (stg == 0 && cfg_fits<64, 64, false, 2, 2, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, 0, false, 2>(P, st);
-    if (stg == 0 && cfg_fits<64, 64, false, 1, 3, 2, 0, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, 0, false, 2>(P, st);
-    // The staged two-output convs (conv2) the same way, with three weight
-    // stages (0.417 / 0.431 -> 0.383 / 0.415 ms; two weight stages gained
-    // nothing).  The branch sum, tried the same way, went 0.31 -> 0.38 ms and
-    // keeps its configuration below.
-    if (stg == 2 && cfg_fits<64, 64, false, 1, 3, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, 2, false, 2>(P, st);
-    const bool deep = stg == 0 ? cfg_fits<64, 64, false, 2, 4, 4, 0>(P, 2) : cfg_fits<64, 64, false, 2, 3, 4, 2>(P, 2);
-    return deep ? launch_staged<64, 64, false, 2, 4, 2, 3, 4>(P, stg, 2, st)
-                : launch_staged<64, 64, false, 3, 2, 2, 2, 4>(P, stg, 2, st);
+    if (branch_sum) return launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st);
+    // Two-window tiles (one weight stage serves 256 rows) where two CTAs per
+    // SM still fit (measured on B200: the dilation-1 conv1 0.321 -> 0.297 ms),
+    // else -- the wider windows of dilations 3 / 5 -- with a single window
+    // stage, the other CTA on the SM covering the next window's load (0.33 /
+    // 0.35 -> 0.30 ms, forward -1 % sustained).
+    if (cfg_fits<64, 64, false, 2, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st);
+    if (cfg_fits<64, 64, false, 1, 3, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, false, 2>(P, st);
+    // Else four weight stages (eight taps in flight) where that still fits
+    // two CTAs per SM: the 64-column MMAs are short, and with two stages the
+    // MMA warp waited on weight loads (4-8 % faster).
+    return cfg_fits<64, 64, false, 2, 4, 4>(P, 2) ? launch_cfg<64, 64, false, 2, 4, 4>(P, st)
+                                                 : launch_cfg<64, 64, false, 3, 2, 4>(P, st);
   }
   return cudaErrorInvalidValue;
 }
