@@ -912,17 +912,6 @@ def main():
         mine = dec.forward_device(torch.from_numpy(zr).cuda(), torch.from_numpy(gr).cuda())
         torch.cuda.synchronize()
         gather_check = {"rank_checked": ws - 1, "bit_exact": bool(torch.equal(last[ws - 1], mine))}
-    # Per-launch profile (roofline) from the same K steps run again with an
-    # event pair around every launch; kept out of the timed loop above, which
-    # runs the launches exactly as a caller does (no event records between
-    # them, so each kernel may start during the tail of the one before).
-    dec.set_stage_timing(2)
-    for _ in range(args.steps):
-        dec.forward_device(zt, gt, out=out)
-    torch.cuda.synchronize()
-    stats = dec.launch_stats()
-    dec.set_stage_timing(0)
-
     # ---- end to end through the public call with host buffers (e2e) --------
     # Every step copies its z / g in from pinned host memory and its waveform
     # back out.  Headline: gsvdec_forward with GSV_MEM_HOST_ASYNC, the call a
@@ -934,10 +923,18 @@ def main():
     wh = torch.empty(B * T0 * hop, dtype=torch.float32).pin_memory()
     zn, gn, wn = zh.numpy(), gh.numpy(), wh.numpy()
 
+    # Same protocol as the device-resident loop above (warm-up, the same short
+    # idle while the clock sampler starts, then K steps), so both start from
+    # the same power state: under the 1 kW cap the SM clock falls after
+    # ~0.5 s of back-to-back decoding, and a loop timed straight after the
+    # others would measure that instead of the host path.
     def timed_host(call):
         for _ in range(args.warmup):
             call()
         torch.cuda.synchronize()
+        cs = ClockSampler(local)
+        cs.start()
+        time.sleep(0.3)
         barrier()
         torch.cuda.synchronize()
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -947,20 +944,32 @@ def main():
         h1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        return max_over_ranks(h0.elapsed_time(h1))
+        return max_over_ranks(h0.elapsed_time(h1)), cs.stop()
 
-    ms_e2e = timed_host(lambda: dec.forward_async(zh, gh, out=wh, stream=stream.cuda_stream))
+    ms_e2e, clk_e2e = timed_host(lambda: dec.forward_async(zh, gh, out=wh, stream=stream.cuda_stream))
     dec.sync_status(stream.cuda_stream)
     wav_async = wn.copy()
-    ms_block = timed_host(lambda: dec.forward(zn, gn, out=wn, stream=stream.cuda_stream))
+    ms_block, _ = timed_host(lambda: dec.forward(zn, gn, out=wn, stream=stream.cuda_stream))
     assert np.array_equal(wav_async, wn), "overlapped and blocking host calls disagree"
     e2e = {"value": ws * secs_per_step * args.steps / (ms_e2e / 1e3), "unit": UNIT,
            "h2d_bytes_per_step": int(zn.nbytes + gn.nbytes), "d2h_bytes_per_step": int(wn.nbytes),
            "ms_per_step": ms_e2e / args.steps,
            "call": "gsvdec_forward(GSV_MEM_HOST_ASYNC) on pinned host buffers, one call per step",
+           "clocks": clk_e2e,
            "blocking": {"value": ws * secs_per_step * args.steps / (ms_block / 1e3),
                         "ms_per_step": ms_block / args.steps,
                         "call": "gsvdec_forward(GSV_MEM_HOST): copy in, decode, copy out, sync, per step"}}
+
+    # Per-launch profile (roofline) from the same K steps run again with an
+    # event pair around every launch; kept out of the timed loop above, which
+    # runs the launches exactly as a caller does (no event records between
+    # them, so each kernel may start during the tail of the one before).
+    dec.set_stage_timing(2)
+    for _ in range(args.steps):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    stats = dec.launch_stats()
+    dec.set_stage_timing(0)
 
     # ---- roofline of the dominant kernel + layer-weighted fraction ----------
     pk, pk_kind = peaks()
