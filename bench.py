@@ -983,12 +983,13 @@ def main():
         peak = FP32_CORE_TFLOPS
         bound = "fp32-core"
     achieved_all = f_conv / t_conv / 1e12 if t_conv > 0 else None
-    # The dominant kernel: the 128-channel single-output tap GEMM (rb1's three
-    # conv1 groups and its branch sum; tapconv_tc_kernel<64, 128, ...> with
-    # plain stores, the largest share of the forward in the ncu launch list).
-    # achieved = their algorithmic FLOPs / their CUDA-event time; traffic =
-    # DRAM bytes of one such launch from a single-launch ncu capture.
-    dom_names = ("rb1.step0.conv1", "rb1.step1.conv1", "rb1.step2.conv1", "rb1.final")
+    # The dominant kernel: tapconv_tc_kernel<64, 128, ...>, every launch of it
+    # (rb1's conv1 / conv2 groups and branch sum, and ups2: the largest share
+    # of the forward in the ncu launch list).  achieved = their algorithmic
+    # FLOPs / their CUDA-event time; traffic = DRAM bytes of one rb1.step1.conv1
+    # launch from a single-launch ncu capture.
+    dom_names = ("rb1.step0.conv1", "rb1.step0.conv2", "rb1.step1.conv1", "rb1.step1.conv2", "rb1.step2.conv1",
+                 "rb1.final", "ups2")
     dom = [s for s in conv if s["name"] in dom_names]
     f_dom = sum(s["flops"] for s in dom)
     t_dom = sum(s["ms"] for s in dom) / 1e3
@@ -1004,8 +1005,8 @@ def main():
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                 "frac": achieved / peak if achieved else None, "traffic": traffic,
                 "traffic_unit": "DRAM bytes per launch (ncu, one rb1.step1.conv1 launch)",
-                "kernel": "tapconv_tc_kernel<64, 128, ...> single-output launches (rb1 conv1 groups and "
-                          "branch sum: 4 launches per forward, " + ", ".join(dom_names) + ")",
+                "kernel": "tapconv_tc_kernel<64, 128, ...>, every launch of it (" + str(len(dom_names)) +
+                          " per forward: " + ", ".join(dom_names) + ")",
                 "launches_per_step": len(dom),
                 "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
                                                  else "nominal fp32 CUDA-core"),
