@@ -578,8 +578,12 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
               y[k] = (masked || dead) ? 0.0f : tanhf(a) * (1.0f / (1.0f + expf(-sg)));
             }
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(o.out_raw) + ((size_t)b * o.Lout + q) * H + n / 2;
-            store8(dst, y);
-            store8(dst + 8, y + 8);
+            if (ea.v8) {  // 16 outputs = 32 bytes at a 16-channel offset (H % 16 == 0)
+              st_global_v8(dst, pack_bf16x8(y), pack_bf16x8(y + 8));
+            } else {
+              store8(dst, y);
+              store8(dst + 8, y + 8);
+            }
           }
           continue;
         }
