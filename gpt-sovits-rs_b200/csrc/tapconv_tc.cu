@@ -121,8 +121,8 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
 // Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q.  Their flat
 // output indices e0..e0+15 are consecutive (gsv_internal.h) and, since Cout
 // and e0 are multiples of 16, lie in ONE output row t at channels c..c+15:
-// one mask test, 16-byte vector bias reads from shared memory, two packed
-// bf16 stores per output.
+// one mask test, 16-byte vector bias reads from shared memory, one 256-bit
+// store per output (two 16-byte ones where a base is not 32-byte aligned).
 __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const float* acc) {
   const int e0 = q * a.N + n - a.crop;
   if (e0 < 0 || e0 >= a.total) return;  // cropped ConvTranspose rows
@@ -671,7 +671,7 @@ bool tapconv_tc_supported(const TapConv& op) {
   }
   const int ck = ck_for(cin), nt = nt_for(op.N);
   if (!ck || !nt || op.N % nt) return false;
-  if (op.Cout % 16) return false;  // 16-element epilogue runs stay 16-byte aligned
+  if (op.Cout % 16) return false;  // 16-element epilogue runs stay 32-byte aligned
   if (op.gate && (op.N != op.Cout || op.N % 32 || op.crop || op.Q != op.Lout || op.nres)) return false;
   if ((long long)op.Lout * op.Cout >= (1ll << 31) || (long long)op.Q * op.N >= (1ll << 31))
     return false;  // 32-bit per-utterance index math
