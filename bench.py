@@ -668,10 +668,16 @@ def sharded_result(workload, dec, ws, rank, steps, warmup, mode):
         return t_ms, out
 
     ms, res = timed(step_dev)
-    ms_host, _ = timed(step_host)
+    ms_host, res_host = timed(step_host)
     if rank != 0:
         return None
     res = [r.cpu().numpy() for r in res] if isinstance(res, list) else res.cpu().numpy()
+    # The host path's waveform (views of a reused pinned buffer: compared now)
+    # must be the device path's, sample for sample.
+    if isinstance(res, list):
+        host_same = all(np.array_equal(a, np.asarray(b)) for a, b in zip(res, res_host))
+    else:
+        host_same = bool(np.array_equal(res, np.asarray(res_host)))
     if workload == "varlen256":
         idx = [0, int(np.argmax(lens)), int(np.argmin(lens))]
         errs, exact = [], True
@@ -693,7 +699,8 @@ def sharded_result(workload, dec, ws, rank, steps, warmup, mode):
         "e2e": {"value": total_s * steps / (ms_host / 1e3), "unit": UNIT, "ms_per_step": ms_host / steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "note": "host arrays in (one pinned H2D of each rank's share), waveform to rank 0's host "
-                        "(one D2H)"},
+                        "(one D2H)",
+                "bit_exact_vs_device": bool(host_same)},
         "parity": parity,
     }
 

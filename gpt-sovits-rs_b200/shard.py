@@ -200,18 +200,36 @@ def decode_batch_sharded(decode: Callable, z: np.ndarray, g: Optional[np.ndarray
 
 
 _PINNED = {}
+_PINNED_COPY = {}  # purpose -> event recorded after the last copy out of that buffer
 
 
-def _pinned(n: int, dtype):
-    """A pinned host buffer of at least n elements, reused across calls (page
-    locking hundreds of MB per call would cost more than the copy)."""
+def _pinned(n: int, dtype, purpose: str):
+    """A pinned host buffer of at least n elements for one purpose ("z", "g",
+    "wav"), reused across calls (page locking hundreds of MB per call would
+    cost more than the copy).  Each purpose has its own buffer, and a buffer
+    is handed out again only after the last asynchronous copy out of it (see
+    _h2d) has finished, so refilling it never races a copy in flight."""
     import torch
-    key = str(dtype)
+    key = (purpose, str(dtype))
+    ev = _PINNED_COPY.pop(purpose, None)
+    if ev is not None:
+        ev.synchronize()
     buf = _PINNED.get(key)
     if buf is None or buf.numel() < n:
         buf = torch.empty(max(n, 1), dtype=dtype, pin_memory=True)
         _PINNED[key] = buf
     return buf[:n]
+
+
+def _h2d(buf, device, purpose: str):
+    """Asynchronous copy of the pinned buffer `buf` to `device`; the buffer
+    stays reserved until the copy has run (_pinned waits for it)."""
+    import torch
+    out = buf.to(device, non_blocking=True)
+    ev = torch.cuda.Event()
+    ev.record()
+    _PINNED_COPY[purpose] = ev
+    return out
 
 
 def _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets, plan):
@@ -222,14 +240,17 @@ def _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets,
     mine = plan[rank]
     T0 = int(z.shape[2])
     if mine:
-        zs = _pinned(len(mine) * z.shape[1] * T0, torch.float32).view(len(mine), z.shape[1], T0)
-        zs.numpy()[:] = z[mine]
-        zd = zs.to(device, non_blocking=True)
+        # This rank's utterances, gathered straight into the pinned buffer (one
+        # multi-threaded copy, no temporary), then one asynchronous H2D.
+        sel = torch.as_tensor(mine, dtype=torch.int64)
+        zs = _pinned(len(mine) * z.shape[1] * T0, torch.float32, "z").view(len(mine), z.shape[1], T0)
+        torch.index_select(torch.from_numpy(np.ascontiguousarray(z, np.float32)), 0, sel, out=zs)
+        zd = _h2d(zs, device, "z")
         gd = None
         if g is not None:
-            gs = _pinned(len(mine) * int(np.prod(g.shape[1:])), torch.float32).view(len(mine), *g.shape[1:])
-            gs.numpy()[:] = g[mine]
-            gd = gs.to(device, non_blocking=True)
+            gs = _pinned(len(mine) * int(np.prod(g.shape[1:])), torch.float32, "g").view(len(mine), *g.shape[1:])
+            torch.index_select(torch.from_numpy(np.ascontiguousarray(g, np.float32)), 0, sel, out=gs)
+            gd = _h2d(gs, device, "g")
         local = [int(lengths[i]) for i in mine]
         parts = {}
         for bucket in plan_buckets(local, max_buckets):
@@ -251,7 +272,7 @@ def _decode_staged(decode, z, g, lengths, hop, dist, group, device, max_buckets,
     if got is None:
         return None
     flat = torch.cat(got)
-    host = _pinned(flat.numel(), torch.float32)
+    host = _pinned(flat.numel(), torch.float32, "wav")
     host.copy_(flat)  # one device-to-host copy of every piece
     arr = host.numpy()
     out: List[Optional[np.ndarray]] = [None] * len(lengths)
@@ -283,6 +304,8 @@ def decode_long_chunked(decode_chunk: Callable, T0: int, hop: int, dist, group=N
     if piece is None:
         piece = np.zeros(0, np.float32)
     sizes = [(ee - bb) * hop for bb, ee in chunks]
+    if world == 1:  # the one chunk is the whole waveform: no gather, no device round trip
+        return piece if on_dev else np.asarray(piece, np.float32)
     maxlen = max(1, max(sizes))
     n_valid = int(piece.numel()) if on_dev else int(np.asarray(piece).size)
     src = piece if on_dev else torch.from_numpy(np.asarray(piece, np.float32)).to(device)

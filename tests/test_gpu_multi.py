@@ -130,3 +130,50 @@ def test_multi_rejects_bad_handle_lists(gsv, sd):
     finally:
         a.close()
         b.close()
+
+
+class _Solo:
+    """torch.distributed's calls for one process (no process group)."""
+
+    @staticmethod
+    def get_rank(group=None):
+        return 0
+
+    @staticmethod
+    def get_world_size(group=None):
+        return 1
+
+    @staticmethod
+    def all_gather(out, t, group=None):
+        out[0].copy_(t)
+
+    @staticmethod
+    def gather(t, gather_list=None, dst=0, group=None):
+        gather_list[0].copy_(t)
+
+
+def test_sharded_host_arrays_match_device_path(gsv, sd):
+    """shard.decode_batch_sharded with host arrays on a CUDA device (one pinned
+    H2D per input, device buckets, one D2H) gives the device path's samples,
+    also on the next call, which refills the same pinned buffers; the
+    one-rank long-utterance path returns the whole decode."""
+    import torch
+    dec = gsv.Decoder.load(sd, device=0, mode="bf16")
+    try:
+        B, T0 = 9, 30
+        lens = np.array([30, 7, 19, 1, 25, 30, 12, 3, 22], np.int32)
+        z, g = gsv.synth.make_inputs(B, T0, seed_z=331, seed_g=332)
+        decode = lambda zb, gb, lb: dec.forward_device(zb, gb, lb)  # noqa: E731
+        zd, gd = torch.from_numpy(z).cuda(), torch.from_numpy(g).cuda()
+        want = [w.cpu().numpy() for w in
+                gsv.shard.decode_batch_sharded(decode, zd, gd, lens, dec.hop, _Solo, device="cuda")]
+        for call in range(2):
+            got = gsv.shard.decode_batch_sharded(decode, z, g, lens, dec.hop, _Solo, device="cuda")
+            for b in range(B):
+                assert np.array_equal(np.asarray(got[b]), want[b]), (call, b)
+        whole = dec.forward(z[:1], g[:1])
+        one = gsv.shard.decode_long_chunked(lambda b, e: dec.forward_chunk(z[:1], g[:1], b, e, halo=16),
+                                            T0, dec.hop, _Solo, device="cuda")
+        assert np.array_equal(one, whole)
+    finally:
+        dec.close()
