@@ -685,11 +685,25 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   TcParams P;
   memset(&P, 0, sizeof P);
   P.grp = g;
-  const int ck = ck_for(g.op[0].seg[0].Cin), nt = nt_for(g.op[0].N);
+  const int ck = ck_for(g.op[0].seg[0].Cin);
+  int nt = nt_for(g.op[0].N);
+  // A launch that would not fill the SMs (a short utterance, one time chunk
+  // of a long one) runs each tile's whole MMA chain on its own: narrower
+  // column tiles halve that chain and double the tiles.  Each output column's
+  // arithmetic is the same, so are the samples.
+  bool gated = false;
+  for (int i = 0; i < g.n; ++i) gated = gated || g.op[i].gate;
+  if (ck == 64 && !gated) {
+    long long tiles = (long long)g.op[0].B * cdiv(g.op[0].Q, kM) * (g.op[0].N / std::max(nt, 1)) * g.n;
+    while (nt > 64 && tiles < sm_count() && g.op[0].N % (nt / 2) == 0) {
+      nt /= 2;
+      tiles *= 2;
+    }
+  }
   int nflat = 0, wtiles = 0, max_rows = 0;
   for (int i = 0; i < g.n; ++i) {
     TapConv& op = P.grp.op[i];
-    if (!tapconv_tc_supported(op) || ck_for(op.seg[0].Cin) != ck || nt_for(op.N) != nt ||
+    if (!tapconv_tc_supported(op) || ck_for(op.seg[0].Cin) != ck || op.N % nt ||
         op.N != g.op[0].N || op.Q != g.op[0].Q || op.B != g.op[0].B)
       return cudaErrorInvalidValue;
     op.row_tiles = cdiv(op.Q, kM);
@@ -742,25 +756,31 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   // epilogue writes with 256-bit stores: they beat the shared-memory staged
   // TMA-store epilogue this kernel used to have for two-output layers (conv2
   // 3-9 % at 64-256 channels, the stride-2 ConvTranspose 10 %).
-  if (ck == 16 && nt == 16 && P.n_tiles == 1)
-    return branch_sum ? launch_cfg<16, 16, true, 6, 1, 4>(P, st)
-                      : launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);
+  // Multi-window tiles only where the launch has tiles to spare: they divide
+  // the tile count, and a sub-wave launch is bound by one tile's chain.
+  const bool spare = P.total_tiles >= 4 * sm_count();
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) {
+    if (branch_sum || !spare) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
+    return launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);
+  }
   if (ck == 32 && nt == 32 && P.n_tiles == 1)
-    return branch_sum ? launch_cfg<32, 32, true, 3, 1, 4, false, 2>(P, st)
-                      : launch_cfg<32, 32, true, 2, 1, 4, false, 2>(P, st);
+    return spare ? (branch_sum ? launch_cfg<32, 32, true, 3, 1, 4, false, 2>(P, st)
+                               : launch_cfg<32, 32, true, 2, 1, 4, false, 2>(P, st))
+                 : launch_cfg<32, 32, true, 3, 1, 4>(P, st);
   // 256 columns (one CTA per SM): three window stages (rb0 conv2 / branch sum
   // 2-6 % faster than two).
   if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 3, 4, 2>(P, st);
   if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2>(P, st);
   if (ck == 64 && nt == 64) {
-    if (branch_sum) return launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st);
+    if (branch_sum) return spare ? launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st)
+                                 : launch_cfg<64, 64, false, 3, 2, 4>(P, st);
     // Two-window tiles (one weight stage serves 256 rows) where two CTAs per
     // SM still fit (measured on B200: the dilation-1 conv1 0.321 -> 0.297 ms),
     // else -- the wider windows of dilations 3 / 5 -- with a single window
     // stage, the other CTA on the SM covering the next window's load (0.33 /
     // 0.35 -> 0.30 ms, forward -1 % sustained).
-    if (cfg_fits<64, 64, false, 2, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st);
-    if (cfg_fits<64, 64, false, 1, 3, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, false, 2>(P, st);
+    if (spare && cfg_fits<64, 64, false, 2, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, false, 2>(P, st);
+    if (spare && cfg_fits<64, 64, false, 1, 3, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 1, 3, 2, false, 2>(P, st);
     // Else four weight stages (eight taps in flight) where that still fits
     // two CTAs per SM: the 64-column MMAs are short, and with two stages the
     // MMA warp waited on weight loads (4-8 % faster).
