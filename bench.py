@@ -23,10 +23,12 @@ extra keys, the other configs of the same job in the same run:
           long60     one 60 s utterance in N halo time chunks (strong
                      scaling), with parity;
           fp32_cfg1  the fp32 CUDA-core mode on batch 1 x 5 s, with its
-                     roofline against the FP32 peak (rank 0).
+                     roofline against the FP32 peak (rank 0);
+          bf16_cfg1  the bf16 mode's latency on batch 1 x 5 s, device-resident
+                     and through the blocking host-memory call (rank 0).
           With N > 1 the headline's waveforms are gathered to rank 0 over NCCL
           inside the timed region too.
-roofline  the dominant kernel (the 128-channel single-output tap GEMM):
+roofline  the dominant kernel (the 128-channel tap GEMM, every launch of it):
           achieved = algorithmic FLOPs / launch time (CUDA events around
           every launch on the forward's stream); traffic from a single-launch
           ncu capture; layer_roofline adds the
@@ -733,6 +735,41 @@ def run_sharded(args, ws, rank, local):
         dist.destroy_process_group()
 
 
+def bf16_cfg1_result(sd, local, steps, warmup):
+    """Latency of one 5 s utterance (batch 1, z [1,192,250]) in the bf16 mode:
+    device-resident inputs (CUDA events around K back-to-back forwards), and
+    the blocking host-memory call an interactive caller makes (numpy in,
+    numpy waveform out, host wall clock per call)."""
+    import torch
+    gsv = load_pkg()
+    dec = gsv.Decoder.load(sd, device=local, mode="bf16")
+    z, g = gsv.synth.make_inputs(1, 250)
+    zt, gt = torch.from_numpy(z).cuda(), torch.from_numpy(g).cuda()
+    out = torch.empty(250 * dec.hop, device="cuda")
+    for _ in range(warmup):
+        dec.forward_device(zt, gt, out=out)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dec.forward_device(zt, gt, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wav = np.empty(250 * dec.hop, np.float32)
+    for _ in range(warmup):
+        dec.forward(z, g, out=wav)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        dec.forward(z, g, out=wav)
+    ms_host = (time.perf_counter() - t0) * 1e3 / steps
+    dec.close()
+    return {"value": 5.0 / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
+            "dtype": "bf16", "workload": "bf16 mode, B=1 x 5 s (z [1,192,250] -> 160 000 samples), latency",
+            "host_call_ms": ms_host,
+            "host_call": "gsvdec_forward(GSV_MEM_HOST) per call: numpy z / g in, numpy waveform out, host wall clock"}
+
+
 def fp32_cfg1_result(sd, local, steps, warmup, pk):
     """The fp32 CUDA-core mode on its own config: batch 1 x 5 s (z [1,192,250]),
     device-resident inputs, CUDA events around K steps; the layer-weighted
@@ -1048,6 +1085,7 @@ def main():
                 extra[wl] = r
         if rank == 0:
             extra["fp32_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk)
+            extra["bf16_cfg1"] = bf16_cfg1_result(sd, local, max(10, args.steps), 5)
         barrier()
 
     if rank == 0:
