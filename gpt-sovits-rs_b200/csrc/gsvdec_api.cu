@@ -1034,10 +1034,15 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
     // segments (no global loads in the epilogue); narrow layers read them in
     // the epilogue instead (an extra TMA window costs more there than the MMA
     // saves), and so do convs whose input width differs from Cout (every GEMM
-    // segment shares one input width).
+    // segment shares one input width).  The three-residual branch sums at
+    // >= 128 channels also read theirs in the epilogue (256-bit loads): three
+    // identity segments there cost 24 MMAs per tile on top of 168 (rb1's
+    // branch sum 0.448 -> 0.416 ms on B200; single-residual conv2 and the
+    // narrower sums measured slower that way).
     for (int i = 0; i < grp.n; ++i) {
       TapConv& op = grp.op[i];
       if (op.nres == 0 || op.Cout < kIdentityResidualMinC || op.seg[0].Cin != op.Cout) continue;
+      if (op.nres >= 2 && op.Cout >= 128) continue;
       auto it = h->ident_off.find(op.Cout);
       if (it == h->ident_off.end() || op.N != op.Cout || op.crop != 0 || op.Q != op.Lout ||
           op.nseg + op.nres > kMaxSeg)
