@@ -1028,12 +1028,12 @@ def main():
         bound = "fp32-core"
     achieved_all = f_conv / t_conv / 1e12 if t_conv > 0 else None
     # The dominant kernel: tapconv_tc_kernel<64, 128, ...>, every launch of it
-    # (rb1's conv1 / conv2 groups and branch sum, and ups2: the largest share
+    # (conv_pre, rb1's conv1 / conv2 groups and branch sum, and ups2: the largest share
     # of the forward in the ncu launch list).  achieved = their algorithmic
     # FLOPs / their CUDA-event time; traffic = DRAM bytes of one rb1.step1.conv1
     # launch from a single-launch ncu capture.
-    dom_names = ("rb1.step0.conv1", "rb1.step0.conv2", "rb1.step1.conv1", "rb1.step1.conv2", "rb1.step2.conv1",
-                 "rb1.final", "ups2")
+    dom_names = ("conv_pre", "rb1.step0.conv1", "rb1.step0.conv2", "rb1.step1.conv1", "rb1.step1.conv2",
+                 "rb1.step2.conv1", "rb1.final", "ups2")
     dom = [s for s in conv if s["name"] in dom_names]
     f_dom = sum(s["flops"] for s in dom)
     t_dom = sum(s["ms"] for s in dom) / 1e3
