@@ -770,7 +770,7 @@ def bf16_cfg1_result(sd, local, steps, warmup):
             "host_call": "gsvdec_forward(GSV_MEM_HOST) per call: numpy z / g in, numpy waveform out, host wall clock"}
 
 
-def fp32_cfg1_result(sd, local, steps, warmup, pk):
+def fp32_cfg1_result(sd, local, steps, warmup, pk, cpu=False):
     """The fp32 CUDA-core mode on its own config: batch 1 x 5 s (z [1,192,250]),
     device-resident inputs, CUDA events around K steps; the layer-weighted
     roofline and the tap-GEMM launches' achieved TF/s against the nominal FP32
@@ -799,6 +799,12 @@ def fp32_cfg1_result(sd, local, steps, warmup, pk):
     dec.set_stage_timing(0)
     dec.close()
     roof_s, meas_s, _ = layer_roofline(stats, "fp32", pk)
+    cpu_base = None
+    if cpu:  # the same batch-1 5 s input through the oracle port on the host cores
+        reps, el, threads = cpu_port_sample(sd, z, g, min_seconds=3.0, max_reps=6)
+        cpu_base = {"value": reps * 5.0 / el, "unit": UNIT, "ms_per_utterance": 1e3 * el / reps, "cores": threads,
+                    "kind": "port", "sample": f"{reps} x the same 5 s utterance (z [1,192,250]), C restatement of "
+                                              "the reference decoder, float accumulation"}
     conv = [s_ for s_ in stats if s_["kind"] == 0]
     f_conv = sum(s_["flops"] for s_ in conv)
     t_conv = sum(s_["ms"] for s_ in conv) / 1e3
@@ -813,6 +819,7 @@ def fp32_cfg1_result(sd, local, steps, warmup, pk):
         "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
                            "sum_meas_ms": 1e3 * meas_s},
         "gpu_launches": len(stats) * steps,
+        "cpu_baseline": cpu_base,
     }
 
 
@@ -1084,7 +1091,8 @@ def main():
             if rank == 0:
                 extra[wl] = r
         if rank == 0:
-            extra["fp32_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk)
+            extra["fp32_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk,
+                                                  cpu=ws == 1 and not args.no_cpu_baseline)
             extra["bf16_cfg1"] = bf16_cfg1_result(sd, local, max(10, args.steps), 5)
         barrier()
 
