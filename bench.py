@@ -643,11 +643,13 @@ def sharded_result(workload, dec, ws, rank, steps, warmup, mode):
             return gsv.shard.decode_long_chunked(
                 lambda b, e: dec.forward_chunk_device(zd, gd, b, e, halo=halo), T0, hop, dd, group, device="cuda")
 
-        def step_host():
-            return gsv.shard.decode_long_chunked(
-                lambda b, e: dec.forward_chunk(z, g, b, e, halo=halo), T0, hop, dd, group, device="cuda")
+        def step_host():  # each rank's halo window in (pinned), the waveform out on rank 0
+            return gsv.shard.decode_long_staged(
+                lambda zw, gw, b, e: dec.forward_chunk_device(zw, gw, b, e, halo=halo), z, g, hop, dd, group,
+                device="cuda", halo=halo)
         desc = f"one 60 s utterance (z [1,192,{T0}]) in {ws} time chunks, halo {halo} frames"
-        h2d = int(z.nbytes + g.nbytes)
+        wins = [gsv.shard.halo_window(b, e, T0, halo) for b, e in gsv.shard.plan_chunks(T0, ws) if e > b]
+        h2d = int(sum(z.shape[1] * (hi - lo) * 4 + g.nbytes for lo, hi in wins))
         d2h = T0 * hop * 4
 
     def timed(step):
@@ -700,8 +702,8 @@ def sharded_result(workload, dec, ws, rank, steps, warmup, mode):
         "gather": "waveform pieces to rank 0 inside the timed region (NCCL gather)",
         "e2e": {"value": total_s * steps / (ms_host / 1e3), "unit": UNIT, "ms_per_step": ms_host / steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "note": "host arrays in (one pinned H2D of each rank's share), waveform to rank 0's host "
-                        "(one D2H)",
+                "note": "host arrays in (one pinned H2D of each rank's share: its utterances, or its chunk's "
+                        "halo window), waveform to rank 0's host (one pinned D2H)",
                 "bit_exact_vs_device": bool(host_same)},
         "parity": parity,
     }

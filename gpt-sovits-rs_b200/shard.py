@@ -313,3 +313,53 @@ def decode_long_chunked(decode_chunk: Callable, T0: int, hop: int, dist, group=N
     if got is None:
         return None
     return torch.cat(got) if on_dev else np.concatenate(got)
+
+
+def decode_long_staged(decode_chunk: Callable, z: np.ndarray, g: Optional[np.ndarray], hop: int, dist,
+                       group=None, device="cuda", halo: int = 16):
+    """decode_long_chunked for a host utterance z [1, C, T0] (g [1, gin, 1] or
+    None) on a CUDA device: each rank copies only its chunk's input window
+    (the chunk plus `halo` frames per side, clamped) into a reused pinned
+    buffer and moves it with ONE asynchronous host-to-device copy, decodes it
+    on the device with `decode_chunk(zw, gw, begin, end)` (zw [1, C, w] the
+    window on the device, [begin, end) the chunk's frames inside it; e.g.
+    ``lambda zw, gw, b, e: dec.forward_chunk_device(zw, gw, b, e, halo)``),
+    the device pieces are gathered to rank 0, and rank 0 brings the waveform
+    back with ONE device-to-host copy into a pinned buffer.  Rank 0 returns a
+    numpy view of that buffer (reused by the next such call: copy it to keep
+    it), other ranks None.  The samples equal decode_long_chunked's: a chunk
+    decoded from its clamped window sees exactly the frames it would see in
+    the whole utterance."""
+    import torch
+    rank = dist.get_rank(group)
+    world = dist.get_world_size(group)
+    if z.ndim != 3 or z.shape[0] != 1:
+        raise ValueError("z must be [1, C, T0]")
+    T0 = int(z.shape[2])
+    chunks = plan_chunks(T0, world)
+    b, e = chunks[rank]
+    sizes = [(ee - bb) * hop for bb, ee in chunks]
+    if e > b:
+        lo, hi = halo_window(b, e, T0, halo)
+        zs = _pinned(z.shape[1] * (hi - lo), torch.float32, "z").view(1, z.shape[1], hi - lo)
+        np.copyto(zs.numpy(), z[:, :, lo:hi], casting="same_kind")
+        zd = _h2d(zs, device, "z")
+        gd = None
+        if g is not None:
+            gs = _pinned(int(np.prod(g.shape)), torch.float32, "g").view(*g.shape)
+            np.copyto(gs.numpy(), g, casting="same_kind")
+            gd = _h2d(gs, device, "g")
+        piece = decode_chunk(zd, gd, b - lo, e - lo)
+    else:
+        piece = torch.zeros(0, device=device)
+    if world == 1:
+        flat = piece
+    else:
+        got = _gather_to_root(piece, int(piece.numel()), max(1, max(sizes)), dist, group, device,
+                              as_numpy=False, sizes=sizes)
+        if got is None:
+            return None
+        flat = torch.cat(got)
+    host = _pinned(flat.numel(), torch.float32, "wav")
+    host.copy_(flat)  # the one device-to-host copy
+    return host.numpy()

@@ -177,3 +177,53 @@ def test_sharded_host_arrays_match_device_path(gsv, sd):
         assert np.array_equal(one, whole)
     finally:
         dec.close()
+
+
+class _SeqRank:
+    """torch.distributed's calls for rank `r` of `w`, the ranks run one after
+    the other in this process: a rank's gather leaves its piece in `sink`,
+    and rank 0 (run last) collects every rank's piece from it."""
+
+    def __init__(self, r, w, sink):
+        self.r, self.w, self.sink = r, w, sink
+
+    def get_rank(self, group=None):
+        return self.r
+
+    def get_world_size(self, group=None):
+        return self.w
+
+    def gather(self, t, gather_list=None, dst=0, group=None):
+        self.sink[self.r] = t.clone()
+        if gather_list is not None:
+            for k in range(self.w):
+                gather_list[k].copy_(self.sink[k])
+
+
+def test_long_staged_host_path_matches_whole_decode(gsv, sd):
+    """shard.decode_long_staged (each rank's halo window copied in, device
+    chunk decode, device gather, one D2H on rank 0) gives the whole-utterance
+    decode sample for sample, for 1 and 3 ranks (run in turn in this process),
+    also on a second call that refills the same pinned buffers."""
+    import torch
+    dec = gsv.Decoder.load(sd, device=0, mode="bf16")
+    try:
+        T0, halo = 100, 16
+        z, g = gsv.synth.make_inputs(1, T0, seed_z=341, seed_g=342)
+        whole = dec.forward(z, g)
+        chunk = lambda zw, gw, b, e: dec.forward_chunk_device(zw, gw, b, e, halo=halo)  # noqa: E731
+        for w in (1, 3):
+            for call in range(2):
+                sink = {}
+                got = None
+                for r in reversed(range(w)):
+                    out = gsv.shard.decode_long_staged(chunk, z, g, dec.hop, _SeqRank(r, w, sink),
+                                                       device="cuda", halo=halo)
+                    if r == 0:
+                        got = np.array(out)
+                    else:
+                        assert out is None
+                torch.cuda.synchronize()
+                assert np.array_equal(got, whole), (w, call)
+    finally:
+        dec.close()
