@@ -8,7 +8,7 @@ offline) -- giving 16 x 320 000 samples at 32 kHz.  Every rank decodes its own
 batch (utterances are independent units: weak scaling, no collective on the
 data path).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode bf16|fp32]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode bf16|fp32|fp32tc]
     python bench.py --impl reference ...   # the CPU reference arm
 
 value     audio-seconds per second, whole job, inputs resident in HBM.
@@ -24,6 +24,9 @@ extra keys, the other configs of the same job in the same run:
                      scaling), with parity;
           fp32_cfg1  the fp32 CUDA-core mode on batch 1 x 5 s, with its
                      roofline against the FP32 peak (rank 0);
+          fp32tc_cfg1  the same config in the fp32tc mode (fp32 accuracy on
+                     the tensor cores, three bf16 pieces per value), against
+                     the measured bf16 peak / 6 (rank 0);
           bf16_cfg1  the bf16 mode's latency on batch 1 x 5 s, device-resident
                      and through the blocking host-memory call (rank 0).
           With N > 1 the headline's waveforms are gathered to rank 0 over NCCL
@@ -228,7 +231,8 @@ def layer_roofline(stats, mode, pk):
     sum over the reference convs it computes of max(F / P, bytes / BW), each
     conv's F and bytes counted as if it ran alone (unfused layer I/O)."""
     p_tensor = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) * 1e12
-    p_comp = p_tensor if mode == "bf16" else FP32_CORE_TFLOPS * 1e12
+    # fp32tc: six bf16 tensor-core products per fp32 product
+    p_comp = {"bf16": p_tensor, "fp32tc": p_tensor / 6}.get(mode, FP32_CORE_TFLOPS * 1e12)
     bw = pk["hbm_gbs"] * 1e9
     rows, roof, meas = [], 0.0, 0.0
     for s in stats:
@@ -772,14 +776,18 @@ def bf16_cfg1_result(sd, local, steps, warmup):
             "host_call": "gsvdec_forward(GSV_MEM_HOST) per call: numpy z / g in, numpy waveform out, host wall clock"}
 
 
-def fp32_cfg1_result(sd, local, steps, warmup, pk, cpu=False):
-    """The fp32 CUDA-core mode on its own config: batch 1 x 5 s (z [1,192,250]),
+def fp32_cfg1_result(sd, local, steps, warmup, pk, cpu=False, mode="fp32"):
+    """An fp32-accurate mode on its own config: batch 1 x 5 s (z [1,192,250]),
     device-resident inputs, CUDA events around K steps; the layer-weighted
-    roofline and the tap-GEMM launches' achieved TF/s against the nominal FP32
-    CUDA-core peak (148 SMs x 128 lanes x 2 FLOP x 1.965 GHz)."""
+    roofline and the tap-GEMM launches' achieved TF/s.  mode "fp32": the CUDA
+    cores, against the nominal FP32 CUDA-core peak (148 SMs x 128 lanes x 2
+    FLOP x 1.965 GHz); "fp32tc": three bf16 pieces per value on the tensor
+    cores, against the measured bf16 peak / 6 (six piece products per fp32
+    product), its achieved rate also given as a fraction of the FP32 CUDA-core
+    peak."""
     import torch
     gsv = load_pkg()
-    dec = gsv.Decoder.load(sd, device=local, mode="fp32")
+    dec = gsv.Decoder.load(sd, device=local, mode=mode)
     z, g = gsv.synth.make_inputs(1, 250)
     zt, gt = torch.from_numpy(z).cuda(), torch.from_numpy(g).cuda()
     out = torch.empty(250 * dec.hop, device="cuda")
@@ -800,7 +808,7 @@ def fp32_cfg1_result(sd, local, steps, warmup, pk, cpu=False):
     stats = dec.launch_stats()
     dec.set_stage_timing(0)
     dec.close()
-    roof_s, meas_s, _ = layer_roofline(stats, "fp32", pk)
+    roof_s, meas_s, _ = layer_roofline(stats, mode, pk)
     cpu_base = None
     if cpu:  # the same batch-1 5 s input through the oracle port on the host cores
         reps, el, threads = cpu_port_sample(sd, z, g, min_seconds=3.0, max_reps=6)
@@ -811,13 +819,24 @@ def fp32_cfg1_result(sd, local, steps, warmup, pk, cpu=False):
     f_conv = sum(s_["flops"] for s_ in conv)
     t_conv = sum(s_["ms"] for s_ in conv) / 1e3
     achieved = f_conv / t_conv / 1e12 if t_conv > 0 else None
+    if mode == "fp32tc":
+        peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) / 6
+        roof = {"bound": "tensor (six bf16 products per fp32 product)", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak if achieved else None,
+                "frac_of_fp32_core_peak": achieved / FP32_CORE_TFLOPS if achieved else None,
+                "kernel": "tapconv_tc launches of one forward (all 97 convs except conv_post), three-piece operands",
+                "peak_source": "measured bf16_tflops_sustained (MEASURED_PEAKS.json) / 6"}
+        wl = "fp32tc mode (fp32 accuracy on the tensor cores), B=1 x 5 s (z [1,192,250] -> 160 000 samples)"
+    else:
+        roof = {"bound": "fp32-core", "achieved": achieved, "peak": FP32_CORE_TFLOPS, "unit": "TFLOP/s",
+                "frac": achieved / FP32_CORE_TFLOPS if achieved else None,
+                "kernel": "tapconv_f32 launches of one forward (all 97 convs except conv_post)",
+                "peak_source": "nominal FP32 CUDA-core peak (not in MEASURED_PEAKS.json)"}
+        wl = "fp32 CUDA-core mode, B=1 x 5 s (z [1,192,250] -> 160 000 samples)"
     return {
         "value": 5.0 / (ms / 1e3), "unit": UNIT, "ms_per_step": ms, "steps": steps, "warmup": warmup,
-        "dtype": "f32", "workload": "fp32 CUDA-core mode, B=1 x 5 s (z [1,192,250] -> 160 000 samples)",
-        "roofline": {"bound": "fp32-core", "achieved": achieved, "peak": FP32_CORE_TFLOPS, "unit": "TFLOP/s",
-                     "frac": achieved / FP32_CORE_TFLOPS if achieved else None,
-                     "kernel": "tapconv_f32 launches of one forward (all 97 convs except conv_post)",
-                     "peak_source": "nominal FP32 CUDA-core peak (not in MEASURED_PEAKS.json)"},
+        "dtype": "f32", "workload": wl,
+        "roofline": roof,
         "layer_roofline": {"frac": roof_s / meas_s if meas_s else None, "sum_roof_ms": 1e3 * roof_s,
                            "sum_meas_ms": 1e3 * meas_s},
         "gpu_launches": len(stats) * steps,
@@ -831,7 +850,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--mode", choices=("bf16", "fp32"), default="bf16")
+    ap.add_argument("--mode", choices=("bf16", "fp32", "fp32tc"), default="bf16")
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--frames", type=int, default=500)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1095,6 +1114,7 @@ def main():
         if rank == 0:
             extra["fp32_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk,
                                                   cpu=ws == 1 and not args.no_cpu_baseline)
+            extra["fp32tc_cfg1"] = fp32_cfg1_result(sd, local, max(3, min(args.steps, 10)), 3, pk, mode="fp32tc")
             extra["bf16_cfg1"] = bf16_cfg1_result(sd, local, max(10, args.steps), 5)
         barrier()
 

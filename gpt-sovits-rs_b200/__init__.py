@@ -28,7 +28,7 @@ STATUS = {
     -1: "GSV_E_INVALID_ARG", -2: "GSV_E_MISSING_KEY", -3: "GSV_E_SHAPE", -4: "GSV_E_DTYPE",
     -5: "GSV_E_CUDA", -6: "GSV_E_OOM", -7: "GSV_E_UNSUPPORTED", -8: "GSV_E_TIMEOUT",
 }
-MODES = {"fp32": 0, "bf16": 1}
+MODES = {"fp32": 0, "bf16": 1, "fp32tc": 2}  # fp32tc: fp32 accuracy on tensor cores (three bf16 pieces)
 MEM_HOST, MEM_DEVICE, MEM_HOST_ASYNC = 0, 1, 2
 DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 
@@ -177,7 +177,7 @@ class Decoder:
         info = _Info()
         _check(library().gsvdec_get_info(self._h, ctypes.byref(info)))
         self.info = {f: getattr(info, f) for f, _ in _Info._fields_}
-        self.mode = "fp32" if info.mode == 0 else "bf16"
+        self.mode = {v: k for k, v in MODES.items()}[info.mode]
         self.hop = info.hop
 
     # -- Decoder::load ------------------------------------------------------

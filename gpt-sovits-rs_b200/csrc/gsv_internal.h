@@ -42,6 +42,14 @@ struct TapSeg {
   int ntaps;
   int off0;       // row offset of tap 0
   int offstep;    // row offset step between taps
+  // Three-piece operands (bf16 tcgen05 only): when pc > 0, x holds [B][Lin][3 pc]
+  // (three bf16 pieces X0, X1, X2 of each fp32 value, channel planes of width
+  // pc) and the segment's Cin channels are a K list of pc-wide blocks over
+  // those planes: Cin = 5 pc reads planes [X2 X1 X0 X1 X0] (against weight
+  // pieces [W0 W1 W2 W0 W1]: the five small products), Cin = pc reads X0
+  // (against W0: the large one), Cin = 3 pc reads [X2 X1 X0] (against
+  // identities: a residual).
+  int pc;
 };
 
 struct TapConv {
@@ -59,6 +67,9 @@ struct TapConv {
   const int* len;        // [B] valid output rows, or null
   int row_tiles;         // tiles per utterance along q (set by the launcher)
   int bias_bc_ld;        // row stride of bias_bc (0: Cout)
+  // Three-piece outputs (bf16 tcgen05 only): out_raw / out_act (and the
+  // residuals read) hold [B][Lout][3 Cout], each value as its three bf16 pieces.
+  int split;
   // Gated-activation epilogue (bf16 tcgen05 only): the N = 2H GEMM columns are
   // interleaved in 16-column (a, b) pairs and the op writes
   // out_raw[b][q][H] = tanh(a + bias + bias_bc) * sigmoid(b + bias + bias_bc).

@@ -6,8 +6,12 @@
 
 namespace gsv {
 
-// Element type of activations / packed weights in one arithmetic mode.
-enum class Dt { F32 = 0, BF16 = 1 };
+// Element type of activations / packed weights in one arithmetic mode.  X3:
+// an fp32 value held as the exact sum of three bf16 pieces, stored as three
+// channel planes per row ([B][L][3][C], piece 0 the bf16 rounding of the
+// value, piece 1 that of the remainder, piece 2 the rest); the decoder
+// activations of GSV_MODE_FP32_TC.
+enum class Dt { F32 = 0, BF16 = 1, X3 = 2 };
 
 // fp32 CUDA-core tap GEMM (weights packed [tap][Cin][N] fp32).
 cudaError_t launch_tapconv_f32(const TapConvGroup& g, cudaStream_t st);

@@ -451,7 +451,9 @@ struct GemmConv {
   int Cin = 0, Cout = 0, N = 0, ntaps = 0, off0 = 0, offstep = 1;
   int stride = 1, pad = 0, K = 0;  // ConvT: Q/crop/Lout derive from these
   bool transposed = false;
-  size_t w_off = 0;  // byte offset in the weight arena
+  bool x3 = false;   // three-piece packing (GSV_MODE_FP32_TC decoder), in the second arena
+  size_t w_off = 0;  // byte offset in the weight arena (three-piece: the five small-product blocks)
+  size_t w_off2 = 0; // three-piece: the large-product block W0
   size_t b_off = 0;  // float offset in the bias arena
   int Lout(int Lin) const {
     return transposed ? (Lin - 1) * stride + K - 2 * pad : Lin + 2 * pad - (ntaps - 1) * offstep;
@@ -466,6 +468,7 @@ struct GemmConv {
 // temporaries are handed over with conv(HostConv&&).
 struct Packer {
   Dt dt;
+  bool x3 = false;                      // three-piece bf16 packing (dt BF16)
   size_t size = 0;                      // bytes reserved so far
   std::unique_ptr<uint8_t[]> arena;     // size bytes after finish()
   std::vector<float> biases;
@@ -477,6 +480,7 @@ struct Packer {
     const int* rows; // conv: packed column n reads weight row rows[n] (NULL: n)
     int Cin, Cout, N, K, stride;
     size_t base;
+    size_t base2;    // three-piece: the W0 block
     int j, n0, n1;   // tap j, packed columns [n0, n1)
   };
   std::vector<Job> jobs;
@@ -485,6 +489,13 @@ struct Packer {
   std::vector<std::unique_ptr<std::vector<int>>> owned_rows;
 
   size_t esize() const { return dt == Dt::F32 ? 4 : 2; }
+  // Packed K entries per input channel: a three-piece conv's first K list
+  // is five weight pieces long ([W0 W1 W2 W0 W1] against [X2 X1 X0 X1 X0]);
+  // its second (W0 against X0) follows at w_off2.
+  int kmul() const { return x3 ? 5 : 1; }
+  void reserve_x3_second(GemmConv& g) {
+    if (x3) g.w_off2 = reserve((size_t)g.ntaps * g.N * g.Cin * esize());
+  }
   size_t reserve(size_t bytes) {
     const size_t r = (size + 1023) / 1024 * 1024;
     if (r > size) gaps.emplace_back(size, r - size);
@@ -497,7 +508,8 @@ struct Packer {
     const int cols = std::max(1, 65536 / std::max(Cin, 1));
     for (int j = 0; j < g.ntaps; ++j)
       for (int n0 = 0; n0 < g.N; n0 += cols)
-        jobs.push_back(Job{kind, w, rows, Cin, g.Cout, g.N, K, stride, g.w_off, j, n0, std::min(g.N, n0 + cols)});
+        jobs.push_back(Job{kind, w, rows, Cin, g.Cout, g.N, K, stride, g.w_off, g.w_off2, j, n0,
+                           std::min(g.N, n0 + cols)});
   }
 
   GemmConv conv(const HostConv& c) { return conv_from(c, c.w.data()); }
@@ -523,8 +535,9 @@ struct Packer {
   GemmConv conv_from(const HostConv& c, const float* w, const int* rows = nullptr) {
     GemmConv g;
     g.Cin = c.d1; g.Cout = c.d0; g.N = c.d0; g.ntaps = c.K;
-    g.off0 = -c.pad; g.offstep = c.dil; g.pad = c.pad; g.K = c.K;
-    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * esize());
+    g.off0 = -c.pad; g.offstep = c.dil; g.pad = c.pad; g.K = c.K; g.x3 = x3;
+    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * kmul() * esize());
+    reserve_x3_second(g);
     add_jobs(kConv, w, g, g.Cin, c.K, 1, rows);
     g.b_off = biases.size();
     for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
@@ -534,7 +547,7 @@ struct Packer {
   size_t identity(int C) {
     GemmConv g;
     g.Cin = C; g.Cout = C; g.N = C; g.ntaps = 1;
-    g.w_off = reserve((size_t)C * C * esize());
+    g.w_off = reserve((size_t)C * C * (x3 ? 3 : 1) * esize());
     add_jobs(kIdentity, nullptr, g, C, 1, 1);
     return g.w_off;
   }
@@ -545,8 +558,9 @@ struct Packer {
     g.transposed = true;
     g.Cin = c.d0; g.Cout = c.d1; g.stride = c.stride; g.pad = c.pad; g.K = c.K;
     g.ntaps = (c.K + c.stride - 1) / c.stride;
-    g.N = c.stride * g.Cout; g.off0 = 0; g.offstep = -1;
-    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * esize());
+    g.N = c.stride * g.Cout; g.off0 = 0; g.offstep = -1; g.x3 = x3;
+    g.w_off = reserve((size_t)g.ntaps * g.N * g.Cin * kmul() * esize());
+    reserve_x3_second(g);
     add_jobs(kConvT, c.w.data(), g, g.Cin, c.K, c.stride);
     g.b_off = biases.size();
     for (int n = 0; n < g.Cout; ++n) biases.push_back(c.b.empty() ? 0.0f : c.b[n]);
@@ -560,6 +574,40 @@ struct Packer {
   void fill(const Job& b, F src) {
     const int Cin = b.Cin, N = b.N, j = b.j, n0 = b.n0, n1 = b.n1;
     uint8_t* base = arena.get() + b.base;
+    if (x3 && b.kind == kIdentity) {  // [I I I] against [X2 X1 X0]: a residual, exactly
+      uint16_t* out = reinterpret_cast<uint16_t*>(base);
+      for (int n = n0; n < n1; ++n) {
+        uint16_t* row = out + ((size_t)j * N + n) * 3 * Cin;
+        for (int k = 0; k < 3; ++k)
+          for (int ci = 0; ci < Cin; ++ci)
+            row[k * Cin + ci] = __bfloat16_as_ushort(__float2bfloat16_rn(n == ci ? 1.0f : 0.0f));
+      }
+      return;
+    }
+    if (x3) {
+      // Row (tap j, column n) of the first block: [W0 W1 W2 W0 W1] (paired
+      // with activation planes [X2 X1 X0 X1 X0]); of the second: W0.  W0..W2
+      // are the three bf16 pieces of each weight.
+      uint16_t* out = reinterpret_cast<uint16_t*>(base);
+      uint16_t* out2 = reinterpret_cast<uint16_t*>(arena.get() + b.base2);
+      for (int n = n0; n < n1; ++n) {
+        uint16_t* row = out + ((size_t)j * N + n) * 5 * Cin;
+        uint16_t* row2 = out2 + ((size_t)j * N + n) * Cin;
+        for (int ci = 0; ci < Cin; ++ci) {
+          float r = src(n, ci);
+          uint16_t pc[3];
+          for (int k = 0; k < 3; ++k) {
+            const __nv_bfloat16 hb = __float2bfloat16_rn(r);
+            pc[k] = __bfloat16_as_ushort(hb);
+            r = r - __bfloat162float(hb);
+          }
+          const int piece[5] = {0, 1, 2, 0, 1};
+          for (int k = 0; k < 5; ++k) row[k * Cin + ci] = pc[piece[k]];
+          row2[ci] = pc[0];
+        }
+      }
+      return;
+    }
     if (dt == Dt::BF16) {
       uint16_t* out = reinterpret_cast<uint16_t*>(base);
       for (int n = n0; n < n1; ++n) {
@@ -644,6 +692,14 @@ struct gsvdec {
   int* h_err = nullptr;
   int* d_err = nullptr;
   std::map<int, size_t> ident_off;  // bf16: identity weights per channel width
+  // GSV_MODE_FP32_TC: the decoder's convs packed as three-piece K lists in a
+  // second arena (same geometry and biases as pre / stages).
+  bool x3 = false;
+  GemmConv xpre;
+  std::vector<Stage> xstages;
+  void* d_wx = nullptr;
+  size_t wx_bytes = 0;
+  std::map<int, size_t> xident_off;  // three-piece identities [I I I] per channel width
   std::map<std::string, GemmConv> layers;  // every tap-GEMM conv by its dec.* prefix
   std::string layer_names;                 // newline-separated, in forward order
   void* lws = nullptr;                     // single-layer workspace
@@ -733,6 +789,11 @@ namespace gsv {
 namespace {
 
 size_t act_bytes(const gsvdec* h) { return h->dt == Dt::F32 ? 4 : 2; }
+// Bytes per element of the decoder forward's activations (three bf16 pieces
+// in GSV_MODE_FP32_TC).
+size_t fwd_act_bytes(const gsvdec* h) { return h->x3 ? 6 : act_bytes(h); }
+// Element type of the decoder forward's activations.
+Dt fwd_dt(const gsvdec* h) { return h->x3 ? Dt::X3 : h->dt; }
 
 // GEMM column col of a fused-gate in_layer holds original channel gate_src:
 // column 32p + r is tanh-half channel 16p + r (r < 16), else sigmoid-half
@@ -903,7 +964,7 @@ constexpr long long kSplitScratchFloats = 1LL << 24;  // 64 MB
 
 int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_t drain = nullptr) {
   const size_t act = max_act_elems(h, T0) * (size_t)B;
-  const size_t eb = act_bytes(h);
+  const size_t eb = fwd_act_bytes(h);
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   const int L = out_len(h, T0);
   size_t need = 0;
@@ -941,12 +1002,15 @@ int ensure_ws(gsvdec* h, int B, int T0, bool with_tap, Workspace& w, cudaStream_
   return GSV_OK;
 }
 
-TapSeg make_seg(const gsvdec* h, const GemmConv& g, const void* x, int Lin) {
+// part (three-piece convs only): 0 = the five small-product blocks, 1 = the
+// large-product block.
+TapSeg make_seg(const gsvdec* h, const GemmConv& g, const void* x, int Lin, int part = 0) {
   TapSeg s{};
   s.x = x;
-  s.w = static_cast<const char*>(h->d_w) + g.w_off;
+  s.w = static_cast<const char*>(g.x3 ? h->d_wx : h->d_w) + (part ? g.w_off2 : g.w_off);
   s.Lin = Lin;
-  s.Cin = g.Cin;
+  s.Cin = g.x3 && !part ? 5 * g.Cin : g.Cin;
+  s.pc = g.x3 ? g.Cin : 0;
   s.ntaps = g.ntaps;
   s.off0 = g.off0;
   s.offstep = g.offstep;
@@ -957,6 +1021,10 @@ TapConv make_op(const gsvdec* h, const GemmConv& g, int B, const void* x, int Li
   TapConv op{};
   op.seg[0] = make_seg(h, g, x, Lin);
   op.nseg = 1;
+  if (g.x3) {  // small products first, the large one last (fewer roundings against the big sum)
+    op.seg[1] = make_seg(h, g, x, Lin, 1);
+    op.nseg = 2;
+  }
   op.B = B;
   op.Q = g.Q(Lin);
   op.N = g.N;
@@ -966,6 +1034,7 @@ TapConv make_op(const gsvdec* h, const GemmConv& g, int B, const void* x, int Li
   op.bias = h->d_bias + g.b_off;
   op.div = 1.0f;
   op.slope = 0.1f;
+  op.split = g.x3 ? 1 : 0;
   return op;
 }
 
@@ -1027,7 +1096,35 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
   grp.partial = h->cur_part;
   grp.partial_cap = h->cur_part_cap;
   cudaError_t e;
-  if (h->dt == Dt::F32) {
+  if (grp.op[0].split) {
+    // Three-piece ops (GSV_MODE_FP32_TC): a single residual enters the GEMM as
+    // a last segment [X2 X1 X0] against [I I I] (after the large products:
+    // three more roundings of the sum); the three-residual branch sums add
+    // theirs in the epilogue in fp32, each read as the sum of its pieces.
+    for (int i = 0; i < grp.n; ++i) {
+      TapConv& op = grp.op[i];
+      if (!op.split) return set_err(GSV_E_UNSUPPORTED, "%s mixes three-piece and plain ops", name.c_str());
+      if (op.nres != 1) continue;
+      auto it = h->xident_off.find(op.Cout);
+      if (it == h->xident_off.end() || op.N != op.Cout || op.crop != 0 || op.Q != op.Lout || op.nseg >= kMaxSeg)
+        return set_err(GSV_E_UNSUPPORTED, "residual of %s cannot be folded into the GEMM", name.c_str());
+      TapSeg& sg = op.seg[op.nseg++];
+      sg = TapSeg{};
+      sg.x = op.res[0];
+      sg.w = static_cast<const char*>(h->d_wx) + it->second;
+      sg.Lin = op.Lout;
+      sg.Cin = 3 * op.Cout;
+      sg.pc = op.Cout;
+      sg.ntaps = 1;
+      sg.off0 = 0;
+      sg.offstep = 1;
+      op.nres = 0;
+    }
+    bool tc = true;
+    for (int i = 0; i < grp.n; ++i) tc = tc && tapconv_tc_supported(grp.op[i]);
+    if (!tc) return set_err(GSV_E_UNSUPPORTED, "layer geometry not supported by the tcgen05 kernel");
+    e = launch_tapconv_tc(grp, st);
+  } else if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
   } else {
     // Residuals of wide layers enter the tensor-core GEMM as identity-weight
@@ -1146,7 +1243,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   }
   auto stage_len = [&](int s) -> const int* { return lens ? lens + (size_t)s * B : nullptr; };
 
-  CUDA_TRY(launch_transpose_in(zsrc, B, h->in_ch, Tsrc, t_off, T0, lens ? lens : nullptr, w.zin, h->dt, st));
+  CUDA_TRY(launch_transpose_in(zsrc, B, h->in_ch, Tsrc, t_off, T0, lens ? lens : nullptr, w.zin, fwd_dt(h), st));
   GSV_TRY(after_launch(h, st, "input_relayout", 1, 0, 0.0, (4.0 + eb) * B * h->in_ch * T0));
   const float* bias_bc = nullptr;
   if (h->has_cond && gdev) {
@@ -1157,7 +1254,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   }
   auto tap_out = [&](int idx, const void* src, int L, int C) -> int {
     if (!taps || !taps[idx]) return GSV_OK;
-    CUDA_TRY(launch_to_ncl(src, h->dt, B, L, C, w.tap, st));
+    CUDA_TRY(launch_to_ncl(src, fwd_dt(h), B, L, C, w.tap, st));
     CUDA_TRY(cudaMemcpyAsync(taps[idx], w.tap, sizeof(float) * (size_t)B * L * C, cudaMemcpyDeviceToHost, st));
     return GSV_OK;
   };
@@ -1165,7 +1262,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   // first upsample (:390-408).
   int L = T0;
   {
-    TapConv op = make_op(h, h->pre, B, w.zin, L);
+    TapConv op = make_op(h, h->x3 ? h->xpre : h->pre, B, w.zin, L);
     op.bias_bc = bias_bc;
     op.len = stage_len(0);
     op.out_act = OUT;
@@ -1178,7 +1275,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
   }
   mark(h, st);
   for (int i = 0; i < nst; ++i) {
-    const Stage& sg = h->stages[i];
+    const Stage& sg = (h->x3 ? h->xstages : h->stages)[i];
     const bool last = i + 1 == nst;
     const float next_slope = last ? 0.01f : 0.1f;
     const int nb = (int)sg.c1.size();
@@ -1295,6 +1392,14 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
         f.res[r] = S == 1 ? X : XR[r];
       }
       f.nseg = nb;
+      if (h->x3) {  // every branch's small-product blocks first, then the large ones
+        for (int r = 0; r < nb; ++r) {
+          const GemmConv& g = sg.c2[r][sg.c2[r].size() - 1];
+          f.seg[r] = make_seg(h, g, TT[r], L, 0);
+          f.seg[nb + r] = make_seg(h, g, TT[r], L, 1);
+        }
+        f.nseg = 2 * nb;
+      }
       f.nres = nb;
       f.bias = h->d_bias + sg.c2[0][sg.c2[0].size() - 1].b_off;  // replaced below when nb > 1
       f.div = (float)nb;
@@ -1313,7 +1418,7 @@ int forward_device(gsvdec* h, const float* zsrc, int Tsrc, int t_off, const floa
     mark(h, st);
   }
   // LeakyReLU(0.01) was applied by the producer; conv_post + tanh (:449-455).
-  CUDA_TRY(launch_post(OUT, h->dt, B, L, h->post_C, h->d_post_w, h->post_wh_ok ? &h->post_wh : nullptr,
+  CUDA_TRY(launch_post(OUT, fwd_dt(h), B, L, h->post_C, h->d_post_w, h->post_wh_ok ? &h->post_wh : nullptr,
                        h->post_K, h->post_pad,
                        h->post_bias, stage_len(nst), wav_dev, taps && taps[1 + 2 * nst] ? w.tap : nullptr, st));
   GSV_TRY(after_launch(h, st, "conv_post", 2, 1, 2.0 * h->post_C * h->post_K * (double)L * B,
@@ -1563,7 +1668,8 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   if (!out) return set_err(GSV_E_INVALID_ARG, "out is NULL");
   *out = nullptr;
   if (!ts || n <= 0) return set_err(GSV_E_INVALID_ARG, "no tensors given");
-  if (mode != GSV_MODE_FP32 && mode != GSV_MODE_BF16) return set_err(GSV_E_INVALID_ARG, "bad mode %d", mode);
+  if (mode != GSV_MODE_FP32 && mode != GSV_MODE_BF16 && mode != GSV_MODE_FP32_TC)
+    return set_err(GSV_E_INVALID_ARG, "bad mode %d", mode);
   // Validate every tensor first (cheap), then convert and fold all weights in
   // parallel, then pack (the packing jobs also run in parallel, in finish()).
   HostModel m;
@@ -1598,7 +1704,8 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   std::unique_ptr<gsvdec, HandleDeleter> h(new gsvdec());
   h->mode = mode;
   h->device = device;
-  h->dt = mode == GSV_MODE_FP32 ? Dt::F32 : Dt::BF16;
+  h->dt = mode == GSV_MODE_BF16 ? Dt::BF16 : Dt::F32;
+  h->x3 = mode == GSV_MODE_FP32_TC;
   h->in_ch = m.pre.d1;
   h->C0 = m.pre.d0;
   h->has_cond = m.has_cond;
@@ -1659,6 +1766,50 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
       for (auto& br : s.c2) for (auto& g : br) all = all && ok(g);
     }
     if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the bf16 tcgen05 kernel");
+  }
+  // GSV_MODE_FP32_TC: the decoder's convs again, as three-piece K lists in a
+  // second arena; biases stay those of the FP32 packing (same offsets).
+  Packer px{Dt::BF16};
+  px.x3 = true;
+  if (h->x3) {
+    h->xpre = px.conv(m.pre);
+    h->xpre.b_off = h->pre.b_off;
+    for (size_t i = 0; i < m.ups.size(); ++i) {
+      const Stage& f = h->stages[i];
+      Stage s;
+      s.up = px.convT(m.ups[i]);
+      s.up.b_off = f.up.b_off;
+      for (size_t r = 3 * i, br = 0; r < std::min(3 * i + 3, m.rbs.size()); ++r, ++br) {
+        std::vector<GemmConv> a, b;
+        for (size_t k = 0; k < m.rbs[r].c1.size(); ++k) {
+          a.push_back(px.conv(m.rbs[r].c1[k]));
+          a.back().b_off = f.c1[br][k].b_off;
+        }
+        for (size_t k = 0; k < m.rbs[r].c2.size(); ++k) {
+          b.push_back(px.conv(m.rbs[r].c2[k]));
+          b.back().b_off = f.c2[br][k].b_off;
+        }
+        s.c1.push_back(std::move(a));
+        s.c2.push_back(std::move(b));
+      }
+      if (!s.c2.empty() && !h->xident_off.count(s.up.Cout)) h->xident_off[s.up.Cout] = px.identity(s.up.Cout);
+      h->xstages.push_back(std::move(s));
+    }
+    auto ok = [&](const GemmConv& g) {
+      TapConv op{};
+      op.nseg = 2; op.seg[0].Cin = 5 * g.Cin; op.seg[0].pc = g.Cin; op.seg[0].ntaps = g.ntaps;
+      op.seg[0].offstep = g.offstep; op.seg[0].off0 = g.off0; op.N = g.N; op.Cout = g.Cout; op.split = 1;
+      op.seg[1] = op.seg[0];
+      op.seg[1].Cin = g.Cin;
+      return tapconv_tc_supported(op);
+    };
+    bool all = ok(h->xpre);
+    for (auto& s : h->xstages) {
+      all = all && ok(s.up);
+      for (auto& br : s.c1) for (auto& g : br) all = all && ok(g);
+      for (auto& br : s.c2) for (auto& g : br) all = all && ok(g);
+    }
+    if (!all) return set_err(GSV_E_UNSUPPORTED, "a layer geometry is not supported by the three-piece tcgen05 path");
   }
   // The flow (optional), packed into the same weight arena.
   std::vector<std::vector<float>> flow_cond_w, flow_cond_b;
@@ -1727,6 +1878,12 @@ int create_impl(const gsvdec_tensor* ts, int n, int mode, int device, gsvdec_t**
   h->w_bytes = pk.size;
   CUDA_TRY(dev_malloc(&h->d_w, std::max<size_t>(h->w_bytes, 256)));
   CUDA_TRY(cudaMemcpy(h->d_w, pk.arena.get(), h->w_bytes, cudaMemcpyHostToDevice));
+  if (h->x3) {
+    px.finish();
+    h->wx_bytes = px.size;
+    CUDA_TRY(dev_malloc(&h->d_wx, std::max<size_t>(h->wx_bytes, 256)));
+    CUDA_TRY(cudaMemcpy(h->d_wx, px.arena.get(), h->wx_bytes, cudaMemcpyHostToDevice));
+  }
   CUDA_TRY(dev_malloc(&h->d_bias, sizeof(float) * std::max<size_t>(pk.biases.size(), 1)));
   CUDA_TRY(cudaMemcpy(h->d_bias, pk.biases.data(), sizeof(float) * pk.biases.size(), cudaMemcpyHostToDevice));
   if (post_w.size() <= sizeof(h->post_wh.w) / sizeof(float)) {
@@ -1777,6 +1934,7 @@ void destroy_impl(gsvdec* h) {
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
   cudaFree(h->d_w);
+  cudaFree(h->d_wx);
   cudaFree(h->d_bias);
   cudaFree(h->d_cond_w);
   cudaFree(h->d_cond_b);
@@ -2428,7 +2586,7 @@ int gsvdec_get_info(const gsvdec_t* h, gsvdec_info* info) {
   }
   halo += (double)h->post_pad / rate;
   info->receptive_halo = (int)std::ceil(halo);
-  info->weight_bytes = (int64_t)h->w_bytes;
+  info->weight_bytes = (int64_t)(h->w_bytes + h->wx_bytes);
   return GSV_OK;
 }
 
@@ -2682,7 +2840,7 @@ int noalloc_scratch(int device, void** out) {
 // Lays the forward's device-mode buffers out inside [base, base + cap).
 int carve_noalloc(const gsvdec* h, int B, int T0, char* base, size_t cap, Workspace& w) {
   const size_t act = max_act_elems(h, T0) * (size_t)B;
-  const size_t eb = act_bytes(h);
+  const size_t eb = fwd_act_bytes(h);
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   size_t off = 0;
   const size_t o_zin = off; off += al((size_t)B * T0 * h->in_ch * eb);

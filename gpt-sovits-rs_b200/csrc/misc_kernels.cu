@@ -37,6 +37,37 @@ __global__ void transpose_in_kernel(const float* __restrict__ z, int Cin, int Ts
   }
 }
 
+// Three bf16 pieces of v at p[0], p[C], p[2C] (their sum is v exactly).
+__device__ __forceinline__ void st_x3(__nv_bfloat16* p, int C, float v) {
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    p[(size_t)k * C] = h;
+    v = v - __bfloat162float(h);
+  }
+}
+
+// The same relayout into three-piece rows [B][T][3 Cin] (GSV_MODE_FP32_TC).
+__global__ void transpose_in_x3_kernel(const float* __restrict__ z, int Cin, int Tsrc, int t_off, int Tn,
+                                       const int* __restrict__ len, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const int lim = len ? len[b] : Tn;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + threadIdx.x;
+    float v = 0.0f;
+    if (c < Cin && t < Tn && t < lim) v = z[((size_t)b * Cin + c) * Tsrc + t_off + t];
+    tile[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + threadIdx.x;
+    if (t < Tn && c < Cin) st_x3(out + ((size_t)b * Tn + t) * 3 * Cin + c, Cin, tile[threadIdx.x][i]);
+  }
+}
+
 // One warp per output channel: bias_bc[b][c] = bc[c] + sum_i wc[c][i] g[b][i].
 __global__ void cond_kernel(const float* __restrict__ g, const float* __restrict__ wc,
                             const float* __restrict__ bc, int B, int gin, int C,
@@ -172,7 +203,9 @@ constexpr int post_per() { return sizeof(T) == 2 ? 4 : 2; }
 // Each row is fetched from HBM once and read from shared memory as 4 K bytes
 // instead of K times 32; the sums run in the same order as a direct
 // per-sample loop (over c within a tap, then over taps, from the bias).
-template <typename T, int K>
+// NP = 3: three-piece rows [L][3][16] bf16 (GSV_MODE_FP32_TC), each value the
+// exact sum of its pieces.
+template <typename T, int K, int NP = 1>
 __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __restrict__ x, int L,
                                                                  const __grid_constant__ PostWeights P,
                                                                  int pad, float bias,
@@ -188,11 +221,25 @@ __global__ void __launch_bounds__(kPostThreads) post_fast_kernel(const T* __rest
   const int b = blockIdx.y;
   const int t_base = blockIdx.x * kPostOut;
   const int r0 = t_base - pad;
-  const uint4* xb = reinterpret_cast<const uint4*>(x + (size_t)b * L * C);
+  const uint4* xb = reinterpret_cast<const uint4*>(x + (size_t)b * L * C * NP);
   for (int i = threadIdx.x; i < kRows; i += kPostThreads) {
     const int row = r0 + i;
     float v[C];
-    if (row >= 0 && row < L) {
+    if (NP == 3 && row >= 0 && row < L) {
+#pragma unroll
+      for (int c = 0; c < C; ++c) v[c] = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 3 * U; ++k) {  // plane k / U, channels 8 (k % U) ..
+        const uint4 u = __ldg(xb + (size_t)row * 3 * U + k);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[8 * (k % U) + 2 * e] += f.x;
+          v[8 * (k % U) + 2 * e + 1] += f.y;
+        }
+      }
+    } else if (row >= 0 && row < L) {
 #pragma unroll
       for (int k = 0; k < U; ++k) {
         const uint4 u = __ldg(xb + (size_t)row * U + k);
@@ -266,6 +313,28 @@ __global__ void to_ncl_kernel(const T* __restrict__ x, int L, int C, float* __re
   }
 }
 
+// Three-piece rows [B][L][3 C] -> [B][C][L] fp32 (each value the sum of its pieces).
+__global__ void to_ncl_x3_kernel(const __nv_bfloat16* __restrict__ x, int L, int C, float* __restrict__ y) {
+  pdl_wait();
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int t = t0 + i, c = c0 + threadIdx.x;
+    float v = 0.0f;
+    if (t < L && c < C) {
+      const __nv_bfloat16* p = x + ((size_t)b * L + t) * 3 * C + c;
+      v = __bfloat162float(p[0]) + __bfloat162float(p[C]) + __bfloat162float(p[2 * C]);
+    }
+    tile[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int c = c0 + i, t = t0 + threadIdx.x;
+    if (c < C && t < L) y[((size_t)b * C + c) * L + t] = tile[threadIdx.x][i];
+  }
+}
+
 // WN gated activation, 8 channels per thread.
 template <typename T>
 __global__ void gate_kernel(const T* __restrict__ xin, const float* __restrict__ cond, int cond_ld,
@@ -303,7 +372,13 @@ __global__ void gate_kernel(const T* __restrict__ xin, const float* __restrict__
 cudaError_t launch_transpose_in(const float* z, int B, int Cin, int Tsrc, int t_off, int T,
                                 const int* len, void* zt, Dt dt, cudaStream_t st) {
   dim3 grid(cdiv(T, 32), cdiv(Cin, 32), B), block(32, 8);
-  if (dt == Dt::F32)
+  if (dt == Dt::X3)
+    {
+      const cudaError_t e_ = launch_k(transpose_in_x3_kernel, grid, block, 0, st, z, Cin, Tsrc, t_off, T, len,
+                                      static_cast<__nv_bfloat16*>(zt));
+      if (e_ != cudaSuccess) return e_;
+    }
+  else if (dt == Dt::F32)
     {
       const cudaError_t e_ = launch_k(transpose_in_kernel<float>, grid, block, 0, st, z, Cin, Tsrc, t_off, T,
                                       len, static_cast<float*>(zt));
@@ -356,6 +431,16 @@ cudaError_t launch_zero_tails(float* wav, const int* len, int B, int T0, int hop
 cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* w, const PostWeights* wh,
                         int K, int pad, float bias, const int* len, float* wav, float* pre, cudaStream_t st) {
   if (K > 64 || C != 16) return cudaErrorInvalidValue;
+  if (dt == Dt::X3) {  // three-piece rows: the kernel-parameter path only
+    if (wh == nullptr || K != 7) return cudaErrorNotSupported;
+    {
+      const cudaError_t e_ = launch_k(post_fast_kernel<__nv_bfloat16, 7, 3>,
+                                      dim3(cdiv(L, kPostThreads * post_per<__nv_bfloat16>()), B), kPostThreads,
+                                      0, st, static_cast<const __nv_bfloat16*>(x), L, *wh, pad, bias, len, wav, pre);
+      if (e_ != cudaSuccess) return e_;
+    }
+    return cudaGetLastError();
+  }
   if (wh != nullptr && K == 7) {
     if (dt == Dt::F32)
       {
@@ -393,7 +478,14 @@ cudaError_t launch_post(const void* x, Dt dt, int B, int L, int C, const float* 
 cudaError_t launch_to_ncl(const void* x, Dt dt, int B, int L, int C, float* y, cudaStream_t st,
                           const int* perm) {
   dim3 grid(cdiv(L, 32), cdiv(C, 32), B), block(32, 8);
-  if (dt == Dt::F32)
+  if (dt == Dt::X3)
+    {
+      if (perm != nullptr) return cudaErrorInvalidValue;
+      const cudaError_t e_ = launch_k(to_ncl_x3_kernel, grid, block, 0, st, static_cast<const __nv_bfloat16*>(x),
+                                      L, C, y);
+      if (e_ != cudaSuccess) return e_;
+    }
+  else if (dt == Dt::F32)
     {
       const cudaError_t e_ = launch_k(to_ncl_kernel<float>, grid, block, 0, st, static_cast<const float*>(x), L,
                                       C, y, perm);

@@ -34,7 +34,9 @@ namespace gsv {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr int kMaxFlat = kMaxSeg;  // segments summed over the ops of one launch
+// Segments summed over the ops of one launch (three three-piece conv2 ops of
+// three segments each: small products, large product, residual).
+constexpr int kMaxFlat = 9;
 
 struct alignas(64) TcParams {
   CUtensorMap mapA[kMaxFlat];  // activation windows, one per flattened segment
@@ -58,11 +60,14 @@ static_assert(sizeof(TcParams) <= 4096, "kernel parameter space");
 // Per-op descriptor copied to shared memory at CTA start, so the roles' inner
 // loops never index the kernel-parameter block dynamically.
 struct SmSeg {
-  int ntaps, off0, offstep, Cin, minoff, wtap0, flat, rows;
+  int ntaps, off0, offstep, Cin, minoff, wtap0;
+  short flat, pc;  // pc: piece width of three-piece operands (0: plain)
+  int rows;
 };
+static_assert(sizeof(SmSeg) == 32, "op table layout");
 struct SmOp {
   int nseg, Q, N, Cout, Lout, crop, cout_shift, bias_off;  // bias_off: into the smem bias table
-  int nres, gate, bias_bc_ld, pad_;
+  int nres, gate, bias_bc_ld, split;
   const __nv_bfloat16* res[4];
   const int* len;
   const float* bias;
@@ -89,6 +94,7 @@ struct EpiArgs {
   bool has_div;
   bool v8;   // both output bases 32-byte aligned: one 256-bit store per 16-column run
   bool v8r;  // every residual base 32-byte aligned: one 256-bit load per run
+  bool split;  // outputs as three bf16 pieces per value ([Lout][3 Cout] rows)
 };
 
 __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, int b) {
@@ -96,8 +102,9 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   a.total = o.Lout * o.Cout;
   a.nres = o.nres;
 #pragma unroll
+  const size_t rst = (size_t)a.total * (o.split ? 3 : 1);  // elements per utterance
   for (int r = 0; r < kMaxRes; ++r)
-    a.res[r] = r < o.nres ? o.res[r] + (size_t)b * a.total : nullptr;
+    a.res[r] = r < o.nres ? o.res[r] + (size_t)b * rst : nullptr;
   a.N = o.N;
   a.crop = o.crop;
   a.Cout = o.Cout;
@@ -105,8 +112,10 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   a.lim = o.len ? o.len[b] : 0x7fffffff;
   a.bias = sbias + o.bias_off;
   a.bias_bc = o.bias_bc ? o.bias_bc + (size_t)b * o.bias_bc_ld : nullptr;
-  a.raw = o.out_raw ? o.out_raw + (size_t)b * a.total : nullptr;
-  a.act = o.out_act ? o.out_act + (size_t)b * a.total : nullptr;
+  a.split = o.split != 0;
+  const size_t ust = (size_t)a.total * (a.split ? 3 : 1);  // output elements per utterance
+  a.raw = o.out_raw ? o.out_raw + (size_t)b * ust : nullptr;
+  a.act = o.out_act ? o.out_act + (size_t)b * ust : nullptr;
   a.slope = o.slope;
   a.has_div = o.div != 1.0f;
   a.inv_div = o.div;
@@ -116,6 +125,36 @@ __device__ __forceinline__ EpiArgs epi_args(const SmOp& o, const float* sbias, i
   for (int r = 0; r < kMaxRes; ++r) ra |= reinterpret_cast<uintptr_t>(a.res[r]);
   a.v8r = (ra & 31) == 0;
   return a;
+}
+
+// 16 fp32 values as their three bf16 pieces at p, p + C, p + 2C: piece 0 the
+// round-to-nearest bf16 of v, piece 1 that of the (exact) remainder v - piece
+// 0, piece 2 that of what is left.  A normal fp32 value has 24 significant
+// bits and each piece takes the next 8, so the three sum back to v exactly.
+__device__ __forceinline__ void store_x3(__nv_bfloat16* p, int C, const float* v, bool v8) {
+  float r[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r[i] = v[i];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const uint4 u0 = pack_bf16x8(r), u1 = pack_bf16x8(r + 8);
+    if (k < 2) {
+      const __nv_bfloat16* h0 = reinterpret_cast<const __nv_bfloat16*>(&u0);
+      const __nv_bfloat16* h1 = reinterpret_cast<const __nv_bfloat16*>(&u1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        r[i] = r[i] - __bfloat162float(h0[i]);
+        r[8 + i] = r[8 + i] - __bfloat162float(h1[i]);
+      }
+    }
+    __nv_bfloat16* q = p + (size_t)k * C;
+    if (v8) {
+      st_global_v8(q, u0, u1);
+    } else {
+      *reinterpret_cast<uint4*>(q) = u0;
+      *reinterpret_cast<uint4*>(q + 8) = u1;
+    }
+  }
 }
 
 // Epilogue of 16 consecutive GEMM columns [n, n + 16) of row q.  Their flat
@@ -153,9 +192,40 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
         v[4 * k + 3] += bv.w;
       }
     }
+    if (a.split) {  // three-piece residuals: each value the exact sum of its pieces
+      const size_t at = (size_t)t * 3 * a.Cout + c;
+#pragma unroll
+      for (int r = 0; r < kMaxRes; ++r) {
+        if (r >= a.nres) break;
+        float x[16];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + at + (size_t)k * a.Cout);
+          uint4 ru[2];
+          if (a.v8r) {
+            ld_global_nc_v8(rp, ru[0], ru[1]);
+          } else {
+            ru[0] = __ldg(rp);
+            ru[1] = __ldg(rp + 1);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&ru[h]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = __bfloat1622float2(h2[i]);
+              x[8 * h + 2 * i] = k == 0 ? f.x : x[8 * h + 2 * i] + f.x;
+              x[8 * h + 2 * i + 1] = k == 0 ? f.y : x[8 * h + 2 * i + 1] + f.y;
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = x[i] + v[i];
+      }
+    }
 #pragma unroll
     for (int r = 0; r < kMaxRes; ++r) {  // residual runs: 16 contiguous bf16
-      if (r >= a.nres) break;
+      if (a.split || r >= a.nres) break;
       const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
       uint4 ru[2];
       if (a.v8r) {
@@ -180,6 +250,17 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
     }
+  }
+  if (a.split) {  // three bf16 pieces per value, planes Cout apart in the row
+    const size_t at = (size_t)t * 3 * a.Cout + c;
+    if (a.raw) store_x3(a.raw + at, a.Cout, v, a.v8);
+    if (a.act) {
+      float w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = lrelu(v[i], a.slope);
+      store_x3(a.act + at, a.Cout, w, a.v8);
+    }
+    return;
   }
   const uint4 u0 = pack_bf16x8(v), u1 = pack_bf16x8(v + 8);
   // e0 is a multiple of 16 elements (32 bytes): with 32-byte aligned bases a
@@ -321,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
     o.out_act = static_cast<__nv_bfloat16*>(g.out_act);
     o.slope = g.slope;
     o.div = g.div;
+    o.split = g.split;
     for (int s = 0; s < g.nseg; ++s) {
       const int f = P.seg_base[threadIdx.x] + s;
       SmSeg& d = o.seg[s];
@@ -330,7 +412,8 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       d.Cin = g.seg[s].Cin;
       d.minoff = P.seg_minoff[f];
       d.wtap0 = P.seg_wtap0[f];
-      d.flat = f;
+      d.pc = (short)g.seg[s].pc;
+      d.flat = (short)f;
       d.rows = kM + (d.ntaps - 1) * abs(d.offstep);
     }
   }
@@ -410,9 +493,18 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
               break;
             }
             mbar_expect_tx(a_full + 8 * st, MT * wbytes);
+            // Three-piece operands: K block c0 / pc of the five-block list reads
+            // plane 2, 1, 0, 1, 0, of the three-block list (a residual against
+            // identities) 2, 1, 0, the one-block list plane 0.
+            int ac0 = c0;
+            if (d.pc) {
+              const int kb = c0 / d.pc, r = c0 - kb * d.pc;
+              const int plane = d.Cin == d.pc ? 0 : (kb == 0 ? 2 : (kb & 1 ? 1 : 0));
+              ac0 = plane * d.pc + r;
+            }
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-              tma_load_3d(smem_u32(sA + st * a_stage + m * a_win), &P.mapA[d.flat], a_full + 8 * st, c0,
+              tma_load_3d(smem_u32(sA + st * a_stage + m * a_win), &P.mapA[d.flat], a_full + 8 * st, ac0,
                           q0 + m * kM + d.minoff, b);
             ++ia;
             if (!RES) {
@@ -662,14 +754,26 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
 
 }  // namespace
 
+// Channel width that sets a segment's chunk: its piece width for three-piece
+// operands, else its input width.
+static int seg_width(const TapSeg& s) { return s.pc ? s.pc : s.Cin; }
+
 bool tapconv_tc_supported(const TapConv& op) {
   if (op.nseg < 1 || op.nseg > kMaxSeg) return false;
-  const int cin = op.seg[0].Cin;
+  const int cin = op.seg[0].Cin, cw = seg_width(op.seg[0]);
   for (int s = 0; s < op.nseg; ++s) {
-    if (op.seg[s].Cin != cin || op.seg[s].ntaps < 1) return false;
-    if ((op.seg[s].ntaps - 1) * abs(op.seg[s].offstep) > 256 - kM) return false;  // TMA box rows
+    const TapSeg& sg = op.seg[s];
+    if (sg.ntaps < 1) return false;
+    if ((sg.ntaps - 1) * abs(sg.offstep) > 256 - kM) return false;  // TMA box rows
+    if (sg.pc) {  // a K list over three pieces: every segment the same piece width
+      if (sg.pc != cw || sg.pc > 4096 || (sg.Cin != sg.pc && sg.Cin != 3 * sg.pc && sg.Cin != 5 * sg.pc))
+        return false;
+    } else if (sg.Cin != cin || op.seg[0].pc) {
+      return false;
+    }
   }
-  const int ck = ck_for(cin), nt = nt_for(op.N);
+  if (op.split && (op.gate || !op.seg[0].pc)) return false;
+  const int ck = ck_for(cw), nt = nt_for(op.N);
   if (!ck || !nt || op.N % nt) return false;
   if (op.Cout % 16) return false;  // 16-element epilogue runs stay 32-byte aligned
   if (op.gate && (op.N != op.Cout || op.N % 32 || op.crop || op.Q != op.Lout || op.nres)) return false;
@@ -685,7 +789,7 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   TcParams P;
   memset(&P, 0, sizeof P);
   P.grp = g;
-  const int ck = ck_for(g.op[0].seg[0].Cin);
+  const int ck = ck_for(seg_width(g.op[0].seg[0]));
   int nt = nt_for(g.op[0].N);
   // A launch that would not fill the SMs (a short utterance, one time chunk
   // of a long one) runs each tile's whole MMA chain on its own: narrower
@@ -703,7 +807,7 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   int nflat = 0, wtiles = 0, max_rows = 0;
   for (int i = 0; i < g.n; ++i) {
     TapConv& op = P.grp.op[i];
-    if (!tapconv_tc_supported(op) || ck_for(op.seg[0].Cin) != ck || op.N % nt ||
+    if (!tapconv_tc_supported(op) || ck_for(seg_width(op.seg[0])) != ck || op.N % nt ||
         op.N != g.op[0].N || op.Q != g.op[0].Q || op.B != g.op[0].B)
       return cudaErrorInvalidValue;
     op.row_tiles = cdiv(op.Q, kM);
@@ -716,7 +820,8 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
       P.seg_minoff[nflat] = sg.offstep >= 0 ? sg.off0 : sg.off0 + (sg.ntaps - 1) * sg.offstep;
       P.seg_wtap0[nflat] = wtiles;
       wtiles += sg.ntaps;
-      if (!encode_act(&P.mapA[nflat], sg.x, op.B, sg.Lin, sg.Cin, ck, rows)) return cudaErrorInvalidValue;
+      if (!encode_act(&P.mapA[nflat], sg.x, op.B, sg.Lin, sg.pc ? 3 * sg.pc : sg.Cin, ck, rows))
+        return cudaErrorInvalidValue;
       if (!encode_w(&P.mapB[nflat], sg.w, sg.ntaps * op.N, sg.Cin, ck, nt)) return cudaErrorInvalidValue;
     }
   }
@@ -759,6 +864,15 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   // Multi-window tiles only where the launch has tiles to spare: they divide
   // the tile count, and a sub-wave launch is bound by one tile's chain.
   const bool spare = P.total_tiles >= 4 * sm_count();
+  // Segments of more than one channel chunk (three-piece K lists) at 16 / 32
+  // channels stream their weights: the resident-weight configurations hold
+  // one chunk per tap.
+  bool multi = false;
+  for (int i = 0; i < g.n; ++i)
+    for (int s = 0; s < g.op[i].nseg; ++s) multi = multi || g.op[i].seg[s].Cin > ck;
+  if (multi && ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, false, 4, 4, 4>(P, st);
+  if (multi && ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, false, 4, 4, 4>(P, st);
+  if (multi && ck < 64) return cudaErrorInvalidValue;
   if (ck == 16 && nt == 16 && P.n_tiles == 1) {
     if (branch_sum || !spare) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
     return launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);

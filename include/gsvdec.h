@@ -49,9 +49,15 @@ extern "C" {
 
 /* Arithmetic modes.  FP32: fp32 CUDA-core convolutions (the reference's own
  * F32 arithmetic, src/config/mod.rs:52-58).  BF16: bf16 operands and
- * activations, fp32 accumulation on tcgen05 tensor cores. */
+ * activations, fp32 accumulation on tcgen05 tensor cores.  FP32_TC: the
+ * decoder forward at fp32 accuracy on tcgen05 tensor cores -- every
+ * activation and weight held as the exact sum of three bf16 pieces, each
+ * product formed from the six piece products that reach 2^-24 of it, fp32
+ * accumulation; the flow, EncP chains and single-layer calls of such a handle
+ * run as in FP32 mode. */
 #define GSV_MODE_FP32 0
 #define GSV_MODE_BF16 1
+#define GSV_MODE_FP32_TC 2
 
 /* Where the z / g / lengths / wav pointers of a forward call live. */
 #define GSV_MEM_HOST 0    /* host memory; the call copies in and out and syncs the stream */

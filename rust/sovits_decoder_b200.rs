@@ -53,6 +53,9 @@ const GSV_DTYPE_F16: c_int = 1;
 const GSV_DTYPE_BF16: c_int = 2;
 const GSV_MODE_FP32: c_int = 0;
 const GSV_MODE_BF16: c_int = 1;
+/// The decoder at fp32 accuracy on the tensor cores (three bf16 pieces per
+/// value); for `DecoderB200::load_mode`.
+pub const GSV_MODE_FP32_TC: c_int = 2;
 const GSV_MEM_HOST: c_int = 0;
 const GSV_MEM_DEVICE: c_int = 1;
 
@@ -124,6 +127,12 @@ impl DecoderB200 {
     /// (F32 / F16 / BF16, src/utils/weights.rs:140-151) handed over by pointer;
     /// the library folds weight norm, packs and uploads them.
     pub fn load(sd: &StateDict, device: &Device, dtype: DType) -> Result<Self> {
+        Self::load_mode(sd, device, mode_of(dtype))
+    }
+
+    /// `load` with an explicit arithmetic mode (GSV_MODE_FP32_TC: F32 results at
+    /// tensor-core speed).
+    pub fn load_mode(sd: &StateDict, device: &Device, mode: c_int) -> Result<Self> {
         let dev = ordinal(device)?;
         let mut names = Vec::new();
         let mut bytes: Vec<Vec<u8>> = Vec::new();
@@ -155,7 +164,7 @@ impl DecoderB200 {
             bytes.push(raw);
         }
         let mut h = std::ptr::null_mut();
-        check(unsafe { gsvdec_create(ts.as_ptr(), ts.len() as c_int, mode_of(dtype), dev, &mut h) })?;
+        check(unsafe { gsvdec_create(ts.as_ptr(), ts.len() as c_int, mode, dev, &mut h) })?;
         Self::wrap(h)
     }
 
