@@ -1123,7 +1123,21 @@ int run_group(gsvdec* h, TapConvGroup& grp, cudaStream_t st, const std::string& 
     bool tc = true;
     for (int i = 0; i < grp.n; ++i) tc = tc && tapconv_tc_supported(grp.op[i]);
     if (!tc) return set_err(GSV_E_UNSUPPORTED, "layer geometry not supported by the tcgen05 kernel");
-    e = launch_tapconv_tc(grp, st);
+    if (grp.op[0].Cout <= 32 && grp.n > 1) {
+      // Narrow three-piece ops keep their weights resident in shared memory
+      // (six K blocks per tap): one launch per op, so one op's weights fit.
+      e = cudaSuccess;
+      for (int i = 0; i < grp.n && e == cudaSuccess; ++i) {
+        TapConvGroup one{};
+        one.op[0] = grp.op[i];
+        one.n = 1;
+        one.err = grp.err;
+        e = launch_tapconv_tc(one, st);
+      }
+      h->launches += grp.n - 1;
+    } else {
+      e = launch_tapconv_tc(grp, st);
+    }
   } else if (h->dt == Dt::F32) {
     e = launch_tapconv_f32(grp, st);
   } else {

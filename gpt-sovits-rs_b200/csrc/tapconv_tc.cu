@@ -292,7 +292,8 @@ struct TcShape {
   // Taps per streamed weight stage: one barrier wait, fence and commit per
   // stage, so narrow tiles (whose 4 MMAs per tap are short) load two taps at
   // a time.
-  static constexpr int kTapsPerB = NT <= 64 ? 2 : 1;
+  // (32 columns and below -- streamed only for three-piece K lists -- four.)
+  static constexpr int kTapsPerB = NT <= 32 ? 4 : (NT <= 64 ? 2 : 1);
   static constexpr int kCols = NBUF * MT * NT;  // NBUF accumulators of MT x NT fp32 columns
   static constexpr uint32_t kTmemCols =
       kCols <= 32 ? 32 : (kCols <= 64 ? 64 : (kCols <= 128 ? 128 : (kCols <= 256 ? 256 : 512)));
@@ -462,12 +463,14 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
       bool ok = true;
       if (RES) {
         mbar_expect_tx(w_full, (uint32_t)P.w_tiles * S::kBBytes);
+        // Tile (chunk c0 / CK, tap j) of a segment at wtap0 + (c0 / CK) * ntaps + j.
         for (int o = 0; o < nops; ++o)
           for (int s = 0; s < ops[o].nseg; ++s) {
             const SmSeg& d = ops[o].seg[s];
-            for (int j = 0; j < d.ntaps; ++j)
-              tma_load_2d(smem_u32(sB + (size_t)(d.wtap0 + j) * S::kBPitch), &P.mapB[d.flat], w_full,
-                          0, j * ops[o].N);
+            for (int c0 = 0; c0 < d.Cin; c0 += CK)
+              for (int j = 0; j < d.ntaps; ++j)
+                tma_load_2d(smem_u32(sB + (size_t)(d.wtap0 + (c0 / CK) * d.ntaps + j) * S::kBPitch),
+                            &P.mapB[d.flat], w_full, c0, j * ops[o].N);
           }
       }
       for (int o = 0; o < nops; ++o)
@@ -591,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
               ad += ad_step;
             };
             if (RES) {
-              uint64_t bd = sdesc<CK>(smem_u32(sB + (size_t)sg.wtap0 * S::kBPitch));
+              uint64_t bd = sdesc<CK>(smem_u32(sB + (size_t)(sg.wtap0 + (c0 / CK) * sg.ntaps) * S::kBPitch));
 #pragma unroll 2
               for (int j = 0; j < sg.ntaps; ++j) {
                 tap_mmas(bd);
@@ -819,7 +822,7 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
       max_rows = std::max(max_rows, rows);
       P.seg_minoff[nflat] = sg.offstep >= 0 ? sg.off0 : sg.off0 + (sg.ntaps - 1) * sg.offstep;
       P.seg_wtap0[nflat] = wtiles;
-      wtiles += sg.ntaps;
+      wtiles += sg.ntaps * (sg.Cin / ck);
       if (!encode_act(&P.mapA[nflat], sg.x, op.B, sg.Lin, sg.pc ? 3 * sg.pc : sg.Cin, ck, rows))
         return cudaErrorInvalidValue;
       if (!encode_w(&P.mapB[nflat], sg.w, sg.ntaps * op.N, sg.Cin, ck, nt)) return cudaErrorInvalidValue;
@@ -870,8 +873,18 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   bool multi = false;
   for (int i = 0; i < g.n; ++i)
     for (int s = 0; s < g.op[i].nseg; ++s) multi = multi || g.op[i].seg[s].Cin > ck;
-  if (multi && ck == 16 && nt == 16 && P.n_tiles == 1) return launch_cfg<16, 16, false, 4, 4, 4>(P, st);
-  if (multi && ck == 32 && nt == 32 && P.n_tiles == 1) return launch_cfg<32, 32, false, 4, 4, 4>(P, st);
+  // They keep every chunk's weights resident where that fits one CTA per SM,
+  // else stream four taps per stage over two-window tiles.
+  if (multi && ck == 16 && nt == 16 && P.n_tiles == 1) {
+    if (spare && cfg_fits<16, 16, true, 3, 1, 4, 4>(P, 1)) return launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);
+    if (cfg_fits<16, 16, true, 4, 1, 4>(P, 1)) return launch_cfg<16, 16, true, 4, 1, 4>(P, st);
+    return launch_cfg<16, 16, false, 2, 4, 4, false, 2>(P, st);
+  }
+  if (multi && ck == 32 && nt == 32 && P.n_tiles == 1) {
+    if (spare && cfg_fits<32, 32, true, 2, 1, 4, 2>(P, 1)) return launch_cfg<32, 32, true, 2, 1, 4, false, 2>(P, st);
+    if (cfg_fits<32, 32, true, 3, 1, 4>(P, 1)) return launch_cfg<32, 32, true, 3, 1, 4>(P, st);
+    return launch_cfg<32, 32, false, 2, 4, 4, false, 2>(P, st);
+  }
   if (multi && ck < 64) return cudaErrorInvalidValue;
   if (ck == 16 && nt == 16 && P.n_tiles == 1) {
     if (branch_sum || !spare) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
