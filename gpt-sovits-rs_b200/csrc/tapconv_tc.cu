@@ -162,6 +162,9 @@ __device__ __forceinline__ void store_x3(__nv_bfloat16* p, int C, const float* v
 // and e0 are multiples of 16, lie in ONE output row t at channels c..c+15:
 // one mask test, 16-byte vector bias reads from shared memory, one 256-bit
 // store per output (two 16-byte ones where a base is not 32-byte aligned).
+// X3: three-piece outputs and residuals (compiled only into the three-piece
+// instantiations, whose register budget that code raises).
+template <bool X3>
 __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const float* acc) {
   const int e0 = q * a.N + n - a.crop;
   if (e0 < 0 || e0 >= a.total) return;  // cropped ConvTranspose rows
@@ -192,7 +195,7 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
         v[4 * k + 3] += bv.w;
       }
     }
-    if (a.split) {  // three-piece residuals: each value the exact sum of its pieces
+    if constexpr (X3) {  // three-piece residuals: each value the exact sum of its pieces
       const size_t at = (size_t)t * 3 * a.Cout + c;
 #pragma unroll
       for (int r = 0; r < kMaxRes; ++r) {
@@ -225,7 +228,7 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
     }
 #pragma unroll
     for (int r = 0; r < kMaxRes; ++r) {  // residual runs: 16 contiguous bf16
-      if (a.split || r >= a.nres) break;
+      if (X3 || r >= a.nres) break;
       const uint4* rp = reinterpret_cast<const uint4*>(a.res[r] + e0);
       uint4 ru[2];
       if (a.v8r) {
@@ -251,7 +254,7 @@ __device__ __forceinline__ void epi16(const EpiArgs& a, int q, int n, const floa
       for (int i = 0; i < 16; ++i) v[i] = v[i] / a.inv_div;
     }
   }
-  if (a.split) {  // three bf16 pieces per value, planes Cout apart in the row
+  if constexpr (X3) {  // three bf16 pieces per value, planes Cout apart in the row
     const size_t at = (size_t)t * 3 * a.Cout + c;
     if (a.raw) store_x3(a.raw + at, a.Cout, v, a.v8);
     if (a.act) {
@@ -350,7 +353,8 @@ __device__ __forceinline__ bool tile_masked(const SmOp& o, int b, int q0) {
 // NBUF: TMEM accumulators in flight between the MMA warp and the epilogue;
 // GATE: the ops are gated-activation ops (kept out of the other
 // instantiations, whose register budget it would raise).
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE, int MT>
+// X3: three-piece operands (K-block plane remap) and outputs.
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE, int MT, bool X3>
 __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_constant__ TcParams P) {
   using S = TcShape<CK, NT, NBUF, MT>;
   static_assert(MT == 1 || ((MT == 2 || MT == 4) && !GATE), "multi-window tiles: plain epilogue only");
@@ -500,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
             // plane 2, 1, 0, 1, 0, of the three-block list (a residual against
             // identities) 2, 1, 0, the one-block list plane 0.
             int ac0 = c0;
-            if (d.pc) {
+            if (X3 && d.pc) {
               const int kb = c0 / d.pc, r = c0 - kb * d.pc;
               const int plane = d.Cin == d.pc ? 0 : (kb == 0 ? 2 : (kb & 1 ? 1 : 0));
               ac0 = plane * d.pc + r;
@@ -691,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1) tapconv_tc_kernel(const __grid_co
 #pragma unroll
             for (int k = 0; k < 16; ++k) v[k] = 0.0f;
           }
-          if (live) epi16(ea, q, n0 + c0, v);
+          if (live) epi16<X3>(ea, q, n0 + c0, v);
         }
       }  // windows of the tile
       tc_fence_before();
@@ -726,12 +730,12 @@ bool cfg_fits(const TcParams& P, int per_sm) {
   return per_sm * (cfg_smem<CK, NT, RES, SA, SB, NBUF, MT>(P) + 1024) <= (size_t)smem_per_sm();
 }
 
-template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE = false, int MT = 1>
+template <int CK, int NT, bool RES, int SA, int SB, int NBUF, bool GATE = false, int MT = 1, bool X3 = false>
 cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
   using S = TcShape<CK, NT, NBUF, MT>;
   const size_t smem = cfg_smem<CK, NT, RES, SA, SB, NBUF, MT>(P);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, GATE, MT>;
+  auto kern = tapconv_tc_kernel<CK, NT, RES, SA, SB, NBUF, GATE, MT, X3>;
   // CTAs per SM, bounded by shared memory (1 KB reserved per CTA), registers,
   // threads and TMEM (each CTA holds kTmemCols of the SM's 512 columns).
   int nregs = 0;
@@ -756,6 +760,34 @@ cudaError_t launch_cfg(TcParams& P, cudaStream_t st) {
 }
 
 }  // namespace
+
+// Configurations of the three-piece ops (GSV_MODE_FP32_TC), instantiated
+// apart from the bf16 ones so that the bf16 kernels keep their register budget.
+// Narrow layers (whose K lists span several channel chunks) keep every chunk's
+// weights resident where that fits one CTA per SM, else stream four taps per
+// stage over two-window tiles; wider ones take the bf16 choices.
+static cudaError_t launch_x3(TcParams& P, int ck, int nt, bool spare, bool branch_sum, cudaStream_t st) {
+  if (ck == 16 && nt == 16 && P.n_tiles == 1) {
+    if (spare && cfg_fits<16, 16, true, 3, 1, 4, 4>(P, 1)) return launch_cfg<16, 16, true, 3, 1, 4, false, 4, true>(P, st);
+    if (cfg_fits<16, 16, true, 4, 1, 4>(P, 1)) return launch_cfg<16, 16, true, 4, 1, 4, false, 1, true>(P, st);
+    return launch_cfg<16, 16, false, 2, 4, 4, false, 2, true>(P, st);
+  }
+  if (ck == 32 && nt == 32 && P.n_tiles == 1) {
+    if (spare && cfg_fits<32, 32, true, 2, 1, 4, 2>(P, 1)) return launch_cfg<32, 32, true, 2, 1, 4, false, 2, true>(P, st);
+    if (cfg_fits<32, 32, true, 3, 1, 4>(P, 1)) return launch_cfg<32, 32, true, 3, 1, 4, false, 1, true>(P, st);
+    return launch_cfg<32, 32, false, 2, 4, 4, false, 2, true>(P, st);
+  }
+  if (ck == 64 && nt == 256) return launch_cfg<64, 256, false, 3, 4, 2, false, 1, true>(P, st);
+  if (ck == 64 && nt == 128) return launch_cfg<64, 128, false, 2, 3, 2, false, 1, true>(P, st);
+  if (ck == 64 && nt == 64) {
+    if (branch_sum) return spare ? launch_cfg<64, 64, false, 2, 2, 2, false, 2, true>(P, st)
+                                 : launch_cfg<64, 64, false, 3, 2, 4, false, 1, true>(P, st);
+    if (spare && cfg_fits<64, 64, false, 2, 2, 2, 2>(P, 2)) return launch_cfg<64, 64, false, 2, 2, 2, false, 2, true>(P, st);
+    return cfg_fits<64, 64, false, 2, 4, 4>(P, 2) ? launch_cfg<64, 64, false, 2, 4, 4, false, 1, true>(P, st)
+                                                 : launch_cfg<64, 64, false, 3, 2, 4, false, 1, true>(P, st);
+  }
+  return cudaErrorInvalidValue;
+}
 
 // Channel width that sets a segment's chunk: its piece width for three-piece
 // operands, else its input width.
@@ -867,24 +899,18 @@ cudaError_t launch_tapconv_tc(const TapConvGroup& g, cudaStream_t st) {
   // Multi-window tiles only where the launch has tiles to spare: they divide
   // the tile count, and a sub-wave launch is bound by one tile's chain.
   const bool spare = P.total_tiles >= 4 * sm_count();
-  // Segments of more than one channel chunk (three-piece K lists) at 16 / 32
-  // channels stream their weights: the resident-weight configurations hold
-  // one chunk per tap.
-  bool multi = false;
-  for (int i = 0; i < g.n; ++i)
+  bool x3 = false, multi = false, sum3 = false;
+  for (int i = 0; i < g.n; ++i) {
+    x3 = x3 || g.op[i].split;
+    sum3 = sum3 || g.op[i].nres >= 2;
     for (int s = 0; s < g.op[i].nseg; ++s) multi = multi || g.op[i].seg[s].Cin > ck;
-  // They keep every chunk's weights resident where that fits one CTA per SM,
-  // else stream four taps per stage over two-window tiles.
-  if (multi && ck == 16 && nt == 16 && P.n_tiles == 1) {
-    if (spare && cfg_fits<16, 16, true, 3, 1, 4, 4>(P, 1)) return launch_cfg<16, 16, true, 3, 1, 4, false, 4>(P, st);
-    if (cfg_fits<16, 16, true, 4, 1, 4>(P, 1)) return launch_cfg<16, 16, true, 4, 1, 4>(P, st);
-    return launch_cfg<16, 16, false, 2, 4, 4, false, 2>(P, st);
   }
-  if (multi && ck == 32 && nt == 32 && P.n_tiles == 1) {
-    if (spare && cfg_fits<32, 32, true, 2, 1, 4, 2>(P, 1)) return launch_cfg<32, 32, true, 2, 1, 4, false, 2>(P, st);
-    if (cfg_fits<32, 32, true, 3, 1, 4>(P, 1)) return launch_cfg<32, 32, true, 3, 1, 4>(P, st);
-    return launch_cfg<32, 32, false, 2, 4, 4, false, 2>(P, st);
+  if (x3) {
+    for (int i = 0; i < g.n; ++i)
+      if (!g.op[i].split) return cudaErrorInvalidValue;  // a group is all three-piece or none
+    return launch_x3(P, ck, nt, spare, sum3, st);
   }
+  // The resident-weight configurations below hold one channel chunk per tap.
   if (multi && ck < 64) return cudaErrorInvalidValue;
   if (ck == 16 && nt == 16 && P.n_tiles == 1) {
     if (branch_sum || !spare) return launch_cfg<16, 16, true, 6, 1, 4>(P, st);
