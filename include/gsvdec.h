@@ -299,7 +299,7 @@ int gsvdec_get_launch_stats(gsvdec_t* h, gsvdec_launch_stat* out, int max, int* 
  * static device array of gsvdec_noalloc_scratch_bytes() bytes (32 MiB) that
  * every GPU loading this library holds until process exit; this call never
  * calls cudaMalloc / cudaFree.  Requests whose buffers do not fit (about
- * 130 frames of B*T0 in BF16 mode, 65 in FP32 mode) are rejected with
+ * 130 frames of B*T0 in BF16 mode, 65 in FP32 mode, 45 in FP32_TC mode) are rejected with
  * GSV_E_INVALID_ARG and a message giving the bytes needed.
  * The first call on a device looks up the array's device address (once per
  * device, with that device made current); make that first call before any
