@@ -67,6 +67,9 @@ def test_bad_dtype_and_mode(gsv):
     h = ctypes.c_void_p()
     assert lib.gsvdec_create(t, 1, 0, 0, ctypes.byref(h)) == -4
     assert lib.gsvdec_create(t, 1, 7, 0, ctypes.byref(h)) == -1
+    assert lib.gsvdec_create(t, 1, 3, 0, ctypes.byref(h)) == -1  # modes are FP32 0, BF16 1, FP32_TC 2
+    assert "mode" in lib.gsvdec_last_error().decode()
+    assert lib.gsvdec_create(t, 1, 2, 0, ctypes.byref(h)) == -4  # FP32_TC accepted: the bad dtype is next
     assert lib.gsvdec_create(None, 0, 0, 0, ctypes.byref(h)) == -1
     assert lib.gsvdec_forward(None, None, None, None, 1, 1, None, 0, None) == -1
     assert "NULL" in lib.gsvdec_last_error().decode()
