@@ -257,7 +257,8 @@ def roofline_by_bound(stats, mode, pk):
     against the compute peak vs algorithmic bytes against HBM): compute-bound
     launches report achieved TF/s against the compute peak, HBM-bound ones
     achieved GB/s against the HBM peak."""
-    p_comp = (pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) if mode == "bf16" else FP32_CORE_TFLOPS) * 1e12
+    p_tensor = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
+    p_comp = {"bf16": p_tensor, "fp32tc": p_tensor / 6}.get(mode, FP32_CORE_TFLOPS) * 1e12
     bw = pk["hbm_gbs"] * 1e9
     acc = {"compute": [0, 0.0, 0.0, 0.0], "hbm": [0, 0.0, 0.0, 0.0]}  # launches, flops, bytes, seconds
     for s in stats:
@@ -1051,6 +1052,9 @@ def main():
     if args.mode == "bf16":
         peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
         bound = "tensor"
+    elif args.mode == "fp32tc":  # six bf16 tensor-core products per fp32 product
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 6
+        bound = "tensor (three-piece fp32)"
     else:
         peak = FP32_CORE_TFLOPS
         bound = "fp32-core"
@@ -1080,8 +1084,9 @@ def main():
                 "kernel": "tapconv_tc_kernel<64, 128, ...>, every launch of it (" + str(len(dom_names)) +
                           " per forward: " + ", ".join(dom_names) + ")",
                 "launches_per_step": len(dom),
-                "peak_source": f"{pk_kind} " + ("bf16_tflops_sustained" if args.mode == "bf16"
-                                                 else "nominal fp32 CUDA-core"),
+                "peak_source": f"{pk_kind} " + {"bf16": "bf16_tflops_sustained",
+                                                "fp32tc": "bf16_tflops_sustained / 6"}.get(args.mode,
+                                                                                           "nominal fp32 CUDA-core"),
                 "all_tap_gemm": {"achieved": achieved_all, "frac": achieved_all / peak if achieved_all else None,
                                  "note": "every tap-GEMM launch (tapconv_tc + fused rbstep_tc), HBM-bound ones "
                                          "included, against the tensor peak"}}
